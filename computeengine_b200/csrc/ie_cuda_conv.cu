@@ -1,0 +1,603 @@
+// C ABI of the sm_100a Conv2D forward backend (declared in
+// include/ie_cuda_conv.h).  One translation unit: the kernels are included
+// here so the device-side error word is a single object.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "conv_igemm.cuh"
+#include "direct_kernels.cuh"
+#include "host_util.h"
+#include "layout_kernels.cuh"
+#include "ptx.cuh"
+
+using namespace ie_cuda;
+
+namespace {
+
+constexpr int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+constexpr int64_t ceil_div(int64_t v, int64_t m) { return (v + m - 1) / m; }
+
+// ------------------------------------------------------------- geometry
+
+// conv2d_op.cpp:77-165 and attrs_util.h:185-197.
+int resolve(const ie_conv2d_desc* d, int64_t bias_len, ie_conv2d_shape* out) {
+  if (d == nullptr || out == nullptr) return fail(IE_INVALID_ARGUMENT, "null descriptor");
+  if (d->n <= 0 || d->c <= 0 || d->h <= 0 || d->w <= 0 || d->m <= 0 || d->kh <= 0 ||
+      d->kw <= 0) {
+    return fail(IE_INVALID_ARGUMENT, "Conv2D expects positive dimensions");
+  }
+  if (d->stride_h <= 0 || d->stride_w <= 0 || d->dil_h <= 0 || d->dil_w <= 0) {
+    return fail(IE_INVALID_ARGUMENT, "strides and dilations must be positive");
+  }
+  if (d->group <= 0 || d->c % d->group != 0 || d->m % d->group != 0) {
+    return fail(IE_INVALID_ARGUMENT, "Conv2D group must divide input and output channels");
+  }
+  if (d->depthwise && d->group != d->c) {
+    return fail(IE_INVALID_ARGUMENT, "DepthwiseConv2D requires group == input channels");
+  }
+  if (bias_len >= 0 && bias_len != d->m) {
+    return fail(IE_INVALID_ARGUMENT, "Conv2D bias must have shape [M]");
+  }
+  int64_t pt = d->pad_top, pl = d->pad_left, pb = d->pad_bottom, pr = d->pad_right;
+  if (pt < 0 || pl < 0 || pb < 0 || pr < 0) {
+    return fail(IE_INVALID_ARGUMENT, "pads must be non-negative");
+  }
+  auto same = [](int64_t in, int64_t k, int64_t dil, int64_t s, bool lower, int64_t* b,
+                 int64_t* a) {
+    const int64_t o = (in + s - 1) / s;
+    const int64_t total = std::max<int64_t>(0, (o - 1) * s + dil * (k - 1) + 1 - in);
+    int64_t before = total / 2, after = total - before;
+    if (lower) std::swap(before, after);
+    *b = before;
+    *a = after;
+  };
+  if (d->auto_pad == IE_PAD_VALID) {
+    pt = pl = pb = pr = 0;
+  } else if (d->auto_pad == IE_PAD_SAME_UPPER || d->auto_pad == IE_PAD_SAME_LOWER) {
+    const bool lower = d->auto_pad == IE_PAD_SAME_LOWER;
+    same(d->h, d->kh, d->dil_h, d->stride_h, lower, &pt, &pb);
+    same(d->w, d->kw, d->dil_w, d->stride_w, lower, &pl, &pr);
+  } else if (d->auto_pad != IE_PAD_NOTSET) {
+    return fail(IE_INVALID_ARGUMENT, "unsupported auto_pad");
+  }
+  const int64_t eh = d->dil_h * (d->kh - 1) + 1, ew = d->dil_w * (d->kw - 1) + 1;
+  if (d->h + pt + pb < eh || d->w + pl + pr < ew) {
+    return fail(IE_INVALID_ARGUMENT, "Conv2D kernel exceeds padded input");
+  }
+  const int64_t oh = (d->h + pt + pb - eh) / d->stride_h + 1;
+  const int64_t ow = (d->w + pl + pr - ew) / d->stride_w + 1;
+  if (oh <= 0 || ow <= 0) return fail(IE_INVALID_ARGUMENT, "Conv2D produces an empty output");
+  out->pad_top = pt;
+  out->pad_left = pl;
+  out->pad_bottom = pb;
+  out->pad_right = pr;
+  out->out_h = oh;
+  out->out_w = ow;
+  return IE_OK;
+}
+
+// --------------------------------------------------------- tile choices
+
+// Channel block (bytes of K per tap per stage) that pads the channel count
+// least; ties go to the wider block.
+int choose_bk_bytes(int64_t c_store, int elem_bytes, bool must_divide) {
+  int best = 0;
+  int64_t best_cost = INT64_MAX;
+  for (int bk : {128, 64, 32}) {
+    const int64_t elems = bk / elem_bytes;
+    if (must_divide && c_store % elems != 0) continue;
+    const int64_t cost = round_up(c_store, elems);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bk;
+    }
+  }
+  return best;
+}
+
+int choose_bn(int64_t m) {
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : {256, 128, 64}) {
+    const int64_t cost = round_up(m, bn);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+// ----------------------------------------------------- igemm launching
+
+template <int BN, int BKB, bool I8, bool AS>
+int launch_igemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const IgemmArgs& args,
+                   cudaStream_t st) {
+  constexpr int kParts = I8 ? 1 : 2;
+  constexpr int kStage = kParts * (128 + BN) * BKB;
+  constexpr int kStagesRaw = (192 * 1024) / kStage;
+  constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static_assert(kStages >= 2, "pipeline depth");
+  constexpr int kEpi = BN >= 256 ? 8 : 4;
+  constexpr int kSmem = kStages * kStage + 1024 + 256;
+  auto kern = conv_igemm_kernel<BN, BKB, kStages, kEpi, I8, AS>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  });
+  if (attr_err != cudaSuccess) {
+    return fail(IE_RUNTIME, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  }
+  const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
+  kern<<<grid, 64 + kEpi * 32, kSmem, st>>>(ta, tb, args);
+  return check_launch("conv_igemm_kernel");
+}
+
+using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const IgemmArgs&, cudaStream_t);
+
+template <bool I8, bool AS>
+LaunchFn pick_launch(int bn, int bkb) {
+#define IE_CASE(BN_, BK_) \
+  if (bn == BN_ && bkb == BK_) return launch_igemm_t<BN_, BK_, I8, AS>;
+  IE_CASE(64, 32) IE_CASE(64, 64) IE_CASE(64, 128)
+  IE_CASE(128, 32) IE_CASE(128, 64) IE_CASE(128, 128)
+  IE_CASE(256, 32) IE_CASE(256, 64) IE_CASE(256, 128)
+#undef IE_CASE
+  return nullptr;
+}
+
+struct IgemmSetup {
+  IgemmArgs args;
+  CUtensorMap ta, tb;
+  int bn, bkb;
+};
+
+// Shared set-up of the implicit GEMM for both element kinds.
+//   elem_bytes: 1 (int8) or 2 (bf16; activation and weights hold hi|lo planes)
+int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
+                int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out) {
+  const bool i8 = elem_bytes == 1;
+  const int bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8);
+  if (bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
+                            static_cast<long long>(x_c_store));
+  const int64_t bk_elems = bkb / elem_bytes;
+  const int bn = choose_bn(d->m);
+  const int64_t cblocks = ceil_div(x_c_store, bk_elems);
+  const int64_t taps = d->kh * d->kw;
+  const int64_t ck = cblocks * bk_elems;
+  const int64_t m_total = d->n * s.out_h * s.out_w;
+  if (m_total > (int64_t{1} << 40) || d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "tensor too large");
+  }
+  // TMA im2col corner limits for 4D tensors: [-128, 127]; offsets < 256.
+  const int64_t lower_w = -s.pad_left, lower_h = -s.pad_top;
+  const int64_t upper_w = s.pad_right - (d->kw - 1) * d->dil_w;
+  const int64_t upper_h = s.pad_bottom - (d->kh - 1) * d->dil_h;
+  for (int64_t v : {lower_w, lower_h, upper_w, upper_h}) {
+    if (v < -128 || v > 127) return fail(IE_UNSUPPORTED, "padding / kernel extent too large for TMA im2col");
+  }
+  if ((d->kw - 1) * d->dil_w > 255 || (d->kh - 1) * d->dil_h > 255 || d->stride_h > 8 ||
+      d->stride_w > 8) {
+    return fail(IE_UNSUPPORTED, "kernel extent or stride too large for TMA im2col");
+  }
+  const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int64_t a_chan = i8 ? x_c_store : 2 * x_c_store;
+  int rc = encode_im2col(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
+                         static_cast<int>(bk_elems), static_cast<int>(lower_w),
+                         static_cast<int>(lower_h), static_cast<int>(upper_w),
+                         static_cast<int>(upper_h), static_cast<int>(d->stride_w),
+                         static_cast<int>(d->stride_h));
+  if (rc != IE_OK) return rc;
+  const int64_t b_cols = taps * ck * (i8 ? 1 : 2);
+  rc = encode_2d(&out->tb, packed, dt, elem_bytes, d->m, b_cols, static_cast<int>(bk_elems), bn);
+  if (rc != IE_OK) return rc;
+
+  IgemmArgs& a = out->args;
+  std::memset(&a, 0, sizeof(a));
+  a.n = static_cast<int32_t>(d->n);
+  a.h = static_cast<int32_t>(d->h);
+  a.w = static_cast<int32_t>(d->w);
+  a.c = static_cast<int32_t>(x_c_store);
+  a.out_h = static_cast<int32_t>(s.out_h);
+  a.out_w = static_cast<int32_t>(s.out_w);
+  a.m = static_cast<int32_t>(d->m);
+  a.kh = static_cast<int32_t>(d->kh);
+  a.kw = static_cast<int32_t>(d->kw);
+  a.stride_h = static_cast<int32_t>(d->stride_h);
+  a.stride_w = static_cast<int32_t>(d->stride_w);
+  a.dil_h = static_cast<int32_t>(d->dil_h);
+  a.dil_w = static_cast<int32_t>(d->dil_w);
+  a.pad_t = static_cast<int32_t>(s.pad_top);
+  a.pad_l = static_cast<int32_t>(s.pad_left);
+  a.cblocks = static_cast<int32_t>(cblocks);
+  a.num_k = static_cast<int32_t>(taps * cblocks);
+  a.k_per_tap = static_cast<int32_t>(ck);
+  a.m_total = m_total;
+  a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128));
+  a.n_tiles = static_cast<int32_t>(ceil_div(d->m, bn));
+  out->bn = bn;
+  out->bkb = bkb;
+  return IE_OK;
+}
+
+// Packed-weight geometry for a dense convolution on x_c_store input channels.
+void packed_geom(const ie_conv2d_desc* d, int elem_bytes, int64_t* taps, int64_t* ck) {
+  const int64_t c_store = round_up(d->c, 16);
+  const int bkb = choose_bk_bytes(c_store, elem_bytes, elem_bytes != 1);
+  const int64_t bk_elems = bkb / elem_bytes;
+  *taps = d->kh * d->kw;
+  *ck = ceil_div(c_store, bk_elems) * bk_elems;
+}
+
+int check_dense(const ie_conv2d_desc* d) {
+  if (d->group != 1) return fail(IE_UNSUPPORTED, "the tensor-core path runs group == 1 only");
+  return IE_OK;
+}
+
+int check_ptr(const void* p, const char* what, size_t align) {
+  if (p == nullptr) return fail(IE_INVALID_ARGUMENT, "%s is null", what);
+  if (reinterpret_cast<uintptr_t>(p) % align != 0) {
+    return fail(IE_INVALID_ARGUMENT, "%s must be %zu-byte aligned", what, align);
+  }
+  return IE_OK;
+}
+
+int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const void* packed,
+           const int32_t* bias, const float* mult, void* y, int out_mode, void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(d, -1, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_dense(d)) != IE_OK) return rc;
+  if (q == nullptr) return fail(IE_INVALID_ARGUMENT, "null quantization parameters");
+  if (q->zp_x != 0) {
+    return fail(IE_UNSUPPORTED,
+                "the NHWC kernels take zero-point-0 activations; pack uint8/zp128 input with "
+                "ie_cuda_q8_pack_input(xor_mask=0x80)");
+  }
+  const int32_t lo_lim = q->y_signed ? -128 : 0, hi_lim = q->y_signed ? 127 : 255;
+  if (q->qmin < lo_lim || q->qmax > hi_lim || q->qmin > q->qmax || q->zp_y < lo_lim ||
+      q->zp_y > hi_lim) {
+    return fail(IE_INVALID_ARGUMENT, "output clamp range outside the storage type");
+  }
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(packed, "packed weights", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  if (out_mode != kOutS32 && mult == nullptr) return fail(IE_INVALID_ARGUMENT, "mult is null");
+  const int64_t c_store = round_up(d->c, 16);
+  IgemmSetup su;
+  if ((rc = setup_igemm(d, s, 1, c_store, x, packed, &su)) != IE_OK) return rc;
+  IgemmArgs& a = su.args;
+  a.bias_i32 = bias;
+  a.mult = mult;
+  a.zp_y = q->zp_y;
+  a.lo = q->qmin - q->zp_y;
+  a.hi = q->qmax - q->zp_y;
+  a.out_mode = out_mode == kOutS32 ? kOutS32 : (q->y_signed ? kOutS8 : kOutU8);
+  a.y = y;
+  a.y_ld = round_up(d->m, 16);
+  LaunchFn fn = q->x_signed ? pick_launch<true, true>(su.bn, su.bkb)
+                            : pick_launch<true, false>(su.bn, su.bkb);
+  if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
+  return fn(su.ta, su.tb, a, as_stream(stream));
+}
+
+int grid_1d(int64_t total, int block) {
+  return static_cast<int>(std::min<int64_t>(ceil_div(total, block), int64_t{1} << 30));
+}
+
+}  // namespace
+
+// ===================================================================== ABI
+
+extern "C" {
+
+int ie_conv2d_resolve(const ie_conv2d_desc* desc, int64_t bias_len, ie_conv2d_shape* out) {
+  return resolve(desc, bias_len, out);
+}
+
+const char* ie_cuda_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t ie_cuda_launch_count(int reset) {
+  const uint64_t v = g_launches;
+  if (reset) g_launches = 0;
+  return v;
+}
+
+int ie_cuda_take_device_error(uint32_t* code) {
+  unsigned int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(IE_RUNTIME, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e != cudaSuccess) return fail(IE_RUNTIME, "read error word: %s", cudaGetErrorString(e));
+  const unsigned int zero = 0;
+  e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return fail(IE_RUNTIME, "clear error word: %s", cudaGetErrorString(e));
+  if (code != nullptr) *code = v;
+  return IE_OK;
+}
+
+// -------------------------------------------------------------- int8
+
+size_t ie_cuda_q8_packed_weight_bytes(const ie_conv2d_desc* desc) {
+  if (desc == nullptr) return 0;
+  int64_t taps, ck;
+  packed_geom(desc, 1, &taps, &ck);
+  return static_cast<size_t>(desc->m * taps * ck);
+}
+
+int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
+                            void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_dense(desc)) != IE_OK) return rc;
+  if (w == nullptr || packed == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  int64_t taps, ck;
+  packed_geom(desc, 1, &taps, &ck);
+  const int64_t total = desc->m * taps * ck;
+  pack_weights_q8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      w, static_cast<int8_t*>(packed), static_cast<int32_t>(desc->m),
+      static_cast<int32_t>(desc->c), static_cast<int32_t>(taps), static_cast<int32_t>(ck));
+  return check_launch("pack_weights_q8");
+}
+
+int ie_cuda_q8_pack_input(const void* x_nchw, void* x_nhwc, int64_t n, int64_t c, int64_t h,
+                          int64_t w, int64_t c_store, int32_t xor_mask, void* stream) {
+  if (x_nchw == nullptr || x_nhwc == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || c_store < c) {
+    return fail(IE_INVALID_ARGUMENT, "bad activation shape");
+  }
+  const int64_t hw = h * w;
+  dim3 grid(static_cast<unsigned>(ceil_div(hw, 32)), static_cast<unsigned>(ceil_div(c_store, 32)),
+            static_cast<unsigned>(n));
+  if (grid.z > 65535 || grid.y > 65535) return fail(IE_UNSUPPORTED, "batch or channels too large");
+  pack_nchw_to_nhwc_u8<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x_nchw), static_cast<uint8_t*>(x_nhwc),
+      static_cast<int32_t>(c), hw, static_cast<int32_t>(c_store),
+      static_cast<uint8_t>(xor_mask & 0xFF));
+  return check_launch("pack_nchw_to_nhwc_u8");
+}
+
+int ie_cuda_q8_unpack_output(const void* y_nhwc, void* y_nchw, int64_t n, int64_t c,
+                             int64_t h, int64_t w, int64_t c_store, void* stream) {
+  if (y_nhwc == nullptr || y_nchw == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || c_store < c) {
+    return fail(IE_INVALID_ARGUMENT, "bad activation shape");
+  }
+  const int64_t hw = h * w;
+  dim3 grid(static_cast<unsigned>(ceil_div(hw, 32)), static_cast<unsigned>(ceil_div(c, 32)),
+            static_cast<unsigned>(n));
+  if (grid.z > 65535 || grid.y > 65535) return fail(IE_UNSUPPORTED, "batch or channels too large");
+  unpack_nhwc_to_nchw_u8<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(y_nhwc), static_cast<uint8_t*>(y_nchw),
+      static_cast<int32_t>(c), hw, static_cast<int32_t>(c_store));
+  return check_launch("unpack_nhwc_to_nchw_u8");
+}
+
+int ie_cuda_conv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                      const void* packed, const int32_t* bias, const float* mult, void* y,
+                      void* stream) {
+  return run_q8(desc, q, x, packed, bias, mult, y, kOutU8, stream);
+}
+
+int ie_cuda_conv2d_q8_acc(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                          const void* packed, const int32_t* bias, int32_t* y, void* stream) {
+  return run_q8(desc, q, x, packed, bias, nullptr, y, kOutS32, stream);
+}
+
+size_t ie_cuda_dw_q8_packed_weight_bytes(const ie_conv2d_desc* desc) {
+  if (desc == nullptr) return 0;
+  return static_cast<size_t>(desc->kh * desc->kw * round_up(desc->c, 16));
+}
+
+int ie_cuda_dw_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
+                               void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if (desc->group != desc->c || desc->m != desc->c) {
+    return fail(IE_UNSUPPORTED, "depthwise path needs group == c == m");
+  }
+  if (w == nullptr || packed == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  const int64_t taps = desc->kh * desc->kw, cs = round_up(desc->c, 16);
+  pack_dw_weights_q8<<<grid_1d(taps * cs, 256), 256, 0, as_stream(stream)>>>(
+      w, static_cast<int8_t*>(packed), static_cast<int32_t>(desc->c),
+      static_cast<int32_t>(taps), static_cast<int32_t>(cs));
+  return check_launch("pack_dw_weights_q8");
+}
+
+int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                        const void* packed, const int32_t* bias, const float* mult, void* y,
+                        void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if (desc->group != desc->c || desc->m != desc->c) {
+    return fail(IE_UNSUPPORTED, "depthwise path needs group == c == m");
+  }
+  if (q == nullptr || mult == nullptr) return fail(IE_INVALID_ARGUMENT, "null parameters");
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(packed, "packed weights", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  const int32_t lo_lim = q->y_signed ? -128 : 0, hi_lim = q->y_signed ? 127 : 255;
+  if (q->qmin < lo_lim || q->qmax > hi_lim || q->qmin > q->qmax) {
+    return fail(IE_INVALID_ARGUMENT, "output clamp range outside the storage type");
+  }
+  DwArgs a;
+  a.n = static_cast<int32_t>(desc->n);
+  a.h = static_cast<int32_t>(desc->h);
+  a.w = static_cast<int32_t>(desc->w);
+  a.c_store = static_cast<int32_t>(round_up(desc->c, 16));
+  a.out_h = static_cast<int32_t>(s.out_h);
+  a.out_w = static_cast<int32_t>(s.out_w);
+  a.kh = static_cast<int32_t>(desc->kh);
+  a.kw = static_cast<int32_t>(desc->kw);
+  a.stride_h = static_cast<int32_t>(desc->stride_h);
+  a.stride_w = static_cast<int32_t>(desc->stride_w);
+  a.dil_h = static_cast<int32_t>(desc->dil_h);
+  a.dil_w = static_cast<int32_t>(desc->dil_w);
+  a.pad_t = static_cast<int32_t>(s.pad_top);
+  a.pad_l = static_cast<int32_t>(s.pad_left);
+  a.c = static_cast<int32_t>(desc->c);
+  a.x_signed = q->x_signed;
+  a.zp_x = q->zp_x;
+  a.zp_y = q->zp_y;
+  a.lo = static_cast<float>(q->qmin - q->zp_y);
+  a.hi = static_cast<float>(q->qmax - q->zp_y);
+  const int64_t total = desc->n * s.out_h * s.out_w * (a.c_store / 16);
+  dwconv_q8_nhwc<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x), static_cast<const int8_t*>(packed), bias, mult,
+      static_cast<uint8_t*>(y), a);
+  return check_launch("dwconv_q8_nhwc");
+}
+
+// -------------------------------------------------------------- fp32
+
+size_t ie_cuda_f32_packed_weight_bytes(const ie_conv2d_desc* desc) {
+  if (desc == nullptr) return 0;
+  int64_t taps, ck;
+  packed_geom(desc, 2, &taps, &ck);
+  return static_cast<size_t>(desc->m * taps * 2 * ck * 2);
+}
+
+int ie_cuda_f32_pack_weights(const ie_conv2d_desc* desc, const float* w, void* packed,
+                             void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_dense(desc)) != IE_OK) return rc;
+  if (w == nullptr || packed == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  int64_t taps, ck;
+  packed_geom(desc, 2, &taps, &ck);
+  const int64_t total = desc->m * taps * ck;
+  pack_weights_bf16x2<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      w, static_cast<__nv_bfloat16*>(packed), static_cast<int32_t>(desc->m),
+      static_cast<int32_t>(desc->c), static_cast<int32_t>(taps), static_cast<int32_t>(ck));
+  return check_launch("pack_weights_bf16x2");
+}
+
+int ie_cuda_f32_pack_input(const float* x_nchw, void* x_split, int64_t n, int64_t c, int64_t h,
+                           int64_t w, int64_t c_store, void* stream) {
+  if (x_nchw == nullptr || x_split == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || c_store < c || c_store % 16 != 0) {
+    return fail(IE_INVALID_ARGUMENT, "bad activation shape");
+  }
+  const int64_t hw = h * w;
+  dim3 grid(static_cast<unsigned>(ceil_div(hw, 32)), static_cast<unsigned>(ceil_div(c_store, 32)),
+            static_cast<unsigned>(n));
+  if (grid.z > 65535 || grid.y > 65535) return fail(IE_UNSUPPORTED, "batch or channels too large");
+  pack_nchw_f32_to_bf16x2<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(
+      x_nchw, static_cast<__nv_bfloat16*>(x_split), static_cast<int32_t>(c), hw,
+      static_cast<int32_t>(c_store));
+  return check_launch("pack_nchw_f32_to_bf16x2");
+}
+
+int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x_split,
+                          const void* packed, const float* bias, void* y, int32_t y_format,
+                          void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_dense(desc)) != IE_OK) return rc;
+  if ((rc = check_ptr(x_split, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(packed, "packed weights", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  if (act < IE_ACT_NONE || act > IE_ACT_RELU6) return fail(IE_INVALID_ARGUMENT, "bad activation");
+  const int64_t c_store = round_up(desc->c, 16);
+  IgemmSetup su;
+  if ((rc = setup_igemm(desc, s, 2, c_store, x_split, packed, &su)) != IE_OK) return rc;
+  IgemmArgs& a = su.args;
+  a.bias_f32 = bias;
+  a.act_lo = act == IE_ACT_NONE ? -INFINITY : 0.0f;
+  a.act_hi = act == IE_ACT_RELU6 ? 6.0f : INFINITY;
+  a.y = y;
+  switch (y_format) {
+    case IE_Y_F32_NHWC:
+      a.out_mode = kOutF32;
+      a.y_ld = round_up(desc->m, 16);
+      break;
+    case IE_Y_BF16X2_NHWC:
+      a.out_mode = kOutBF16x2;
+      a.y_ld = 2 * round_up(desc->m, 16);
+      break;
+    case IE_Y_F32_NCHW:
+      a.out_mode = kOutF32Nchw;
+      a.y_ld = 0;
+      break;
+    default:
+      return fail(IE_INVALID_ARGUMENT, "bad output format");
+  }
+  LaunchFn fn = pick_launch<false, false>(su.bn, su.bkb);
+  if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
+  return fn(su.ta, su.tb, a, as_stream(stream));
+}
+
+size_t ie_cuda_conv2d_f32_workspace_bytes(const ie_conv2d_desc* desc) {
+  if (desc == nullptr || desc->group != 1) return 0;
+  const int64_t c_store = round_up(desc->c, 16);
+  const size_t x_bytes =
+      static_cast<size_t>(round_up(desc->n * desc->h * desc->w * c_store * 2 * 2, 256));
+  return x_bytes + round_up(static_cast<int64_t>(ie_cuda_f32_packed_weight_bytes(desc)), 256);
+}
+
+int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x, const float* w,
+                       const float* bias, float* y, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  if (act < IE_ACT_NONE || act > IE_ACT_RELU6) return fail(IE_INVALID_ARGUMENT, "bad activation");
+  if (desc->group != 1) {
+    DirectF32Args a;
+    a.n = static_cast<int32_t>(desc->n);
+    a.c = static_cast<int32_t>(desc->c);
+    a.h = static_cast<int32_t>(desc->h);
+    a.w = static_cast<int32_t>(desc->w);
+    a.m = static_cast<int32_t>(desc->m);
+    a.cg = static_cast<int32_t>(desc->c / desc->group);
+    a.kh = static_cast<int32_t>(desc->kh);
+    a.kw = static_cast<int32_t>(desc->kw);
+    a.stride_h = static_cast<int32_t>(desc->stride_h);
+    a.stride_w = static_cast<int32_t>(desc->stride_w);
+    a.dil_h = static_cast<int32_t>(desc->dil_h);
+    a.dil_w = static_cast<int32_t>(desc->dil_w);
+    a.pad_t = static_cast<int32_t>(s.pad_top);
+    a.pad_l = static_cast<int32_t>(s.pad_left);
+    a.out_h = static_cast<int32_t>(s.out_h);
+    a.out_w = static_cast<int32_t>(s.out_w);
+    a.group = static_cast<int32_t>(desc->group);
+    a.act = act;
+    a.act_lo = 0.0f;
+    a.act_hi = act == IE_ACT_RELU6 ? 6.0f : INFINITY;
+    const int64_t total = desc->n * desc->m * s.out_h * s.out_w;
+    conv_direct_f32_nchw<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(x, w, bias, y, a);
+    return check_launch("conv_direct_f32_nchw");
+  }
+  const size_t need = ie_cuda_conv2d_f32_workspace_bytes(desc);
+  if (workspace == nullptr || workspace_bytes < need) {
+    return fail(IE_INVALID_ARGUMENT, "workspace too small: need %zu bytes", need);
+  }
+  if ((rc = check_ptr(workspace, "workspace", 256)) != IE_OK) return rc;
+  const int64_t c_store = round_up(desc->c, 16);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* x_split = ws;
+  void* packed = ws + round_up(desc->n * desc->h * desc->w * c_store * 4, 256);
+  if ((rc = ie_cuda_f32_pack_input(x, x_split, desc->n, desc->c, desc->h, desc->w, c_store,
+                                   stream)) != IE_OK) {
+    return rc;
+  }
+  if ((rc = ie_cuda_f32_pack_weights(desc, w, packed, stream)) != IE_OK) return rc;
+  return ie_cuda_conv2d_bf16x3(desc, act, x_split, packed, bias, y, IE_Y_F32_NCHW, stream);
+}
+
+}  // extern "C"

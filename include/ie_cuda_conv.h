@@ -1,0 +1,207 @@
+/*
+ * ie_cuda_conv.h -- C ABI of the B200 (sm_100a) Conv2D forward backend.
+ *
+ * This is the thin extern "C" shim between host code (the engine's
+ * CudaConv2DOp / CudaDepthwiseConv2DOp, the benchmark, ctypes tests) and the
+ * hand-written CUDA kernels.  Plain pointers and sizes only: every tensor
+ * pointer is DEVICE memory unless stated otherwise, every call is
+ * asynchronous on the given stream (NULL = legacy default stream), and no call
+ * allocates device memory: buffers and workspaces come from the caller.
+ *
+ * Reference interfaces replaced (grayondream/ComputeEngine):
+ *   conv2d_forward          src/ops/traditional/conv2d_op.cpp:73-245
+ *   Conv2DOp::forward       src/ops/traditional/conv2d_op.h:42-46
+ *   DepthwiseConv2DOp       src/ops/traditional/conv2d_op.h:53-67
+ *   parse_conv_config       src/ops/traditional/conv2d_op.cpp:26-71 (attrs)
+ *   same_padding            src/ops/traditional/attrs_util.h:185-197
+ *   KernelFns::matmul_row   src/core/ops/kernel_fns.h:10-18 (the inner GEMM)
+ *   Int8QuantPlugin         src/converter/quantization/quant_plugins.h:7-22
+ *                           (stub in the reference; the int8 scheme below is
+ *                           this backend's own)
+ *
+ * Status codes mirror ie::Error::Code (src/core/base/error.h:10-17) shifted
+ * by one, so 0 means success.
+ */
+#ifndef IE_CUDA_CONV_H
+#define IE_CUDA_CONV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IE_CUDA_CONV_ABI_VERSION 1
+
+typedef enum ie_status {
+  IE_OK = 0,
+  IE_INVALID_ARGUMENT = 1, /* Error::Code::InvalidArgument */
+  IE_UNSUPPORTED = 2,      /* Error::Code::Unsupported */
+  IE_NOT_FOUND = 3,        /* Error::Code::NotFound */
+  IE_ALREADY_EXISTS = 4,   /* Error::Code::AlreadyExists */
+  IE_OUT_OF_MEMORY = 5,    /* Error::Code::OutOfMemory */
+  IE_RUNTIME = 6           /* Error::Code::Runtime (CUDA errors map here) */
+} ie_status;
+
+/* auto_pad (attrs_util.h:18: AutoPad::{NotSet, Valid, SameUpper, SameLower}) */
+enum { IE_PAD_NOTSET = 0, IE_PAD_VALID = 1, IE_PAD_SAME_UPPER = 2, IE_PAD_SAME_LOWER = 3 };
+
+/* Activation folded into the epilogue.  The reference runs these as separate
+ * Relu (core/ops/common/relu_op.h) and Clip (data_ops.cpp:1078) nodes. */
+enum { IE_ACT_NONE = 0, IE_ACT_RELU = 1, IE_ACT_RELU6 = 2 };
+
+/* Convolution attributes and shapes, the union of ConvConfig
+ * (conv2d_op.h:13-21) and the tensor shapes conv2d_forward reads
+ * (conv2d_op.cpp:94-102).  x is [n, c, h, w], weight [m, c/group, kh, kw]. */
+typedef struct ie_conv2d_desc {
+  int64_t n, c, h, w;
+  int64_t m, kh, kw;
+  int64_t stride_h, stride_w;
+  int64_t dil_h, dil_w;
+  int64_t pad_top, pad_left, pad_bottom, pad_right; /* the "pads" attribute */
+  int64_t group;
+  int32_t auto_pad;  /* IE_PAD_* */
+  int32_t depthwise; /* 1: DepthwiseConv2D semantics (group must equal c) */
+} ie_conv2d_desc;
+
+/* Output of ie_conv2d_resolve: pads after auto_pad, output extent. */
+typedef struct ie_conv2d_shape {
+  int64_t pad_top, pad_left, pad_bottom, pad_right;
+  int64_t out_h, out_w;
+} ie_conv2d_shape;
+
+/* Per-tensor quantization of one int8 convolution.
+ *   acc = sum (xq - zp_x) * wq         int32, padding contributes real 0.0
+ *   t   = acc + bias[m]                int32
+ *   v   = (float)t * mult[m]           mult = s_x * s_w[m] / s_y, fp32
+ *   r   = roundf(v)                    round half away from zero
+ *   yq  = clamp(r, qmin - zp_y, qmax - zp_y) + zp_y
+ * ReLU folds in as qmin = zp_y, ReLU6 as qmax = zp_y + round(6 / s_y). */
+typedef struct ie_q8_params {
+  int32_t x_signed; /* activations stored as int8 (1) or uint8 (0) */
+  int32_t zp_x;     /* must be 0 for the NHWC kernels; see ie_cuda_q8_pack_input */
+  int32_t y_signed; /* output stored as int8 (1) or uint8 (0) */
+  int32_t zp_y;
+  int32_t qmin, qmax;
+} ie_q8_params;
+
+/* ------------------------------------------------------------ geometry */
+
+/* Validates a convolution exactly as conv2d_forward does
+ * (conv2d_op.cpp:77-165): positive dims, group divides c and m, weight
+ * channels == c/group, depthwise needs group == c, bias length (pass -1 for
+ * "no bias"), kernel not larger than the padded input, non-empty output.
+ * Resolves SAME_UPPER / SAME_LOWER / VALID padding (attrs_util.h:185-197).
+ * Host-only, no CUDA call. */
+int ie_conv2d_resolve(const ie_conv2d_desc* desc, int64_t bias_len, ie_conv2d_shape* out);
+
+/* ------------------------------------------------------------ int8 path */
+
+/* Bytes of the packed weight buffer for ie_cuda_q8_pack_weights. */
+size_t ie_cuda_q8_packed_weight_bytes(const ie_conv2d_desc* desc);
+
+/* Repacks int8 weights [m, c/group, kh, kw] (device) into the K-major layout
+ * the implicit-GEMM kernel reads: [m][kh][kw][c padded to the channel block],
+ * zero filled.  Dense convolutions (group == 1) only. */
+int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
+                            void* stream);
+
+/* NCHW -> NHWC for 8-bit activations, c_store >= c channels per pixel
+ * (c_store a multiple of 16, extra channels zero).  xor_mask 0x80 turns
+ * uint8 with zero point 128 into int8 with zero point 0, so zero padding is
+ * exact; pass 0 to copy bytes unchanged. */
+int ie_cuda_q8_pack_input(const void* x_nchw, void* x_nhwc, int64_t n, int64_t c, int64_t h,
+                          int64_t w, int64_t c_store, int32_t xor_mask, void* stream);
+
+/* NHWC (c_store channels per pixel) -> NCHW for 8-bit activations. */
+int ie_cuda_q8_unpack_output(const void* y_nhwc, void* y_nchw, int64_t n, int64_t c,
+                             int64_t h, int64_t w, int64_t c_store, void* stream);
+
+/* int8 convolution, dense (group == 1), NHWC in and out.
+ *   x      [n, h, w, c_store] int8/uint8, c_store = c rounded up to 16
+ *   packed ie_cuda_q8_pack_weights output
+ *   bias   [m] int32 or NULL;  mult [m] fp32
+ *   y      [n, out_h, out_w, m] (m a multiple of 16)
+ * Tensor cores: tcgen05.mma kind::i8, TMA im2col loads, TMEM accumulators,
+ * bias + requantize + clamp fused into the epilogue.  Replaces
+ * conv2d_forward for quantized graphs. */
+int ie_cuda_conv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                      const void* packed, const int32_t* bias, const float* mult, void* y,
+                      void* stream);
+
+/* Same, writing raw int32 (acc + bias) instead of requantized bytes. */
+int ie_cuda_conv2d_q8_acc(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                          const void* packed, const int32_t* bias, int32_t* y, void* stream);
+
+/* Depthwise int8 weights [c, 1, kh, kw] -> [kh*kw][c rounded up to 16]. */
+size_t ie_cuda_dw_q8_packed_weight_bytes(const ie_conv2d_desc* desc);
+int ie_cuda_dw_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
+                               void* stream);
+
+/* Depthwise int8 convolution (group == c == m), NHWC in and out with c
+ * rounded up to 16 channels per pixel.  Any input zero point (padding still
+ * contributes real 0.0).  CUDA cores, 128-bit channel vectors, bandwidth
+ * bound.  Replaces DepthwiseConv2DOp (conv2d_op.h:53-67) for quantized
+ * graphs. */
+int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
+                        const void* packed, const int32_t* bias, const float* mult, void* y,
+                        void* stream);
+
+/* ------------------------------------------------------------ fp32 path */
+
+/* Output formats of ie_cuda_conv2d_bf16x3. */
+enum {
+  IE_Y_F32_NHWC = 0,    /* fp32 [n, oh, ow, m rounded up to 16] */
+  IE_Y_F32_NCHW = 1,    /* fp32 [n, m, oh, ow], the reference layout */
+  IE_Y_BF16X2_NHWC = 2  /* bf16 [n, oh, ow, hi plane | lo plane], next layer's input */
+};
+
+/* fp32 weights [m, c, kh, kw] -> bf16 [m][kh*kw][hi (ck) | lo (ck)]. */
+size_t ie_cuda_f32_packed_weight_bytes(const ie_conv2d_desc* desc);
+int ie_cuda_f32_pack_weights(const ie_conv2d_desc* desc, const float* w, void* packed,
+                             void* stream);
+
+/* fp32 NCHW -> NHWC bf16 [hi plane (c_store) | lo plane (c_store)] per pixel,
+ * c_store >= c a multiple of 16 (padding channels zero). */
+int ie_cuda_f32_pack_input(const float* x_nchw, void* x_split, int64_t n, int64_t c, int64_t h,
+                           int64_t w, int64_t c_store, void* stream);
+
+/* Dense fp32 convolution on split inputs (group == 1): tcgen05.mma kind::f16
+ * with bf16 operands, three MMAs per K block (hi*hi + hi*lo + lo*hi) into
+ * one fp32 TMEM accumulator; bias and activation fused in the epilogue.
+ * x_split has c rounded up to 16 channels per plane. */
+int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x_split,
+                          const void* packed, const float* bias, void* y, int32_t y_format,
+                          void* stream);
+
+/* fp32 convolution, NCHW in and out, the drop-in for conv2d_forward
+ * (conv2d_op.cpp:73-245) on fp32 tensors.  Runs as bf16x3 on the tensor
+ * cores (x = xh + xl, w = wh + wl; xh*wh + xh*wl + xl*wh accumulated in
+ * fp32) for dense convolutions, on CUDA cores for depthwise / grouped ones.
+ * bias may be NULL; act is IE_ACT_*.  workspace must hold
+ * ie_cuda_conv2d_f32_workspace_bytes(desc) bytes (256-byte aligned). */
+size_t ie_cuda_conv2d_f32_workspace_bytes(const ie_conv2d_desc* desc);
+int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x,
+                       const float* w, const float* bias, float* y, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ errors */
+
+/* Human-readable detail of the last failing call on this host thread. */
+const char* ie_cuda_last_error(void);
+
+/* Reads and clears the device-side error word of the current device: nonzero
+ * when a kernel's bounded wait ran out (the kernel then returned early and
+ * its output is invalid).  Synchronizes the device. */
+int ie_cuda_take_device_error(uint32_t* code);
+
+/* Number of kernel launches this library issued on the calling host thread
+ * since the last reset (for the benchmark's launch count). */
+uint64_t ie_cuda_launch_count(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IE_CUDA_CONV_H */

@@ -1,0 +1,190 @@
+"""ctypes front end of the CPU checkers: TEST INFRASTRUCTURE ONLY.
+
+Loaded by the test suite, the smoke check and the CPU-baseline leg of the
+benchmark, never by the shipped library.  Two checkers live here:
+
+* ``Oracle``   -- the C restatement in conv_oracle.c (fp32 and int8), built
+  into oracle/liboracle_conv.so.
+* ``RefConv``  -- the reference engine's own Conv2DOp compiled from its sources
+  into oracle/_ref/libref_conv.so (absent where the reference tree was not
+  available at build time; callers skip in that case).
+
+Arrays are numpy, NCHW, C-contiguous, host memory.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle_conv.so"
+REF_SO = HERE / "_ref" / "libref_conv.so"
+
+# auto_pad codes (reference src/ops/traditional/attrs_util.h:18)
+AUTO_PAD = {"NOTSET": 0, "": 0, "VALID": 1, "SAME_UPPER": 2, "SAME_LOWER": 3}
+# status codes: 0 ok, 1 + ie::Error::Code (reference src/core/base/error.h:10-17)
+OK, INVALID_ARGUMENT, UNSUPPORTED = 0, 1, 2
+
+_i64 = C.c_int64
+_p = C.c_void_p
+
+
+class Geom(C.Structure):
+    _fields_ = [(name, _i64) for name in (
+        "n", "c", "h", "w", "m", "cg", "kh", "kw", "stride_h", "stride_w",
+        "dil_h", "dil_w", "pad_t", "pad_l", "pad_b", "pad_r", "group",
+        "out_h", "out_w")]
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(_p)
+
+
+def build_oracle() -> None:
+    """Compiles the C restatement if its library is missing."""
+    if not ORACLE_SO.exists():
+        subprocess.run(["make", "-C", str(HERE), "liboracle_conv.so"], check=True,
+                       stdout=subprocess.DEVNULL)
+
+
+class OracleError(RuntimeError):
+    def __init__(self, code: int):
+        super().__init__(f"oracle status {code}")
+        self.code = code
+
+
+class Oracle:
+    def __init__(self):
+        build_oracle()
+        lib = C.CDLL(str(ORACLE_SO))
+        lib.orc_conv_resolve.restype = C.c_int
+        lib.orc_conv_resolve.argtypes = [_i64] * 12 + [C.POINTER(_i64), _i64, C.c_int,
+                                                        C.c_int, _i64, C.POINTER(Geom)]
+        lib.orc_conv2d_f32.restype = C.c_int
+        lib.orc_conv2d_f32.argtypes = [C.POINTER(Geom), _p, _p, _p, C.c_int, _p, C.c_int]
+        lib.orc_conv2d_q8.restype = C.c_int
+        lib.orc_conv2d_q8.argtypes = [C.POINTER(Geom), _p, C.c_int, C.c_int32, _p, _p, _p,
+                                      C.c_int32, C.c_int32, C.c_int32, C.c_int, _p, _p,
+                                      C.c_int]
+        lib.orc_requantize.restype = C.c_int32
+        lib.orc_requantize.argtypes = [C.c_int32, C.c_int32, C.c_float, C.c_int32,
+                                       C.c_int32, C.c_int32]
+        lib.orc_same_padding.restype = None
+        lib.orc_same_padding.argtypes = [_i64, _i64, _i64, _i64, C.c_int,
+                                         C.POINTER(_i64), C.POINTER(_i64)]
+        self.lib = lib
+
+    # -- geometry ---------------------------------------------------------
+    def resolve(self, x_shape, w_shape, strides=(1, 1), dilations=(1, 1),
+                pads=(0, 0, 0, 0), group=1, auto_pad="NOTSET", depthwise=False,
+                bias_len=-1) -> Geom:
+        g = Geom()
+        pads4 = (_i64 * 4)(*pads)
+        rc = self.lib.orc_conv_resolve(*x_shape, *w_shape, strides[0], strides[1],
+                                       dilations[0], dilations[1], pads4, group,
+                                       AUTO_PAD[auto_pad], int(depthwise), bias_len,
+                                       C.byref(g))
+        if rc != OK:
+            raise OracleError(rc)
+        return g
+
+    def same_padding(self, size, kernel, dilation, stride, lower):
+        b, a = _i64(), _i64()
+        self.lib.orc_same_padding(size, kernel, dilation, stride, int(lower),
+                                  C.byref(b), C.byref(a))
+        return b.value, a.value
+
+    # -- fp32 -------------------------------------------------------------
+    def conv2d_f32(self, x, w, b=None, act=0, nthreads=1, **geom_kw):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        if b is not None:
+            b = np.ascontiguousarray(b, dtype=np.float32)
+        g = self.resolve(x.shape, w.shape, bias_len=-1 if b is None else b.shape[0],
+                         **geom_kw)
+        y = np.empty((g.n, g.m, g.out_h, g.out_w), np.float32)
+        rc = self.lib.orc_conv2d_f32(C.byref(g), _ptr(x), _ptr(w), _ptr(b), act,
+                                     _ptr(y), nthreads)
+        if rc != OK:
+            raise OracleError(rc)
+        return y
+
+    # -- int8 -------------------------------------------------------------
+    def conv2d_q8(self, x, w, bias, mult, zp_x, zp_y, qmin, qmax, y_signed=False,
+                  want_acc=False, nthreads=1, **geom_kw):
+        assert x.dtype in (np.uint8, np.int8)
+        x = np.ascontiguousarray(x)
+        w = np.ascontiguousarray(w, dtype=np.int8)
+        mult = np.ascontiguousarray(mult, dtype=np.float32)
+        if bias is not None:
+            bias = np.ascontiguousarray(bias, dtype=np.int32)
+        g = self.resolve(x.shape, w.shape, bias_len=-1 if bias is None else bias.shape[0],
+                         **geom_kw)
+        y = np.empty((g.n, g.m, g.out_h, g.out_w), np.int8 if y_signed else np.uint8)
+        acc = np.empty(y.shape, np.int32) if want_acc else None
+        rc = self.lib.orc_conv2d_q8(C.byref(g), _ptr(x), int(x.dtype == np.int8), zp_x,
+                                    _ptr(w), _ptr(bias), _ptr(mult), zp_y, qmin, qmax,
+                                    int(y_signed), _ptr(y), _ptr(acc), nthreads)
+        if rc != OK:
+            raise OracleError(rc)
+        return (y, acc) if want_acc else y
+
+    def requantize(self, acc, bias, mult, zp_y, qmin, qmax):
+        return self.lib.orc_requantize(acc, bias, mult, zp_y, qmin, qmax)
+
+
+class RefConv:
+    """The reference Conv2DOp / DepthwiseConv2DOp, compiled from its sources."""
+
+    def __init__(self):
+        if not REF_SO.exists():
+            raise FileNotFoundError(str(REF_SO))
+        lib = C.CDLL(str(REF_SO))
+        lib.ref_row_kernel.restype = C.c_int
+        lib.ref_conv2d_f32.restype = C.c_int
+        lib.ref_conv2d_f32.argtypes = [_p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                                       _i64, _p, _p, _p, _p, _i64, C.c_int, C.c_int,
+                                       C.c_int, C.c_int, _p, _p]
+        self.lib = lib
+
+    @staticmethod
+    def available() -> bool:
+        return REF_SO.exists()
+
+    def row_kernel(self) -> str:
+        return ["scalar", "sse2", "avx2", "avx512"][self.lib.ref_row_kernel()]
+
+    def conv2d(self, x, w, b=None, strides=(1, 1), dilations=(1, 1), pads=(0, 0, 0, 0),
+               group=1, auto_pad="NOTSET", depthwise=False, kernel_choice=-1,
+               nthreads=1):
+        """Returns (status, y); y is None when status != 0."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        if b is not None:
+            b = np.ascontiguousarray(b, dtype=np.float32)
+        s = np.array(strides, np.int64)
+        d = np.array(dilations, np.int64)
+        p = np.array(pads, np.int64)
+        dims = np.zeros(4, np.int64)
+        rc = self.lib.ref_conv2d_f32(_ptr(x), *x.shape, _ptr(w), *w.shape, _ptr(b), _ptr(s),
+                                     _ptr(d), _ptr(p), group, AUTO_PAD[auto_pad],
+                                     int(depthwise), kernel_choice, 1, None, _ptr(dims))
+        if rc != OK:
+            return rc, None
+        y = np.empty(tuple(int(v) for v in dims), np.float32)
+        rc = self.lib.ref_conv2d_f32(_ptr(x), *x.shape, _ptr(w), *w.shape, _ptr(b), _ptr(s),
+                                     _ptr(d), _ptr(p), group, AUTO_PAD[auto_pad],
+                                     int(depthwise), kernel_choice, nthreads, _ptr(y),
+                                     _ptr(dims))
+        return rc, (y if rc == OK else None)
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1

@@ -1,0 +1,71 @@
+"""int8 implicit-GEMM convolution (tcgen05 kind::i8) against the int8 oracle,
+through the C ABI.  Bit-exact: integer accumulators, then the requantize rule
+(round half away from zero, saturate) on identical fp32 multipliers."""
+import numpy as np
+import pytest
+
+from tests.qconv import make_q8_problem, run_conv_q8_gpu
+
+pytestmark = pytest.mark.gpu
+
+# (n, c, h, w, m, kh, kw, stride, pads)
+ACC_CASES = [
+    (1, 64, 16, 16, 64, 1, 1, (1, 1), (0, 0, 0, 0)),      # plain GEMM, 2 M tiles
+    (1, 64, 16, 16, 64, 3, 3, (1, 1), (1, 1, 1, 1)),      # 3x3 pad 1
+    (2, 128, 14, 14, 128, 3, 3, (1, 1), (1, 1, 1, 1)),    # tile crosses images
+    (1, 256, 7, 7, 256, 1, 1, (1, 1), (0, 0, 0, 0)),      # BN 256, tail tile
+    (2, 64, 15, 13, 96, 3, 3, (2, 2), (1, 1, 1, 1)),      # stride 2, odd sizes
+    (1, 48, 12, 12, 32, 1, 1, (2, 2), (0, 0, 0, 0)),      # 1x1 stride 2, c not /64
+    (1, 16, 20, 20, 64, 7, 7, (2, 2), (3, 3, 3, 3)),      # 7x7 stride 2
+    (3, 512, 7, 7, 512, 3, 3, (1, 1), (1, 1, 1, 1)),      # deep K
+    (1, 32, 9, 11, 16, 3, 3, (1, 1), (0, 2, 1, 0)),       # asymmetric pads, m=16
+    (1, 160, 10, 10, 320, 1, 1, (1, 1), (0, 0, 0, 0)),    # c = 160 (32-byte blocks)
+]
+
+
+@pytest.mark.parametrize("case", ACC_CASES, ids=lambda c: "x".join(map(str, c[:7])) + f"_s{c[7][0]}")
+def test_accumulators_match_oracle(oracle, case):
+    n, c, h, w, m, kh, kw, stride, pads = case
+    rng = np.random.default_rng(1234 + n * c + m)
+    x, wq, bias, mult = make_q8_problem(rng, n, c, h, w, m, kh, kw)
+    got = run_conv_q8_gpu(x, wq, bias, mult, stride=stride, pads=pads, raw_acc=True)
+    _, acc = oracle.conv2d_q8(x, wq, bias, mult, 128, 0, 0, 255, want_acc=True,
+                              strides=stride, pads=pads)
+    want = acc + bias.reshape(1, -1, 1, 1)
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("case", ACC_CASES[:6], ids=lambda c: "x".join(map(str, c[:7])))
+def test_requantized_output_bit_exact(oracle, case):
+    n, c, h, w, m, kh, kw, stride, pads = case
+    rng = np.random.default_rng(99 + c)
+    # Output scale chosen so results spread over 0..255 instead of saturating.
+    x, wq, bias, mult = make_q8_problem(rng, n, c, h, w, m, kh, kw, s_y=0.05 * np.sqrt(c * kh * kw) * 3)
+    got = run_conv_q8_gpu(x, wq, bias, mult, stride=stride, pads=pads)
+    want = oracle.conv2d_q8(x, wq, bias, mult, 128, 0, 0, 255, strides=stride, pads=pads)
+    np.testing.assert_array_equal(got, want)
+    assert 0.05 < np.mean((want > 0) & (want < 255)), "problem should not be all-saturated"
+
+
+def test_config2_int8_conv_bit_exact(oracle):
+    """The single int8 conv workload: x uint8 [8,128,28,28] zp 128 s 0.02,
+    w [128,128,3,3] U{-127..127}, s_w U(0.001,0.01), bias N(0,500),
+    y uint8 s 0.05 zp 0 with ReLU folded, stride 1 pad 1."""
+    rng = np.random.default_rng(0)
+    x, wq, bias, mult = make_q8_problem(rng, 8, 128, 28, 28, 128, 3, 3)
+    got = run_conv_q8_gpu(x, wq, bias, mult, pads=(1, 1, 1, 1))
+    want = oracle.conv2d_q8(x, wq, bias, mult, 128, 0, 0, 255, pads=(1, 1, 1, 1), nthreads=8)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_relu6_clamp_and_unsigned_input(oracle):
+    rng = np.random.default_rng(5)
+    x, wq, bias, mult = make_q8_problem(rng, 2, 64, 10, 10, 64, 3, 3, x_zp=0, x_std=40,
+                                        s_y=0.5)
+    zp_y, qmax = 3, 3 + 120
+    got = run_conv_q8_gpu(x, wq, bias, mult, pads=(1, 1, 1, 1), zp_x=0, zp_y=zp_y, qmin=zp_y,
+                          qmax=qmax)
+    want = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, zp_y, qmax, pads=(1, 1, 1, 1))
+    np.testing.assert_array_equal(got, want)
+    assert want.min() == zp_y and want.max() == qmax
