@@ -70,6 +70,11 @@ def _load() -> C.CDLL:
         "ie_cuda_dw_q8_packed_weight_bytes": (C.c_size_t, [P(ConvDesc)]),
         "ie_cuda_dw_q8_pack_weights": (C.c_int, [P(ConvDesc), _p, _p, _p]),
         "ie_cuda_dwconv2d_q8": (C.c_int, [P(ConvDesc), P(Q8Params), _p, _p, _p, _p, _p, _p]),
+        "ie_cuda_q8_stem_desc": (C.c_int, [_i64, _i64, _i64, _i64, _i64, P(ConvDesc)]),
+        "ie_cuda_q8_stem_pack_input": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i32, _p]),
+        "ie_cuda_q8_stem_pack_weights": (C.c_int, [_p, _p, _i64, _i64, _p]),
+        "ie_cuda_q8_maxpool2d": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                           _i32, _p]),
         "ie_cuda_f32_packed_weight_bytes": (C.c_size_t, [P(ConvDesc)]),
         "ie_cuda_f32_pack_weights": (C.c_int, [P(ConvDesc), _p, _p, _p]),
         "ie_cuda_f32_pack_input": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p]),

@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
           const bool in = ch < args.m;
           if constexpr (KIND_I8) {
             sb[j] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
-            sm[j] = in ? __ldg(args.mult + ch) : 0.0f;
+            sm[j] = (in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f;
             sbf[j] = 0.0f;
           } else {
             sb[j] = 0;

@@ -460,6 +460,76 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
   return check_launch("dwconv_q8_nhwc");
 }
 
+// -------------------------------------------------------------- stem
+
+int ie_cuda_q8_stem_desc(int64_t n, int64_t c, int64_t h, int64_t w, int64_t m,
+                         ie_conv2d_desc* out) {
+  if (out == nullptr) return fail(IE_INVALID_ARGUMENT, "null descriptor");
+  if (n <= 0 || c <= 0 || c > 4 || h <= 0 || w <= 0 || h % 2 || w % 2 || m <= 0) {
+    return fail(IE_UNSUPPORTED, "stem re-layout needs 1 <= c <= 4 and even h, w");
+  }
+  std::memset(out, 0, sizeof(*out));
+  out->n = n;
+  out->c = 64;
+  out->h = h / 2;
+  out->w = w / 2;
+  out->m = m;
+  out->kh = 4;
+  out->kw = 1;
+  out->stride_h = out->stride_w = 1;
+  out->dil_h = out->dil_w = 1;
+  out->pad_top = 2;
+  out->pad_bottom = 1;
+  out->group = 1;
+  return IE_OK;
+}
+
+int ie_cuda_q8_stem_pack_input(const void* x_nchw, void* x_packed, int64_t n, int64_t c,
+                               int64_t h, int64_t w, int32_t xor_mask, void* stream) {
+  ie_conv2d_desc d;
+  int rc = ie_cuda_q8_stem_desc(n, c, h, w, 1, &d);
+  if (rc != IE_OK) return rc;
+  if (x_nchw == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if ((rc = check_ptr(x_packed, "x_packed", 16)) != IE_OK) return rc;
+  const int64_t total = n * (h / 2) * (w / 2) * 4;
+  stem_pack_s2d_u8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x_nchw), static_cast<uint8_t*>(x_packed),
+      static_cast<int32_t>(n), static_cast<int32_t>(c), static_cast<int32_t>(h),
+      static_cast<int32_t>(w), static_cast<uint8_t>(xor_mask & 0xFF));
+  return check_launch("stem_pack_s2d_u8");
+}
+
+int ie_cuda_q8_stem_pack_weights(const int8_t* w, void* packed, int64_t m, int64_t c,
+                                 void* stream) {
+  if (w == nullptr || packed == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if (m <= 0 || c <= 0 || c > 4) return fail(IE_UNSUPPORTED, "stem re-layout needs 1 <= c <= 4");
+  const int64_t total = m * 4 * 64;
+  stem_pack_weights_q8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      w, static_cast<int8_t*>(packed), static_cast<int32_t>(m), static_cast<int32_t>(c));
+  return check_launch("stem_pack_weights_q8");
+}
+
+int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,
+                         int64_t c_store, int64_t k, int64_t stride, int64_t pad,
+                         int32_t is_signed, void* stream) {
+  int rc;
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  if (n <= 0 || h <= 0 || w <= 0 || c_store <= 0 || c_store % 16 || k <= 0 || stride <= 0 ||
+      pad < 0 || pad >= k) {
+    return fail(IE_INVALID_ARGUMENT, "bad pooling shape");
+  }
+  const int64_t oh = (h + 2 * pad - k) / stride + 1, ow = (w + 2 * pad - k) / stride + 1;
+  if (oh <= 0 || ow <= 0) return fail(IE_INVALID_ARGUMENT, "pooling produces an empty output");
+  const int64_t total = n * oh * ow * (c_store / 16);
+  maxpool_q8_nhwc<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), static_cast<int32_t>(n),
+      static_cast<int32_t>(h), static_cast<int32_t>(w), static_cast<int32_t>(c_store),
+      static_cast<int32_t>(oh), static_cast<int32_t>(ow), static_cast<int32_t>(k),
+      static_cast<int32_t>(stride), static_cast<int32_t>(pad), is_signed);
+  return check_launch("maxpool_q8_nhwc");
+}
+
 // -------------------------------------------------------------- fp32
 
 size_t ie_cuda_f32_packed_weight_bytes(const ie_conv2d_desc* desc) {

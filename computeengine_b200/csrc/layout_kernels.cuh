@@ -129,3 +129,103 @@ __global__ void pack_weights_bf16x2(const float* __restrict__ w, __nv_bfloat16* 
 }
 
 }  // namespace ie_cuda
+
+namespace ie_cuda {
+
+// Stem re-layout for a 7x7 / stride 2 / pad 3 convolution on c <= 4 channels.
+// Space-to-depth by 2 plus a 4-column unroll turns the stem into a 4x1,
+// stride-1 convolution over 16*c channels (stored as 64), so it runs on the
+// same implicit-GEMM kernel as every other layer:
+//   out[i][j][((b*2+dy)*2+dx)*c + ch] = x[ch][2i+dy][2(j+b-2)+dx]   (0 if j+b-2
+//   is outside [0, w/2)), i in [0, h/2), j in [0, w/2)
+__global__ void stem_pack_s2d_u8(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                 int32_t n, int32_t c, int32_t h, int32_t w, uint8_t xor_mask) {
+  const int32_t ho = h / 2, wo = w / 2;
+  const int64_t total = static_cast<int64_t>(n) * ho * wo * 4;
+  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= total) return;
+  const int32_t g = static_cast<int32_t>(idx & 3);
+  const int64_t pix = idx >> 2;
+  const int32_t j = static_cast<int32_t>(pix % wo);
+  const int32_t i = static_cast<int32_t>((pix / wo) % ho);
+  const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(wo) * ho));
+  const uint8_t* xi = x + static_cast<int64_t>(img) * c * h * w;
+  uint32_t out[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int32_t chan = g * 16 + k;
+    if (chan < 16 * c) {
+      const int32_t cc = chan % c;
+      const int32_t rest = chan / c;  // (b*2 + dy)*2 + dx
+      const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
+      const int32_t jj = j + b - 2;
+      if (jj >= 0 && jj < wo) {
+        const uint8_t v = xi[(static_cast<int64_t>(cc) * h + 2 * i + dy) * w + 2 * jj + dx] ^ xor_mask;
+        out[k >> 2] |= static_cast<uint32_t>(v) << (8 * (k & 3));
+      }
+    }
+  }
+  reinterpret_cast<uint4*>(y)[idx] = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Weights of the same stem, [m, c, 7, 7] int8 -> the 4x1 layer's weights in
+// packed form [m][4 taps][64 channels].
+__global__ void stem_pack_weights_q8(const int8_t* __restrict__ w, int8_t* __restrict__ out,
+                                     int32_t m, int32_t c) {
+  const int64_t total = static_cast<int64_t>(m) * 4 * 64;
+  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= total) return;
+  const int32_t chan = static_cast<int32_t>(idx % 64);
+  const int32_t a = static_cast<int32_t>((idx / 64) % 4);
+  const int32_t mo = static_cast<int32_t>(idx / 256);
+  int8_t v = 0;
+  if (chan < 16 * c) {
+    const int32_t cc = chan % c;
+    const int32_t rest = chan / c;
+    const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
+    const int32_t ky = 2 * a + dy - 1, kx = 2 * b + dx - 1;
+    if (ky >= 0 && ky < 7 && kx >= 0 && kx < 7) {
+      v = w[((static_cast<int64_t>(mo) * c + cc) * 7 + ky) * 7 + kx];
+    }
+  }
+  out[idx] = v;
+}
+
+// Max pooling over 8-bit NHWC activations, 16 channels per thread; windows
+// only cover real pixels (padding never wins).
+__global__ void maxpool_q8_nhwc(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                int32_t n, int32_t h, int32_t w, int32_t c_store, int32_t oh,
+                                int32_t ow, int32_t k, int32_t stride, int32_t pad,
+                                int32_t is_signed) {
+  const int32_t groups = c_store >> 4;
+  const int64_t total = static_cast<int64_t>(n) * oh * ow * groups;
+  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= total) return;
+  const int32_t g = static_cast<int32_t>(idx % groups);
+  const int64_t pix = idx / groups;
+  const int32_t ox = static_cast<int32_t>(pix % ow);
+  const int32_t oy = static_cast<int32_t>((pix / ow) % oh);
+  const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(ow) * oh));
+  const uint32_t init = is_signed ? 0x80808080u : 0u;
+  uint4 best = make_uint4(init, init, init, init);
+  for (int ky = 0; ky < k; ++ky) {
+    const int32_t iy = oy * stride - pad + ky;
+    if (iy < 0 || iy >= h) continue;
+    for (int kx = 0; kx < k; ++kx) {
+      const int32_t ix = ox * stride - pad + kx;
+      if (ix < 0 || ix >= w) continue;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+          x + ((static_cast<int64_t>(img) * h + iy) * w + ix) * c_store + g * 16));
+      if (is_signed) {
+        best.x = __vmaxs4(best.x, v.x); best.y = __vmaxs4(best.y, v.y);
+        best.z = __vmaxs4(best.z, v.z); best.w = __vmaxs4(best.w, v.w);
+      } else {
+        best.x = __vmaxu4(best.x, v.x); best.y = __vmaxu4(best.y, v.y);
+        best.z = __vmaxu4(best.z, v.z); best.w = __vmaxu4(best.w, v.w);
+      }
+    }
+  }
+  reinterpret_cast<uint4*>(y)[pix * groups + g] = best;
+}
+
+}  // namespace ie_cuda

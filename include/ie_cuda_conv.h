@@ -148,6 +148,32 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
                         const void* packed, const int32_t* bias, const float* mult, void* y,
                         void* stream);
 
+/* Stem of the 53-layer ResNet-50 stack: a 7x7 / stride 2 / pad 3 convolution
+ * on c <= 4 input channels (h, w even).  Space-to-depth by 2 plus a 4-column
+ * unroll turns it into a 4x1 stride-1 convolution over 64 stored channels that
+ * runs on ie_cuda_conv2d_q8 like every other layer:
+ *   ie_cuda_q8_stem_desc         fills that equivalent descriptor
+ *   ie_cuda_q8_stem_pack_input   NCHW [n, c, h, w] 8-bit -> [n, h/2, w/2, 64],
+ *                                xor_mask as in ie_cuda_q8_pack_input
+ *   ie_cuda_q8_stem_pack_weights [m, c, 7, 7] int8 -> packed weights of the
+ *                                equivalent layer (ie_cuda_q8_packed_weight_bytes
+ *                                of the equivalent descriptor)
+ * The result equals the direct 7x7 / stride 2 convolution bit for bit. */
+int ie_cuda_q8_stem_desc(int64_t n, int64_t c, int64_t h, int64_t w, int64_t m,
+                         ie_conv2d_desc* out);
+int ie_cuda_q8_stem_pack_input(const void* x_nchw, void* x_packed, int64_t n, int64_t c,
+                               int64_t h, int64_t w, int32_t xor_mask, void* stream);
+int ie_cuda_q8_stem_pack_weights(const int8_t* w, void* packed, int64_t m, int64_t c,
+                                 void* stream);
+
+/* Max pooling (k x k, stride, symmetric pad, floor output size) over 8-bit
+ * NHWC activations with c_store (multiple of 16) channels per pixel.  The
+ * graph's MaxPool between the stem and stage 1 (pool_ops.cpp); padding never
+ * wins. */
+int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,
+                         int64_t c_store, int64_t k, int64_t stride, int64_t pad,
+                         int32_t is_signed, void* stream);
+
 /* ------------------------------------------------------------ fp32 path */
 
 /* Output formats of ie_cuda_conv2d_bf16x3. */

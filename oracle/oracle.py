@@ -188,3 +188,44 @@ def host_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+def maxpool2d_nchw(x: np.ndarray, k: int, stride: int, pad: int) -> np.ndarray:
+    """Max pooling restated from the reference's pool_ops.cpp (:141-166 of its
+    MaxPool2D path): windows start at oy*stride - pad, only in-bounds pixels
+    compete (the accumulator starts at -inf, so padding never wins), floor
+    output size (no ceil_mode)."""
+    n, c, h, w = x.shape
+    oh = (h + 2 * pad - k) // stride + 1
+    ow = (w + 2 * pad - k) // stride + 1
+    work = np.float32 if np.issubdtype(x.dtype, np.floating) else np.int32
+    big = -np.inf if work is np.float32 else np.iinfo(np.int32).min
+    xp = np.full((n, c, h + 2 * pad, w + 2 * pad), big, work)
+    xp[:, :, pad:pad + h, pad:pad + w] = x
+    out = np.full((n, c, oh, ow), big, work)
+    for ky in range(k):
+        for kx in range(k):
+            win = xp[:, :, ky:ky + stride * (oh - 1) + 1:stride, kx:kx + stride * (ow - 1) + 1:stride]
+            np.maximum(out, win, out=out)
+    return out.astype(x.dtype)
+
+
+def resnet_q8_chain(orc: "Oracle", layers, params, x_u8: np.ndarray, nthreads: int = 1,
+                    inputs=None):
+    """Runs the int8 ResNet-50 conv stack on the CPU oracle.  With ``inputs``
+    (a dict name -> NCHW array of the tensor each layer reads) every layer is
+    checked on its own, else the chain starts from ``x_u8``.  Returns a dict of
+    NCHW uint8 outputs (plus 'pool')."""
+    outs = {}
+    for l in layers:
+        p = params[l.name]
+        if inputs is not None and l.src != "input":
+            src = inputs[l.src]
+        else:
+            src = x_u8 if l.src == "input" else outs[l.src]
+        outs[l.name] = orc.conv2d_q8(src, p.w, p.bias, p.mult, p.zp_x, 0, 0, 255,
+                                     strides=(l.stride, l.stride), pads=(l.pad,) * 4,
+                                     nthreads=nthreads)
+        if l.name == "stem":
+            outs["pool"] = maxpool2d_nchw(outs["stem"], 3, 2, 1)
+    return outs

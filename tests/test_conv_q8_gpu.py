@@ -62,7 +62,7 @@ def test_config2_int8_conv_bit_exact(oracle):
 def test_relu6_clamp_and_unsigned_input(oracle):
     rng = np.random.default_rng(5)
     x, wq, bias, mult = make_q8_problem(rng, 2, 64, 10, 10, 64, 3, 3, x_zp=0, x_std=40,
-                                        s_y=0.5)
+                                        s_y=0.1)
     zp_y, qmax = 3, 3 + 120
     got = run_conv_q8_gpu(x, wq, bias, mult, pads=(1, 1, 1, 1), zp_x=0, zp_y=zp_y, qmin=zp_y,
                           qmax=qmax)
