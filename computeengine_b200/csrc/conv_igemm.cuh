@@ -77,6 +77,52 @@ __host__ __device__ constexpr uint32_t swizzle_layout_code(int row_bytes) {
 
 // ------------------------------------------------------------- epilogue
 
+// round-half-away-from-zero of v, as a float whose truncation is the result:
+// adding copysign(0.5, v) with round-toward-zero and truncating gives
+// floor(|v| + 0.5) * sign(v) exactly for every finite fp32 v (the directed
+// rounding keeps |v| = 0.5 - 2^-25 from rounding the sum up to 1.0).
+__device__ __forceinline__ float round_away_pre_trunc(float v) {
+  const float half = __int_as_float((__float_as_int(v) & 0x80000000) | 0x3f000000);
+  return __fadd_rz(v, half);
+}
+
+__device__ __forceinline__ uint32_t cvt_trunc_sat_u8(float x) {
+  uint32_t r;
+  asm("cvt.rzi.sat.u8.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_trunc_sat_s8(float x) {
+  uint32_t r;
+  asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r & 0xFFu;
+}
+
+// Requantizes 4 accumulators into 4 packed output bytes.
+//   kFast: zp_y == 0 and the clamp range is the whole storage type, so the
+//          saturating conversion is the clamp.
+template <bool kFast, bool kSigned>
+__device__ __forceinline__ uint32_t requant_pack4(const uint32_t* acc, int4 b4, float4 m4,
+                                                  int32_t zp, int32_t qmin, int32_t qmax) {
+  const int32_t bb[4] = {b4.x, b4.y, b4.z, b4.w};
+  const float mm[4] = {m4.x, m4.y, m4.z, m4.w};
+  uint32_t q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int32_t t = static_cast<int32_t>(acc[j] + static_cast<uint32_t>(bb[j]));
+    const float x = round_away_pre_trunc(__fmul_rn(__int2float_rn(t), mm[j]));
+    if constexpr (kFast) {
+      q[j] = kSigned ? cvt_trunc_sat_s8(x) : cvt_trunc_sat_u8(x);
+    } else {
+      int32_t v = __float2int_rz(x) + zp;
+      v = min(max(v, qmin), qmax);
+      q[j] = static_cast<uint32_t>(v) & 0xFFu;
+    }
+  }
+  return __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+}
+
+
 __device__ __forceinline__ uint32_t requant4(const uint32_t* acc, const int32_t* sb,
                                              const float* sm, int32_t zp, float lo, float hi,
                                              bool out_signed) {
@@ -203,7 +249,8 @@ __device__ __forceinline__ void epilogue_chunk(const IgemmArgs& a, const uint32_
 template <int BN, int BK_BYTES, int STAGES, int EPI_WARPS, bool KIND_I8, bool A_SIGNED>
 __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     conv_igemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                      const __grid_constant__ CUtensorMap tmap_b, const IgemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_y, const IgemmArgs args) {
   constexpr int kA = IgemmSmem<BN, BK_BYTES>::kA;
   constexpr int kB = IgemmSmem<BN, BK_BYTES>::kB;
   // bf16x3 stages hold A_hi, A_lo, B_hi, B_lo.
@@ -224,12 +271,19 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
                                                    : 512;
   static_assert(kTmemCols >= kAccCols, "TMEM columns");
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
+  constexpr int kColsPerWarp = EPI_WARPS == 8 ? BN / 2 : BN;
+  constexpr int kOutWarpBytes = 32 * kColsPerWarp;
+  constexpr uint32_t kOutSwizzleMask = kColsPerWarp >= 128 ? 7u : kColsPerWarp == 64 ? 3u : 1u;
+  constexpr int kEpiSmemBytes = EPI_WARPS * (kOutWarpBytes + kColsPerWarp * 8);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stages + STAGES * kStageBytes);
+  // Epilogue staging (int8 outputs): per warp 32 rows x kColsPerWarp bytes,
+  // swizzled like the TMA store map, then per-warp bias / multiplier copies.
+  uint8_t* stage_out = stages + STAGES * kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + kEpiSmemBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;  // [2]
   uint64_t* acce_bar = accf_bar + 2;        // [2]
@@ -246,6 +300,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_y);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
@@ -364,48 +419,115 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     const int ew = warp - 2;             // 0 .. EPI_WARPS-1
     const int quarter = warp & 3;        // TMEM lane quarter this warp may access
     const int half = ew / 4;             // column half (EPI_WARPS == 8)
-    constexpr int kColsPerWarp = EPI_WARPS == 8 ? BN / 2 : BN;
+    // Per-warp bias / multiplier copy for its kColsPerWarp columns.
+    int32_t* s_bias = reinterpret_cast<int32_t*>(stage_out + EPI_WARPS * kOutWarpBytes) +
+                      ew * kColsPerWarp * 2;
+    float* s_mult = reinterpret_cast<float*>(s_bias + kColsPerWarp);
+    uint8_t* s_out = stage_out + ew * kOutWarpBytes;  // 32 rows x kColsPerWarp bytes, swizzled
+    const bool tma_out = KIND_I8 && (args.out_mode == kOutU8 || args.out_mode == kOutS8);
+    const bool out_signed = args.out_mode == kOutS8;
+    const int32_t qmin = args.lo + args.zp_y, qmax = args.hi + args.zp_y;
+    const bool fast_requant = args.zp_y == 0 && qmin == (out_signed ? -128 : 0) &&
+                              qmax == (out_signed ? 127 : 255);
+    int loaded_n_tile = -1;
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       const int n_tile = tile % args.n_tiles;
       const int m_tile = tile / args.n_tiles;
-      if (!mbar_wait(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
-      tc_fence_after();
-      const int64_t pixel = static_cast<int64_t>(m_tile) * 128 + quarter * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int cc = 0; cc < kColsPerWarp; cc += 32) {
-        const int col = half * kColsPerWarp + cc;
-        uint32_t acc[32];
-        tmem_ld_32x32b_x32(t_row + col, acc);
-        tmem_ld_wait();
-        const int32_t col0 = n_tile * BN + col;
-        int32_t sb[32];
-        float sm[32];
-        float sbf[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int32_t ch = col0 + j;
+      if (n_tile != loaded_n_tile) {
+        // (re)load this warp's per-channel epilogue constants
+        __syncwarp();
+        for (int j = lane; j < kColsPerWarp; j += 32) {
+          const int32_t ch = n_tile * BN + half * kColsPerWarp + j;
           const bool in = ch < args.m;
           if constexpr (KIND_I8) {
-            sb[j] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
-            sm[j] = (in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f;
-            sbf[j] = 0.0f;
+            s_bias[j] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
+            s_mult[j] = (in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f;
           } else {
-            sb[j] = 0;
-            sm[j] = 0.0f;
-            sbf[j] = (in && args.bias_f32 != nullptr) ? __ldg(args.bias_f32 + ch) : 0.0f;
+            s_bias[j] = __float_as_int((in && args.bias_f32 != nullptr) ? __ldg(args.bias_f32 + ch)
+                                                                        : 0.0f);
+            s_mult[j] = 0.0f;
           }
         }
-        epilogue_chunk<!KIND_I8>(args, acc, pixel, col0, sb, sm, sbf);
+        loaded_n_tile = n_tile;
+        __syncwarp();
       }
-      // This warp has read its part of the accumulator buffer: hand it back.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce_bar[buf]);
+      if (!mbar_wait(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int64_t row0 = static_cast<int64_t>(m_tile) * 128 + quarter * 32;
+      const int64_t pixel = row0 + lane;
+      const int32_t wcol0 = n_tile * BN + half * kColsPerWarp;  // first output channel of this warp
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN +
+                             half * kColsPerWarp;
+      if (tma_out) {
+        // The staging buffer is free once the previous tile's store has read it.
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
+#pragma unroll 1
+      for (int cc = 0; cc < kColsPerWarp; cc += 32) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(t_row + cc, acc);
+        tmem_ld_wait();
+        if (cc + 32 >= kColsPerWarp) {
+          // Last read of this accumulator buffer by this warp: hand it back so
+          // the MMA warp can start the next tile while we finish the epilogue.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce_bar[buf]);
+        }
+        if (tma_out) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int4 b4 = *reinterpret_cast<const int4*>(s_bias + cc + 4 * q);
+            const float4 m4 = *reinterpret_cast<const float4*>(s_mult + cc + 4 * q);
+            if (fast_requant) {
+              packed[q] = out_signed ? requant_pack4<true, true>(acc + 4 * q, b4, m4, 0, 0, 0)
+                                     : requant_pack4<true, false>(acc + 4 * q, b4, m4, 0, 0, 0);
+            } else {
+              packed[q] = requant_pack4<false, false>(acc + 4 * q, b4, m4, args.zp_y, qmin, qmax);
+            }
+          }
+          // two 16-byte chunks of this lane's row, at swizzled positions
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t off = lane * kColsPerWarp + cc + 16 * h;
+            const uint32_t phys = off ^ (((off >> 7) & kOutSwizzleMask) << 4);
+            *reinterpret_cast<uint4*>(s_out + phys) =
+                make_uint4(packed[4 * h], packed[4 * h + 1], packed[4 * h + 2], packed[4 * h + 3]);
+          }
+        } else {
+          int32_t sb[32];
+          float sm[32];
+          float sbf[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if constexpr (KIND_I8) {
+              sb[j] = s_bias[cc + j];
+              sm[j] = s_mult[cc + j];
+              sbf[j] = 0.0f;
+            } else {
+              sb[j] = 0;
+              sm[j] = 0.0f;
+              sbf[j] = __int_as_float(s_bias[cc + j]);
+            }
+          }
+          epilogue_chunk<!KIND_I8>(args, acc, pixel, wcol0 + cc, sb, sm, sbf);
+        }
+      }
+      if (tma_out) {
+        fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the TMA unit
+        __syncwarp();
+        if (lane == 0 && row0 < args.m_total && wcol0 < args.y_ld) {
+          tma_store_2d(&tmap_y, s_out, wcol0, static_cast<int32_t>(row0));
+          bulk_commit_group();
+        }
+      }
     }
+    if (lane == 0) bulk_wait_group0();
   }
 
   tc_fence_before();

@@ -85,12 +85,19 @@ int resolve(const ie_conv2d_desc* d, int64_t bias_len, ie_conv2d_shape* out) {
 
 // --------------------------------------------------------- tile choices
 
+constexpr int epi_cols_per_warp(int bn);
+constexpr int igemm_stages(int bn, int bkb, bool i8);
+
+// Widest channel block with a kernel variant deep enough (>= 2 stages).
+int igemm_max_bk(int bn, bool i8);
+
 // Channel block (bytes of K per tap per stage) that pads the channel count
 // least; ties go to the wider block.
-int choose_bk_bytes(int64_t c_store, int elem_bytes, bool must_divide) {
+int choose_bk_bytes(int64_t c_store, int elem_bytes, bool must_divide, int max_bk = 128) {
   int best = 0;
   int64_t best_cost = INT64_MAX;
   for (int bk : {128, 64, 32}) {
+    if (bk > max_bk) continue;
     const int64_t elems = bk / elem_bytes;
     if (must_divide && c_store % elems != 0) continue;
     const int64_t cost = round_up(c_store, elems);
@@ -117,16 +124,28 @@ int choose_bn(int64_t m) {
 
 // ----------------------------------------------------- igemm launching
 
+// Columns of the output tile one epilogue warp stores (32 rows each).
+constexpr int epi_cols_per_warp(int bn) { return bn >= 256 ? bn / 2 : bn; }
+
+// Pipeline depth that fits next to the epilogue staging in 227 KB.
+constexpr int igemm_stages(int bn, int bkb, bool i8) {
+  const int stage = (i8 ? 1 : 2) * (128 + bn) * bkb;
+  const int epi = (bn >= 256 ? 8 : 4) * (32 * epi_cols_per_warp(bn) + epi_cols_per_warp(bn) * 8);
+  const int raw = (227 * 1024 - epi - 1024 - 512) / stage;
+  return raw > 8 ? 8 : raw;
+}
+
 template <int BN, int BKB, bool I8, bool AS>
-int launch_igemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const IgemmArgs& args,
-                   cudaStream_t st) {
+int launch_igemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
+                   const IgemmArgs& args, cudaStream_t st) {
   constexpr int kParts = I8 ? 1 : 2;
   constexpr int kStage = kParts * (128 + BN) * BKB;
-  constexpr int kStagesRaw = (192 * 1024) / kStage;
-  constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static_assert(kStages >= 2, "pipeline depth");
   constexpr int kEpi = BN >= 256 ? 8 : 4;
-  constexpr int kSmem = kStages * kStage + 1024 + 256;
+  constexpr int kCols = epi_cols_per_warp(BN);
+  constexpr int kEpiSmem = kEpi * (32 * kCols + kCols * 8);
+  constexpr int kStages = igemm_stages(BN, BKB, I8);
+  static_assert(kStages >= 2, "pipeline depth");
+  constexpr int kSmem = kStages * kStage + kEpiSmem + 1024 + 256;
   auto kern = conv_igemm_kernel<BN, BKB, kStages, kEpi, I8, AS>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -138,16 +157,19 @@ int launch_igemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const IgemmArgs
   }
   const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
-  kern<<<grid, 64 + kEpi * 32, kSmem, st>>>(ta, tb, args);
+  kern<<<grid, 64 + kEpi * 32, kSmem, st>>>(ta, tb, ty, args);
   return check_launch("conv_igemm_kernel");
 }
 
-using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const IgemmArgs&, cudaStream_t);
+using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const IgemmArgs&, cudaStream_t);
 
 template <bool I8, bool AS>
 LaunchFn pick_launch(int bn, int bkb) {
-#define IE_CASE(BN_, BK_) \
-  if (bn == BN_ && bkb == BK_) return launch_igemm_t<BN_, BK_, I8, AS>;
+#define IE_CASE(BN_, BK_)                                 \
+  if constexpr (igemm_stages(BN_, BK_, I8) >= 2) {        \
+    if (bn == BN_ && bkb == BK_) return launch_igemm_t<BN_, BK_, I8, AS>; \
+  }
   IE_CASE(64, 32) IE_CASE(64, 64) IE_CASE(64, 128)
   IE_CASE(128, 32) IE_CASE(128, 64) IE_CASE(128, 128)
   IE_CASE(256, 32) IE_CASE(256, 64) IE_CASE(256, 128)
@@ -155,9 +177,16 @@ LaunchFn pick_launch(int bn, int bkb) {
   return nullptr;
 }
 
+int igemm_max_bk(int bn, bool i8) {
+  for (int bk : {128, 64, 32}) {
+    if (igemm_stages(bn, bk, i8) >= 2) return bk;
+  }
+  return 32;
+}
+
 struct IgemmSetup {
   IgemmArgs args;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ty;
   int bn, bkb;
 };
 
@@ -166,11 +195,11 @@ struct IgemmSetup {
 int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
                 int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out) {
   const bool i8 = elem_bytes == 1;
-  const int bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8);
+  const int bn = choose_bn(d->m);
+  const int bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(bn, i8));
   if (bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
                             static_cast<long long>(x_c_store));
   const int64_t bk_elems = bkb / elem_bytes;
-  const int bn = choose_bn(d->m);
   const int64_t cblocks = ceil_div(x_c_store, bk_elems);
   const int64_t taps = d->kh * d->kw;
   const int64_t ck = cblocks * bk_elems;
@@ -232,7 +261,8 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
 // Packed-weight geometry for a dense convolution on x_c_store input channels.
 void packed_geom(const ie_conv2d_desc* d, int elem_bytes, int64_t* taps, int64_t* ck) {
   const int64_t c_store = round_up(d->c, 16);
-  const int bkb = choose_bk_bytes(c_store, elem_bytes, elem_bytes != 1);
+  const int bkb = choose_bk_bytes(c_store, elem_bytes, elem_bytes != 1,
+                                  igemm_max_bk(choose_bn(d->m), elem_bytes == 1));
   const int64_t bk_elems = bkb / elem_bytes;
   *taps = d->kh * d->kw;
   *ck = ceil_div(c_store, bk_elems) * bk_elems;
@@ -284,10 +314,19 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   a.out_mode = out_mode == kOutS32 ? kOutS32 : (q->y_signed ? kOutS8 : kOutU8);
   a.y = y;
   a.y_ld = round_up(d->m, 16);
+  if (a.out_mode == kOutU8 || a.out_mode == kOutS8) {
+    // the epilogue stores 32-row x (64 or 128)-channel boxes through TMA
+    if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld,
+                        epi_cols_per_warp(su.bn), 32)) != IE_OK) {
+      return rc;
+    }
+  } else {
+    su.ty = su.tb;  // not read by the kernel in this output mode
+  }
   LaunchFn fn = q->x_signed ? pick_launch<true, true>(su.bn, su.bkb)
                             : pick_launch<true, false>(su.bn, su.bkb);
   if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
-  return fn(su.ta, su.tb, a, as_stream(stream));
+  return fn(su.ta, su.tb, su.ty, a, as_stream(stream));
 }
 
 int grid_1d(int64_t total, int block) {
@@ -491,8 +530,10 @@ int ie_cuda_q8_stem_pack_input(const void* x_nchw, void* x_packed, int64_t n, in
   if (rc != IE_OK) return rc;
   if (x_nchw == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
   if ((rc = check_ptr(x_packed, "x_packed", 16)) != IE_OK) return rc;
-  const int64_t total = n * (h / 2) * (w / 2) * 4;
-  stem_pack_s2d_u8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+  const int64_t blocks = n * (h / 2);
+  const size_t smem = static_cast<size_t>(c * 2 * w);
+  if (blocks > INT32_MAX || smem > 48 * 1024) return fail(IE_UNSUPPORTED, "stem input too large");
+  stem_pack_s2d_u8<<<static_cast<unsigned>(blocks), 256, smem, as_stream(stream)>>>(
       static_cast<const uint8_t*>(x_nchw), static_cast<uint8_t*>(x_packed),
       static_cast<int32_t>(n), static_cast<int32_t>(c), static_cast<int32_t>(h),
       static_cast<int32_t>(w), static_cast<uint8_t>(xor_mask & 0xFF));
@@ -606,9 +647,10 @@ int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x
     default:
       return fail(IE_INVALID_ARGUMENT, "bad output format");
   }
+  su.ty = su.tb;  // fp32 outputs use direct stores; the map is not read
   LaunchFn fn = pick_launch<false, false>(su.bn, su.bkb);
   if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
-  return fn(su.ta, su.tb, a, as_stream(stream));
+  return fn(su.ta, su.tb, su.ty, a, as_stream(stream));
 }
 
 size_t ie_cuda_conv2d_f32_workspace_bytes(const ie_conv2d_desc* desc) {

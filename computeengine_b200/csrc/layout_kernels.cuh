@@ -138,34 +138,51 @@ namespace ie_cuda {
 // same implicit-GEMM kernel as every other layer:
 //   out[i][j][((b*2+dy)*2+dx)*c + ch] = x[ch][2i+dy][2(j+b-2)+dx]   (0 if j+b-2
 //   is outside [0, w/2)), i in [0, h/2), j in [0, w/2)
-__global__ void stem_pack_s2d_u8(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
-                                 int32_t n, int32_t c, int32_t h, int32_t w, uint8_t xor_mask) {
+// One block per (image, output row i): input rows 2i and 2i+1 of every
+// channel are staged in shared memory with coalesced loads, then the block
+// writes the output row (w/2 pixels x 64 bytes) with coalesced 16-byte stores.
+__global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restrict__ x,
+                                                        uint8_t* __restrict__ y, int32_t n,
+                                                        int32_t c, int32_t h, int32_t w,
+                                                        uint8_t xor_mask) {
+  extern __shared__ uint8_t rows[];  // [c][2][w]
   const int32_t ho = h / 2, wo = w / 2;
-  const int64_t total = static_cast<int64_t>(n) * ho * wo * 4;
-  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (idx >= total) return;
-  const int32_t g = static_cast<int32_t>(idx & 3);
-  const int64_t pix = idx >> 2;
-  const int32_t j = static_cast<int32_t>(pix % wo);
-  const int32_t i = static_cast<int32_t>((pix / wo) % ho);
-  const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(wo) * ho));
-  const uint8_t* xi = x + static_cast<int64_t>(img) * c * h * w;
-  uint32_t out[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int32_t chan = g * 16 + k;
-    if (chan < 16 * c) {
-      const int32_t cc = chan % c;
-      const int32_t rest = chan / c;  // (b*2 + dy)*2 + dx
-      const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
-      const int32_t jj = j + b - 2;
-      if (jj >= 0 && jj < wo) {
-        const uint8_t v = xi[(static_cast<int64_t>(cc) * h + 2 * i + dy) * w + 2 * jj + dx] ^ xor_mask;
-        out[k >> 2] |= static_cast<uint32_t>(v) << (8 * (k & 3));
+  const int32_t i = blockIdx.x % ho;
+  const int64_t img = blockIdx.x / ho;
+  const uint8_t* xi = x + img * c * h * w;
+  const int32_t span = 2 * w;  // two consecutive input rows are contiguous in NCHW
+  for (int cc = 0; cc < c; ++cc) {
+    const uint8_t* src = xi + (static_cast<int64_t>(cc) * h + 2 * i) * w;
+    uint8_t* dst = rows + cc * span;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (span & 15) == 0) {
+      for (int t = threadIdx.x; t < span / 16; t += blockDim.x) {
+        reinterpret_cast<uint4*>(dst)[t] = __ldg(reinterpret_cast<const uint4*>(src) + t);
       }
+    } else {
+      for (int t = threadIdx.x; t < span; t += blockDim.x) dst[t] = src[t];
     }
   }
-  reinterpret_cast<uint4*>(y)[idx] = make_uint4(out[0], out[1], out[2], out[3]);
+  __syncthreads();
+  uint4* out = reinterpret_cast<uint4*>(y + ((img * ho + i) * static_cast<int64_t>(wo)) * 64);
+  for (int t = threadIdx.x; t < wo * 4; t += blockDim.x) {
+    const int32_t j = t >> 2, g = t & 3;
+    uint32_t v[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int32_t chan = g * 16 + k;
+      if (chan < 16 * c) {
+        const int32_t cc = chan % c;
+        const int32_t rest = chan / c;  // (b*2 + dy)*2 + dx
+        const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
+        const int32_t jj = j + b - 2;
+        if (jj >= 0 && jj < wo) {
+          const uint32_t byte = rows[cc * span + dy * w + 2 * jj + dx] ^ xor_mask;
+          v[k >> 2] |= byte << (8 * (k & 3));
+        }
+      }
+    }
+    out[t] = make_uint4(v[0], v[1], v[2], v[3]);
+  }
 }
 
 // Weights of the same stem, [m, c, 7, 7] int8 -> the 4x1 layer's weights in

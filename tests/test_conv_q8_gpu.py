@@ -69,3 +69,41 @@ def test_relu6_clamp_and_unsigned_input(oracle):
     want = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, zp_y, qmax, pads=(1, 1, 1, 1))
     np.testing.assert_array_equal(got, want)
     assert want.min() == zp_y and want.max() == qmax
+
+
+@pytest.mark.parametrize("y_signed,zp_y,qmin,qmax", [(False, 0, 0, 255), (True, 0, -128, 127),
+                                                      (False, 10, 10, 200), (True, -5, -100, 90)])
+def test_requantize_ties_and_saturation(oracle, y_signed, zp_y, qmin, qmax):
+    """Multipliers 2^-k and 3*2^-k make many requantized values exact .5 ties
+    (round half away from zero), others saturate; the epilogue's fast
+    saturating path and the general clamp path must both match the oracle."""
+    import torch
+    from computeengine_b200 import _lib as L
+    from tests.qconv import desc_for
+    rng = np.random.default_rng(11)
+    n, c, h, w, m = 2, 32, 9, 9, 64
+    x = rng.integers(-60, 61, (n, c, h, w)).astype(np.int8)
+    wq = rng.integers(-127, 128, (m, c, 1, 1)).astype(np.int8)
+    bias = rng.integers(-3000, 3000, m).astype(np.int32)
+    cands = [0.5, 0.25, 0.125, 1.5, 0.75, 0.375, 2.0 ** -10, 3 * 2.0 ** -9, 0.0009765625, 0.01]
+    mult = np.array([cands[i % len(cands)] for i in range(m)], np.float32)
+    d = desc_for(L, n, c, h, w, m, 1, 1)
+    stream = torch.cuda.current_stream().cuda_stream
+    x_nhwc = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 3, 1))).cuda()
+    packed = torch.zeros(int(L.lib.ie_cuda_q8_packed_weight_bytes(d)), dtype=torch.uint8, device="cuda")
+    L.check(L.lib.ie_cuda_q8_pack_weights(d, torch.from_numpy(wq).cuda().data_ptr(), packed.data_ptr(), stream))
+    q = L.Q8Params()
+    q.x_signed, q.zp_x, q.y_signed, q.zp_y, q.qmin, q.qmax = 1, 0, int(y_signed), zp_y, qmin, qmax
+    y = torch.zeros((n, h, w, m), dtype=torch.uint8, device="cuda")
+    bd, md = torch.from_numpy(bias).cuda(), torch.from_numpy(mult).cuda()
+    L.check(L.lib.ie_cuda_conv2d_q8(d, q, x_nhwc.data_ptr(), packed.data_ptr(), bd.data_ptr(),
+                                    md.data_ptr(), y.data_ptr(), stream))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().view(np.int8 if y_signed else np.uint8).transpose(0, 3, 1, 2)
+    want, acc = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, qmin, qmax, y_signed=y_signed,
+                                 want_acc=True)
+    np.testing.assert_array_equal(got, want)
+    v = (acc + bias.reshape(1, -1, 1, 1)).astype(np.float32) * mult.reshape(1, -1, 1, 1)
+    ties = np.mean(np.abs(v - np.trunc(v)) == 0.5)
+    assert ties > 0.05, ties
+    assert (want == qmin).any() and (want == qmax).any()

@@ -1,0 +1,118 @@
+"""The CPU oracle, pinned before it is trusted:
+* fp32: against the reference's own golden vectors (PyTorch float32,
+  tests/data/traditional_reference.h in the reference) and against the
+  reference's Conv2DOp compiled from its sources, on the geometry the
+  reference tests (pads, SAME_UPPER / SAME_LOWER, dilation, groups);
+* int8 accumulation: against the reference Conv2DOp on integer-valued data
+  (exact in fp32 while partial sums stay below 2^24);
+* int8 requantize: against an independent float64 restatement, on ties and
+  saturation edges (the reference has no int8 conv, so this rule is pinned
+  only by its own definition)."""
+import numpy as np
+import pytest
+
+
+def test_golden_conv_and_depthwise(oracle, golden):
+    y = oracle.conv2d_f32(golden["kConvInput"], golden["kConvWeight"], golden["kConvBias"],
+                          pads=(1, 1, 1, 1))
+    np.testing.assert_allclose(y, golden["kConvExpected"], atol=1e-5, rtol=0)
+    y = oracle.conv2d_f32(golden["kConvInput"], golden["kConvWeight"], None, pads=(1, 1, 1, 1))
+    np.testing.assert_allclose(y, golden["kConvExpected"] - golden["kConvBias"].reshape(1, 3, 1, 1),
+                               atol=1e-5, rtol=0)
+    y = oracle.conv2d_f32(golden["kConvInput"], golden["kConvWeight"], golden["kConvBias"],
+                          auto_pad="SAME_UPPER")
+    np.testing.assert_allclose(y, golden["kConvExpected"], atol=1e-5, rtol=0)
+    y = oracle.conv2d_f32(golden["kDepthwiseInput"], golden["kDepthwiseWeight"],
+                          golden["kDepthwiseBias"], group=2, depthwise=True)
+    np.testing.assert_allclose(y, golden["kDepthwiseExpected"], atol=1e-5, rtol=0)
+
+
+def test_reference_known_answers(oracle):
+    # grouped manual values (traditional_ops_test.cpp GroupedMatchesManualValues)
+    x = np.arange(1, 9, dtype=np.float32).reshape(1, 2, 2, 2)
+    w = np.array([2, 3], np.float32).reshape(2, 1, 1, 1)
+    y = oracle.conv2d_f32(x, w, None, group=2)
+    np.testing.assert_array_equal(y.ravel(), [2, 4, 6, 8, 15, 18, 21, 24])
+    # SAME_UPPER / SAME_LOWER direction and dilation (Conv2DAutoPadDirectionAndDilation)
+    x = np.arange(1, 17, dtype=np.float32).reshape(1, 1, 4, 4)
+    ones = np.ones((1, 1, 3, 3), np.float32)
+    up = oracle.conv2d_f32(x, ones, None, strides=(2, 2), auto_pad="SAME_UPPER")
+    lo = oracle.conv2d_f32(x, ones, None, strides=(2, 2), auto_pad="SAME_LOWER")
+    assert up.shape == lo.shape == (1, 1, 2, 2)
+    assert up.ravel()[0] == 1 + 2 + 3 + 5 + 6 + 7 + 9 + 10 + 11
+    assert lo.ravel()[3] == 6 + 7 + 8 + 10 + 11 + 12 + 14 + 15 + 16
+    x3 = np.arange(1, 10, dtype=np.float32).reshape(1, 1, 3, 3)
+    y = oracle.conv2d_f32(x3, np.ones((1, 1, 2, 2), np.float32), None, dilations=(2, 2))
+    assert y.shape == (1, 1, 1, 1) and y.ravel()[0] == 1 + 3 + 7 + 9
+
+
+def test_error_codes_match_reference(oracle):
+    from oracle.oracle import INVALID_ARGUMENT, OracleError
+    with pytest.raises(OracleError) as e:
+        oracle.resolve((1, 2, 5, 5), (3, 2, 3, 3), group=4)
+    assert e.value.code == INVALID_ARGUMENT
+    with pytest.raises(OracleError) as e:
+        oracle.resolve((1, 2, 3, 3), (2, 1, 2, 2), group=1, depthwise=True)
+    assert e.value.code == INVALID_ARGUMENT
+
+
+GEOMETRIES = [
+    dict(x=(2, 3, 9, 11), w=(4, 3, 3, 3), pads=(1, 1, 1, 1)),
+    dict(x=(1, 4, 8, 8), w=(6, 2, 3, 3), group=2, strides=(2, 2), pads=(0, 1, 1, 0)),
+    dict(x=(1, 2, 7, 7), w=(2, 1, 3, 3), group=2, dilations=(2, 2), auto_pad="SAME_LOWER"),
+    dict(x=(1, 3, 10, 6), w=(5, 3, 2, 4), strides=(3, 1), auto_pad="SAME_UPPER"),
+    dict(x=(2, 8, 6, 6), w=(8, 1, 3, 3), group=8, pads=(1, 1, 1, 1), depthwise=True),
+]
+
+
+@pytest.mark.parametrize("g", GEOMETRIES, ids=range(len(GEOMETRIES)))
+def test_fp32_matches_reference_conv(oracle, refconv, g):
+    rng = np.random.default_rng(3)
+    x = rng.normal(size=g["x"]).astype(np.float32)
+    w = rng.normal(size=g["w"]).astype(np.float32)
+    b = rng.normal(size=g["w"][0]).astype(np.float32)
+    kw = {k: v for k, v in g.items() if k not in ("x", "w")}
+    rc, want = refconv.conv2d(x, w, b, **kw)
+    assert rc == 0
+    got = oracle.conv2d_f32(x, w, b, **kw)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("g", GEOMETRIES[:4], ids=range(4))
+def test_int8_accumulators_match_reference_conv(oracle, refconv, g):
+    """Integer-valued fp32 through the reference conv is exact below 2^24, so
+    it pins the int8 oracle's accumulation (geometry, padding = real zero)."""
+    rng = np.random.default_rng(4)
+    zp = 128
+    x = rng.integers(0, 256, g["x"]).astype(np.uint8)
+    w = rng.integers(-127, 128, g["w"]).astype(np.int8)
+    kw = {k: v for k, v in g.items() if k not in ("x", "w")}
+    rc, want = refconv.conv2d(x.astype(np.float32) - zp, w.astype(np.float32), None, **kw)
+    assert rc == 0
+    _, acc = oracle.conv2d_q8(x, w, None, np.ones(g["w"][0], np.float32), zp, 0, 0, 255,
+                              want_acc=True, **kw)
+    np.testing.assert_array_equal(acc, want.astype(np.int64))
+
+
+def _requant_f64(acc, bias, mult, zp, qmin, qmax):
+    v = np.float32(np.float32(np.int32(acc + bias)) * np.float32(mult))
+    r = np.sign(float(v)) * np.floor(abs(float(v)) + 0.5)
+    return int(min(max(r, qmin - zp), qmax - zp) + zp)
+
+
+def test_requantize_edges(oracle):
+    rng = np.random.default_rng(9)
+    cases = []
+    for m in (0.5, 0.25, 1.5, 3 * 2.0 ** -9, 0.0037, 1e-4, 7.0):
+        for acc in list(range(-20, 21)) + [2 ** 24 + 1, -(2 ** 24) - 3, 2 ** 30, -(2 ** 31) + 5]:
+            cases.append((acc, 0, m))
+    for _ in range(5000):
+        cases.append((int(rng.integers(-2 ** 26, 2 ** 26)), int(rng.integers(-5000, 5000)),
+                      float(np.float32(rng.uniform(1e-5, 0.05)))))
+    # 0.49999997 = 0.5 - 2^-25: the value naive "trunc(v + 0.5)" gets wrong
+    cases.append((1, 0, float(np.float32(0.5) - np.float32(2.0 ** -25))))
+    cases.append((-1, 0, float(np.float32(0.5) - np.float32(2.0 ** -25))))
+    for zp, lo, hi in ((0, 0, 255), (3, 3, 123), (-7, -128, 127), (100, 0, 255)):
+        for acc, b, m in cases:
+            assert oracle.requantize(acc, b, m, zp, lo, hi) == _requant_f64(acc, b, m, zp, lo, hi), \
+                (acc, b, m, zp, lo, hi)
