@@ -7,15 +7,9 @@
 
 #include <cstdint>
 
-namespace ie_cuda {
+#include "conv_igemm.cuh"
 
-__device__ __forceinline__ int32_t requant_one(int32_t acc, int32_t bias, float mult, int32_t zp,
-                                               float lo, float hi) {
-  const int32_t t = static_cast<int32_t>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(bias));
-  float r = roundf(__fmul_rn(__int2float_rn(t), mult));
-  r = fminf(fmaxf(r, lo), hi);
-  return __float2int_rz(r) + zp;
-}
+namespace ie_cuda {
 
 struct DwArgs {
   int32_t n, h, w, c_store;  // input NHWC
@@ -23,7 +17,7 @@ struct DwArgs {
   int32_t kh, kw, stride_h, stride_w, dil_h, dil_w, pad_t, pad_l;
   int32_t c;  // real channels (== m)
   int32_t x_signed, zp_x, zp_y;
-  float lo, hi;
+  int32_t qmin, qmax;
 };
 
 // One thread = one output pixel x 16 channels.  Weights packed [kh*kw][c_store].
@@ -78,8 +72,10 @@ __global__ void __launch_bounds__(256) dwconv_q8_nhwc(const uint8_t* __restrict_
     const int32_t ch = c0 + j;
     int32_t q = 0;
     if (ch < a.c) {
-      q = requant_one(acc[j], bias != nullptr ? __ldg(bias + ch) : 0, __ldg(mult + ch), a.zp_y,
-                      a.lo, a.hi);
+      // same exact rule as the implicit-GEMM epilogue (conv_igemm.cuh)
+      const int32_t t = static_cast<int32_t>(static_cast<uint32_t>(acc[j]) +
+                                             static_cast<uint32_t>(bias != nullptr ? __ldg(bias + ch) : 0));
+      q = requant_exact(t, split_multiplier(__ldg(mult + ch)), a.zp_y, a.qmin, a.qmax);
     }
     out[j >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (j & 3));
   }

@@ -90,11 +90,11 @@ inline CUtensorMapSwizzle swizzle_for(int row_bytes) {
 }
 
 // im2col descriptor over an NHWC tensor [n, h, w, c_elems] of elem_bytes-wide
-// elements.  Each load fetches 128 output pixels x box_c channels.
+// elements.  Each load fetches `pixels` output pixels x box_c channels.
 inline int encode_im2col(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                          int elem_bytes, int64_t n, int64_t h, int64_t w, int64_t c_elems,
-                         int box_c, int lower_w, int lower_h, int upper_w, int upper_h,
-                         int stride_w, int stride_h) {
+                         int box_c, int pixels, int lower_w, int lower_h, int upper_w,
+                         int upper_h, int stride_w, int stride_h) {
   const DriverFns& f = driver_fns();
   if (!f.ok) return fail(IE_RUNTIME, "cuTensorMapEncodeIm2col entry point unavailable");
   const cuuint64_t dims[4] = {static_cast<cuuint64_t>(c_elems), static_cast<cuuint64_t>(w),
@@ -107,7 +107,8 @@ inline int encode_im2col(CUtensorMap* map, const void* base, CUtensorMapDataType
   const cuuint32_t estrides[4] = {1, static_cast<cuuint32_t>(stride_w),
                                   static_cast<cuuint32_t>(stride_h), 1};
   const CUresult r = f.im2col(map, dtype, 4, const_cast<void*>(base), dims, strides, lower,
-                              upper, static_cast<cuuint32_t>(box_c), 128u, estrides,
+                              upper, static_cast<cuuint32_t>(box_c),
+                              static_cast<cuuint32_t>(pixels), estrides,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_c * elem_bytes),
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -85,12 +85,6 @@ int resolve(const ie_conv2d_desc* d, int64_t bias_len, ie_conv2d_shape* out) {
 
 // --------------------------------------------------------- tile choices
 
-constexpr int epi_cols_per_warp(int bn);
-constexpr int igemm_stages(int bn, int bkb, bool i8);
-
-// Widest channel block with a kernel variant deep enough (>= 2 stages).
-int igemm_max_bk(int bn, bool i8);
-
 // Channel block (bytes of K per tap per stage) that pads the channel count
 // least; ties go to the wider block.
 int choose_bk_bytes(int64_t c_store, int elem_bytes, bool must_divide, int max_bk = 128) {
@@ -122,54 +116,70 @@ int choose_bn(int64_t m) {
   return best;
 }
 
-// ----------------------------------------------------- igemm launching
-
-// Columns of the output tile one epilogue warp stores (32 rows each).
-constexpr int epi_cols_per_warp(int bn) { return bn >= 256 ? bn / 2 : bn; }
-
-// Pipeline depth that fits next to the epilogue staging in 227 KB.
-constexpr int igemm_stages(int bn, int bkb, bool i8) {
-  const int stage = (i8 ? 1 : 2) * (128 + bn) * bkb;
-  const int epi = (bn >= 256 ? 8 : 4) * (32 * epi_cols_per_warp(bn) + epi_cols_per_warp(bn) * 8);
-  const int raw = (227 * 1024 - epi - 1024 - 512) / stage;
-  return raw > 8 ? 8 : raw;
+// Widest channel block allowed for a tile width: the bf16x3 path keeps its
+// stages (A hi/lo + B hi/lo) small enough for a 3-deep pipeline.
+int igemm_max_bk(int bn, bool i8) {
+  if (i8) return 128;
+  return bn >= 256 ? 64 : 128;
 }
 
-template <int BN, int BKB, bool I8, bool AS>
-int launch_igemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
-                   const IgemmArgs& args, cudaStream_t st) {
-  constexpr int kParts = I8 ? 1 : 2;
-  constexpr int kStage = kParts * (128 + BN) * BKB;
-  constexpr int kEpi = BN >= 256 ? 8 : 4;
-  constexpr int kCols = epi_cols_per_warp(BN);
-  constexpr int kEpiSmem = kEpi * (32 * kCols + kCols * 8);
-  constexpr int kStages = igemm_stages(BN, BKB, I8);
-  static_assert(kStages >= 2, "pipeline depth");
-  constexpr int kSmem = kStages * kStage + kEpiSmem + 1024 + 256;
-  auto kern = conv_igemm_kernel<BN, BKB, kStages, kEpi, I8, AS>;
+constexpr int kSmemLimit = 227 * 1024;
+
+// One compiled variant of the implicit-GEMM kernel.
+struct Variant {
+  int bn, bkb, m_sub, epi;
+  bool b_res, i8, a_signed;
+};
+
+template <int BN, int BKB, int EPI, int MSUB, bool BRES, bool I8, bool AS>
+int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty,
+                   const IgemmArgs& args, int grid, cudaStream_t st) {
+  using P = IgemmPlan<BN, BKB, EPI, MSUB, BRES, I8>;
+  auto kern = conv_igemm_kernel<BN, BKB, EPI, MSUB, BRES, I8, AS>;
+  const int smem = P::bytes(args.stages, args.num_k);
+  if (smem > kSmemLimit) return fail(IE_UNSUPPORTED, "shared memory plan too large (%d)", smem);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   });
   if (attr_err != cudaSuccess) {
     return fail(IE_RUNTIME, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   }
-  const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
-  kern<<<grid, 64 + kEpi * 32, kSmem, st>>>(ta, tb, ty, args);
+  kern<<<grid, 64 + EPI * 32, smem, st>>>(ta, tb, ty, args);
   return check_launch("conv_igemm_kernel");
 }
 
 using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const IgemmArgs&, cudaStream_t);
+                         const IgemmArgs&, int, cudaStream_t);
+
+template <int BN, int BKB, bool I8, bool AS>
+LaunchFn pick_bn_bk(int m_sub, bool b_res) {
+  if constexpr (I8) {
+    if constexpr (BN <= 128) {
+      if (m_sub == 2) {
+        return b_res ? launch_variant<BN, BKB, 8, 2, true, I8, AS>
+                     : launch_variant<BN, BKB, 8, 2, false, I8, AS>;
+      }
+      return nullptr;
+    } else {
+      return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
+                   : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
+    }
+  } else {
+    if (m_sub != 1 || b_res) return nullptr;
+    if constexpr (BN >= 256 && BKB > 64) {
+      return nullptr;
+    } else {
+      return launch_variant<BN, BKB, (BN >= 256 ? 8 : 4), 1, false, I8, AS>;
+    }
+  }
+}
 
 template <bool I8, bool AS>
-LaunchFn pick_launch(int bn, int bkb) {
-#define IE_CASE(BN_, BK_)                                 \
-  if constexpr (igemm_stages(BN_, BK_, I8) >= 2) {        \
-    if (bn == BN_ && bkb == BK_) return launch_igemm_t<BN_, BK_, I8, AS>; \
-  }
+LaunchFn pick_launch(const Variant& v) {
+#define IE_CASE(BN_, BK_) \
+  if (v.bn == BN_ && v.bkb == BK_) return pick_bn_bk<BN_, BK_, I8, AS>(v.m_sub, v.b_res);
   IE_CASE(64, 32) IE_CASE(64, 64) IE_CASE(64, 128)
   IE_CASE(128, 32) IE_CASE(128, 64) IE_CASE(128, 128)
   IE_CASE(256, 32) IE_CASE(256, 64) IE_CASE(256, 128)
@@ -177,17 +187,23 @@ LaunchFn pick_launch(int bn, int bkb) {
   return nullptr;
 }
 
-int igemm_max_bk(int bn, bool i8) {
-  for (int bk : {128, 64, 32}) {
-    if (igemm_stages(bn, bk, i8) >= 2) return bk;
-  }
-  return 32;
+// Shared-memory bytes of a variant (mirrors IgemmPlan::bytes).
+int plan_bytes(const Variant& v, int stages, int num_k) {
+  const int parts = v.i8 ? 1 : 2;
+  const int rows = 128 * v.m_sub;
+  const int ka = rows * v.bkb, kb = v.bn * v.bkb;
+  const int stage = parts * (ka + (v.b_res ? 0 : kb));
+  const int warp_cols = (v.m_sub == 1 && v.epi == 8) ? v.bn / 2 : v.bn;
+  const int epi = v.epi * (32 * warp_cols + warp_cols * 20);
+  const int bars = 8 * (2 * kMaxStages + 6) + 32;
+  return 1024 + stages * stage + (v.b_res ? parts * num_k * kb : 0) + epi + bars;
 }
 
 struct IgemmSetup {
   IgemmArgs args;
   CUtensorMap ta, tb, ty;
-  int bn, bkb;
+  Variant v;
+  int grid;
 };
 
 // Shared set-up of the implicit GEMM for both element kinds.
@@ -195,24 +211,44 @@ struct IgemmSetup {
 int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
                 int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out) {
   const bool i8 = elem_bytes == 1;
-  const int bn = choose_bn(d->m);
-  const int bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(bn, i8));
-  if (bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
-                            static_cast<long long>(x_c_store));
-  const int64_t bk_elems = bkb / elem_bytes;
+  Variant& v = out->v;
+  v.i8 = i8;
+  v.bn = choose_bn(d->m);
+  v.bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(v.bn, i8));
+  if (v.bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
+                              static_cast<long long>(x_c_store));
+  v.m_sub = (i8 && v.bn <= 128) ? 2 : 1;
+  v.epi = (v.m_sub == 2 || v.bn >= 256) ? 8 : 4;
+  const int64_t bk_elems = v.bkb / elem_bytes;
   const int64_t cblocks = ceil_div(x_c_store, bk_elems);
   const int64_t taps = d->kh * d->kw;
   const int64_t ck = cblocks * bk_elems;
+  const int64_t num_k = taps * cblocks;
   const int64_t m_total = d->n * s.out_h * s.out_w;
-  if (m_total > (int64_t{1} << 40) || d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX) {
+  if (m_total > (int64_t{1} << 40) || d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX ||
+      num_k > (1 << 20)) {
     return fail(IE_UNSUPPORTED, "tensor too large");
+  }
+  // Weights resident in shared memory when the CTA's slice fits beside a
+  // pipeline of at least 4 activation stages.
+  v.b_res = false;
+  if (i8) {
+    v.b_res = true;
+    if (plan_bytes(v, 4, static_cast<int>(num_k)) > kSmemLimit) v.b_res = false;
+  }
+  int stages = kMaxStages;
+  while (stages > 2 && plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) --stages;
+  if (plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) {
+    return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
   }
   // TMA im2col corner limits for 4D tensors: [-128, 127]; offsets < 256.
   const int64_t lower_w = -s.pad_left, lower_h = -s.pad_top;
   const int64_t upper_w = s.pad_right - (d->kw - 1) * d->dil_w;
   const int64_t upper_h = s.pad_bottom - (d->kh - 1) * d->dil_h;
-  for (int64_t v : {lower_w, lower_h, upper_w, upper_h}) {
-    if (v < -128 || v > 127) return fail(IE_UNSUPPORTED, "padding / kernel extent too large for TMA im2col");
+  for (int64_t val : {lower_w, lower_h, upper_w, upper_h}) {
+    if (val < -128 || val > 127) {
+      return fail(IE_UNSUPPORTED, "padding / kernel extent too large for TMA im2col");
+    }
   }
   if ((d->kw - 1) * d->dil_w > 255 || (d->kh - 1) * d->dil_h > 255 || d->stride_h > 8 ||
       d->stride_w > 8) {
@@ -221,13 +257,13 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t a_chan = i8 ? x_c_store : 2 * x_c_store;
   int rc = encode_im2col(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
-                         static_cast<int>(bk_elems), static_cast<int>(lower_w),
+                         static_cast<int>(bk_elems), 128 * v.m_sub, static_cast<int>(lower_w),
                          static_cast<int>(lower_h), static_cast<int>(upper_w),
                          static_cast<int>(upper_h), static_cast<int>(d->stride_w),
                          static_cast<int>(d->stride_h));
   if (rc != IE_OK) return rc;
   const int64_t b_cols = taps * ck * (i8 ? 1 : 2);
-  rc = encode_2d(&out->tb, packed, dt, elem_bytes, d->m, b_cols, static_cast<int>(bk_elems), bn);
+  rc = encode_2d(&out->tb, packed, dt, elem_bytes, d->m, b_cols, static_cast<int>(bk_elems), v.bn);
   if (rc != IE_OK) return rc;
 
   IgemmArgs& a = out->args;
@@ -248,13 +284,21 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   a.pad_t = static_cast<int32_t>(s.pad_top);
   a.pad_l = static_cast<int32_t>(s.pad_left);
   a.cblocks = static_cast<int32_t>(cblocks);
-  a.num_k = static_cast<int32_t>(taps * cblocks);
+  a.num_k = static_cast<int32_t>(num_k);
   a.k_per_tap = static_cast<int32_t>(ck);
+  a.stages = stages;
   a.m_total = m_total;
-  a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128));
-  a.n_tiles = static_cast<int32_t>(ceil_div(d->m, bn));
-  out->bn = bn;
-  out->bkb = bkb;
+  a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128 * v.m_sub));
+  a.n_tiles = static_cast<int32_t>(ceil_div(d->m, v.bn));
+  const int sms = num_sms();
+  if (v.b_res) {
+    // each CTA keeps one n_tile: the grid is a multiple of n_tiles
+    const int per_n = static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>(a.m_tiles, std::max(1, sms / a.n_tiles))));
+    out->grid = per_n * a.n_tiles;
+  } else {
+    out->grid = static_cast<int>(std::min<int64_t>(int64_t{a.m_tiles} * a.n_tiles, sms));
+  }
   return IE_OK;
 }
 
@@ -279,6 +323,16 @@ int check_ptr(const void* p, const char* what, size_t align) {
     return fail(IE_INVALID_ARGUMENT, "%s must be %zu-byte aligned", what, align);
   }
   return IE_OK;
+}
+
+int launch_setup(IgemmSetup& su, bool a_signed, cudaStream_t st) {
+  LaunchFn fn = su.v.i8 ? (a_signed ? pick_launch<true, true>(su.v) : pick_launch<true, false>(su.v))
+                        : pick_launch<false, false>(su.v);
+  if (fn == nullptr) {
+    return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d m_sub=%d resident=%d", su.v.bn,
+                su.v.bkb, su.v.m_sub, static_cast<int>(su.v.b_res));
+  }
+  return fn(su.ta, su.tb, su.ty, su.args, su.grid, st);
 }
 
 int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const void* packed,
@@ -309,24 +363,22 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   a.bias_i32 = bias;
   a.mult = mult;
   a.zp_y = q->zp_y;
-  a.lo = q->qmin - q->zp_y;
-  a.hi = q->qmax - q->zp_y;
+  a.qmin = q->qmin;
+  a.qmax = q->qmax;
   a.out_mode = out_mode == kOutS32 ? kOutS32 : (q->y_signed ? kOutS8 : kOutU8);
   a.y = y;
   a.y_ld = round_up(d->m, 16);
   if (a.out_mode == kOutU8 || a.out_mode == kOutS8) {
     // the epilogue stores 32-row x (64 or 128)-channel boxes through TMA
+    const int warp_cols = (su.v.m_sub == 1 && su.v.epi == 8) ? su.v.bn / 2 : su.v.bn;
     if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld,
-                        epi_cols_per_warp(su.bn), 32)) != IE_OK) {
+                        std::min(warp_cols, 128), 32)) != IE_OK) {
       return rc;
     }
   } else {
     su.ty = su.tb;  // not read by the kernel in this output mode
   }
-  LaunchFn fn = q->x_signed ? pick_launch<true, true>(su.bn, su.bkb)
-                            : pick_launch<true, false>(su.bn, su.bkb);
-  if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
-  return fn(su.ta, su.tb, su.ty, a, as_stream(stream));
+  return launch_setup(su, q->x_signed != 0, as_stream(stream));
 }
 
 int grid_1d(int64_t total, int block) {
@@ -490,8 +542,8 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
   a.x_signed = q->x_signed;
   a.zp_x = q->zp_x;
   a.zp_y = q->zp_y;
-  a.lo = static_cast<float>(q->qmin - q->zp_y);
-  a.hi = static_cast<float>(q->qmax - q->zp_y);
+  a.qmin = q->qmin;
+  a.qmax = q->qmax;
   const int64_t total = desc->n * s.out_h * s.out_w * (a.c_store / 16);
   dwconv_q8_nhwc<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
       static_cast<const uint8_t*>(x), static_cast<const int8_t*>(packed), bias, mult,
@@ -628,7 +680,8 @@ int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x
   if ((rc = setup_igemm(desc, s, 2, c_store, x_split, packed, &su)) != IE_OK) return rc;
   IgemmArgs& a = su.args;
   a.bias_f32 = bias;
-  a.act_lo = act == IE_ACT_NONE ? -INFINITY : 0.0f;
+  a.act = act != IE_ACT_NONE;
+  a.act_lo = 0.0f;
   a.act_hi = act == IE_ACT_RELU6 ? 6.0f : INFINITY;
   a.y = y;
   switch (y_format) {
@@ -648,9 +701,7 @@ int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x
       return fail(IE_INVALID_ARGUMENT, "bad output format");
   }
   su.ty = su.tb;  // fp32 outputs use direct stores; the map is not read
-  LaunchFn fn = pick_launch<false, false>(su.bn, su.bkb);
-  if (fn == nullptr) return fail(IE_UNSUPPORTED, "no kernel variant for BN=%d BK=%d", su.bn, su.bkb);
-  return fn(su.ta, su.tb, su.ty, a, as_stream(stream));
+  return launch_setup(su, false, as_stream(stream));
 }
 
 size_t ie_cuda_conv2d_f32_workspace_bytes(const ie_conv2d_desc* desc) {

@@ -73,10 +73,12 @@ typedef struct ie_conv2d_shape {
 
 /* Per-tensor quantization of one int8 convolution.
  *   acc = sum (xq - zp_x) * wq         int32, padding contributes real 0.0
- *   t   = acc + bias[m]                int32
- *   v   = (float)t * mult[m]           mult = s_x * s_w[m] / s_y, fp32
- *   r   = roundf(v)                    round half away from zero
- *   yq  = clamp(r, qmin - zp_y, qmax - zp_y) + zp_y
+ *   t   = acc + bias[m]                int32 (wrapping)
+ *   r   = round_half_away(t * mult[m]) exact: mult (fp32, = s_x * s_w[m] / s_y
+ *                                      computed in double and rounded once) is
+ *                                      the dyadic rational mant * 2^-shift, so
+ *                                      the product is taken in 64-bit integers
+ *   yq  = clamp(r + zp_y, qmin, qmax)
  * ReLU folds in as qmin = zp_y, ReLU6 as qmax = zp_y + round(6 / s_y). */
 typedef struct ie_q8_params {
   int32_t x_signed; /* activations stored as int8 (1) or uint8 (0) */

@@ -9,12 +9,13 @@
  *   src/ops/traditional/conv2d_op.cpp:13-22   ascending-t row dot product
  *   src/ops/traditional/conv2d_op.cpp:223-238 per-channel row, bias after dot
  *
- * Build flags matter for the int8 requantize: no -ffast-math and
- * -ffp-contract=off, so (float)t * mult is one IEEE round-to-nearest multiply.
+ * The int8 requantize is exact integer arithmetic (see orc_requantize), so it
+ * does not depend on floating-point build flags.
  */
 #include "conv_oracle.h"
 
 #include <math.h>
+#include <stdint.h>
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
@@ -237,16 +238,42 @@ int orc_conv2d_f32(const orc_conv_geom* g, const float* x, const float* wt,
 
 /* ------------------------------------------------------------------- int8 */
 
+/* Exact requantize: the fp32 multiplier is a dyadic rational mant * 2^-shift
+ * (mant the 24-bit significand scaled to 31 bits), so t * mult is computed
+ * exactly in 64-bit integers and rounded half away from zero once. */
+static void orc_split_multiplier(float mult, int64_t* mant, int* shift) {
+    if (mult == 0.0f || !isfinite(mult)) {
+        *mant = 0;
+        *shift = 32;
+        return;
+    }
+    int e = 0;
+    const double f = frexp((double)mult, &e);      /* mult = f * 2^e, 0.5 <= |f| < 1 */
+    *mant = (int64_t)ldexp(f, 31);                  /* exact: f has 24 significant bits */
+    *shift = 31 - e;                                /* mult = mant * 2^-shift */
+}
+
 int32_t orc_requantize(int32_t acc, int32_t bias, float mult, int32_t zp_y,
                        int32_t qmin, int32_t qmax) {
     const int32_t t = (int32_t)((uint32_t)acc + (uint32_t)bias);
-    const float v = (float)t * mult;
-    float r = roundf(v);
-    const float lo = (float)(qmin - zp_y);
-    const float hi = (float)(qmax - zp_y);
-    if (!(r >= lo)) r = lo; /* also maps NaN to lo; cannot occur for finite mult */
-    if (r > hi) r = hi;
-    return (int32_t)r + zp_y;
+    int64_t mant;
+    int shift;
+    orc_split_multiplier(mult, &mant, &shift);
+    const int64_t p = (int64_t)t * mant;            /* |p| < 2^62 */
+    int64_t r;
+    if (shift >= 63) {
+        r = 0;                                      /* |t * mult| < 1/2 */
+    } else if (shift <= 0) {
+        r = p == 0 ? 0 : (p > 0 ? INT64_C(1) << 40 : -(INT64_C(1) << 40));  /* saturates */
+    } else {
+        const int64_t half = INT64_C(1) << (shift - 1);
+        /* floor((p + half - [p < 0]) / 2^shift) = round half away from zero */
+        r = (p + half - (p < 0 ? 1 : 0)) >> shift;
+    }
+    int64_t q = r + zp_y;
+    if (q < qmin) q = qmin;
+    if (q > qmax) q = qmax;
+    return (int32_t)q;
 }
 
 typedef struct {

@@ -83,9 +83,10 @@ int orc_conv2d_f32(const orc_conv_geom* g, const float* x, const float* wt,
  *   acc[n,m,p] = sum over (c, ky, kx) of (xq - zp_x) * wq   (int32; taps that
  *                fall in the padding contribute 0, i.e. real 0.0)
  *   t          = acc + bias[m]                             (int32, wraps)
- *   v          = (float)t * mult[m]                        (one RN multiply)
- *   r          = roundf(v)                                 (half away from 0)
- *   yq         = clamp(r, qmin - zp_y, qmax - zp_y) + zp_y
+ *   r          = round_half_away_from_zero(t * mult[m])    (exact: the fp32
+ *                multiplier is mant * 2^-shift, the product is taken in
+ *                64-bit integers and rounded once)
+ *   yq         = clamp(r + zp_y, qmin, qmax)
  * x_signed selects int8 (1) or uint8 (0) storage for x; y_signed likewise for
  * y.  bias may be NULL.  acc_out (optional) receives acc before the bias. */
 int orc_conv2d_q8(const orc_conv_geom* g, const void* x, int x_signed,

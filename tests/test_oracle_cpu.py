@@ -94,10 +94,15 @@ def test_int8_accumulators_match_reference_conv(oracle, refconv, g):
     np.testing.assert_array_equal(acc, want.astype(np.int64))
 
 
-def _requant_f64(acc, bias, mult, zp, qmin, qmax):
-    v = np.float32(np.float32(np.int32(acc + bias)) * np.float32(mult))
-    r = np.sign(float(v)) * np.floor(abs(float(v)) + 0.5)
-    return int(min(max(r, qmin - zp), qmax - zp) + zp)
+def _requant_exact(acc, bias, mult, zp, qmin, qmax):
+    """Independent restatement with Python fractions: round half away from zero
+    of the exact product (int32 acc + bias) * (exact value of the fp32 mult)."""
+    from fractions import Fraction
+    t = int(np.int32(np.int64(acc) + np.int64(bias)))
+    v = Fraction(t) * Fraction(float(np.float32(mult)))
+    a = abs(v)
+    r = int(a + Fraction(1, 2)) if v >= 0 else -int(a + Fraction(1, 2))
+    return int(min(max(r + zp, qmin), qmax))
 
 
 def test_requantize_edges(oracle):
@@ -109,10 +114,16 @@ def test_requantize_edges(oracle):
     for _ in range(5000):
         cases.append((int(rng.integers(-2 ** 26, 2 ** 26)), int(rng.integers(-5000, 5000)),
                       float(np.float32(rng.uniform(1e-5, 0.05)))))
-    # 0.49999997 = 0.5 - 2^-25: the value naive "trunc(v + 0.5)" gets wrong
+    # products a hair below / at / above a tie
     cases.append((1, 0, float(np.float32(0.5) - np.float32(2.0 ** -25))))
     cases.append((-1, 0, float(np.float32(0.5) - np.float32(2.0 ** -25))))
+    cases.append((3, 0, float(np.float32(0.5))))
+    cases.append((-3, 0, float(np.float32(0.5))))
+    cases.append((2 ** 24 + 1, 0, float(np.float32(0.5))))
+    for m in (0.75, 1.0, 3.0, 2.0 ** 20, 2.0 ** 31, 2.0 ** 40, 2.0 ** -40, 2.0 ** -62):
+        for acc in (-7, -1, 0, 1, 5, 2 ** 31 - 1, -(2 ** 31)):
+            cases.append((acc, 0, m))
     for zp, lo, hi in ((0, 0, 255), (3, 3, 123), (-7, -128, 127), (100, 0, 255)):
         for acc, b, m in cases:
-            assert oracle.requantize(acc, b, m, zp, lo, hi) == _requant_f64(acc, b, m, zp, lo, hi), \
+            assert oracle.requantize(acc, b, m, zp, lo, hi) == _requant_exact(acc, b, m, zp, lo, hi), \
                 (acc, b, m, zp, lo, hi)
