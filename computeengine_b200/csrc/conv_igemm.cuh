@@ -487,8 +487,11 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     const int group = ew / 4;
     const int sub = M_SUB == 2 ? group : 0;
     const int col_lo = (M_SUB == 1 && P::kGroups == 2) ? group * kWarpCols : 0;
-    uint8_t* s_out = epi_base + ew * P::kEpiWarpBytes;  // 32 rows x kWarpCols bytes, swizzled
-    int32_t* s_bias = reinterpret_cast<int32_t*>(s_out + P::kOutWarpBytes);
+    // 32 rows x kWarpCols bytes, swizzled: all warps' buffers first so each
+    // stays aligned to the 1024-byte swizzle period, then the constants
+    uint8_t* s_out = epi_base + ew * P::kOutWarpBytes;
+    int32_t* s_bias = reinterpret_cast<int32_t*>(epi_base + EPI_WARPS * P::kOutWarpBytes +
+                                                 ew * kWarpCols * 20);
     int32_t* s_mant = s_bias + kWarpCols;
     int32_t* s_shm = s_mant + kWarpCols;
     long long* s_add = reinterpret_cast<long long*>(s_shm + kWarpCols);
