@@ -46,8 +46,6 @@ enum : unsigned int {
   kErrWaitAccEmpty = 0x103,
   kErrWaitAccFull = 0x104,
   kErrWaitWeights = 0x105,
-  kErrWaitStaged = 0x106,
-  kErrWaitStagingFree = 0x107,
 };
 
 constexpr int kMaxStages = 12;
@@ -242,7 +240,7 @@ struct IgemmPlan {
   // per warp: output staging, then bias / mant / shm32 (int32) and add (int64)
   static constexpr int kEpiWarpBytes = kOutWarpBytes + kWarpCols * 20;
   static constexpr int kEpiBytes = EPI_WARPS * kEpiWarpBytes;
-  static constexpr int kBarBytes = 8 * (2 * kMaxStages + 8) + 32;
+  static constexpr int kBarBytes = 8 * (2 * kMaxStages + 6) + 32;
   static constexpr int kAccCols = M_SUB * BN;
   static constexpr uint32_t kTmemCols = 2 * kAccCols <= 64    ? 64
                                         : 2 * kAccCols <= 128 ? 128
@@ -296,9 +294,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
   uint64_t* acce_bar = accf_bar + 2;            // [2]
   uint64_t* drain_bar = acce_bar + 2;           // [1]
   uint64_t* bres_bar = drain_bar + 1;           // [1]
-  uint64_t* staged_bar = bres_bar + 1;          // [1] epilogue warps -> store leader
-  uint64_t* sfree_bar = staged_bar + 1;         // [1] store leader -> epilogue warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfree_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* kiter_issued = tmem_slot + 2;
   uint32_t* kiter_consumed = tmem_slot + 3;
@@ -340,8 +336,6 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     }
     mbar_init(drain_bar, 1);
     mbar_init(bres_bar, 1);
-    mbar_init(staged_bar, EPI_WARPS);
-    mbar_init(sfree_bar, 1);
     *abort_flag = 0;
     *kiter_issued = 0;
     *kiter_consumed = 0;
@@ -493,13 +487,9 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     const int group = ew / 4;
     const int sub = M_SUB == 2 ? group : 0;
     const int col_lo = (M_SUB == 1 && P::kGroups == 2) ? group * kWarpCols : 0;
-    // Output staging: one [rows x kWarpCols] byte tile per column group, rows
-    // in pixel order (this warp owns 32 of them), swizzled like the TMA store
-    // map; then the per-warp constants.  The staging bases stay aligned to the
-    // 1024-byte swizzle period.
-    constexpr int kStageRows = 128 * M_SUB;
-    uint8_t* s_tile = epi_base + (M_SUB == 1 ? group : 0) * (kStageRows * kWarpCols);
-    uint8_t* s_out = s_tile + (sub * 128 + quarter * 32) * kWarpCols;
+    // 32 rows x kWarpCols bytes, swizzled: all warps' buffers first so each
+    // stays aligned to the 1024-byte swizzle period, then the constants
+    uint8_t* s_out = epi_base + ew * P::kOutWarpBytes;
     int32_t* s_bias = reinterpret_cast<int32_t*>(epi_base + EPI_WARPS * P::kOutWarpBytes +
                                                  ew * kWarpCols * 20);
     int32_t* s_mant = s_bias + kWarpCols;
@@ -537,16 +527,16 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
         loaded_n_tile = n_tile;
         __syncwarp();
       }
-      if (!mbar_wait_warp(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
+      if (!mbar_wait(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(m_tile) * P::kRows + sub * 128 + quarter * 32;
       const int64_t pixel = row0 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              buf * P::kAccCols + sub * BN + col_lo;
       if (tma_out) {
-        // The staging tile is free once the previous tile's store has read it
-        // (the store leader signals that; a fresh barrier passes parity 1).
-        if (!mbar_wait_warp(sfree_bar, (j & 1) ^ 1u, abort_flag, kErrWaitStagingFree)) break;
+        // The staging buffer is free once the previous tile's store has read it.
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
       }
 #pragma unroll 1
       for (int cc = 0; cc < kWarpCols; cc += 32) {
@@ -621,30 +611,13 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       if (tma_out) {
         fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the TMA unit
         __syncwarp();
-        if (lane == 0) mbar_arrive(staged_bar);
-        // One bulk store per column group: TMA instructions cost the same
-        // whatever their size, so the whole tile leaves in one or two.
-        int stop = 0;
-        if (ew == 0 && lane == 0) {
-          stop = mbar_wait(staged_bar, j & 1, abort_flag, kErrWaitStaged) ? 0 : 1;
-        }
-        if (ew == 0 && lane == 0 && !stop) {
-          const int64_t tile_row0 = static_cast<int64_t>(m_tile) * P::kRows;
-          for (int g = 0; g < (M_SUB == 1 ? P::kGroups : 1); ++g) {
-            const int32_t c0 = n_tile * BN + g * kWarpCols;
-            if (c0 < args.y_ld) {
-              tma_store_2d(&tmap_y, epi_base + g * (kStageRows * kWarpCols), c0,
-                           static_cast<int32_t>(tile_row0));
-            }
-          }
+        if (lane == 0 && row0 < args.m_total && wcol0 < args.y_ld) {
+          tma_store_2d(&tmap_y, s_out, wcol0, static_cast<int32_t>(row0));
           bulk_commit_group();
-          bulk_wait_group_read0();
-          mbar_arrive(sfree_bar);
         }
-        if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
       }
     }
-    if (ew == 0 && lane == 0) bulk_wait_group0();
+    if (lane == 0) bulk_wait_group0();
   }
 
   tc_fence_before();

@@ -195,7 +195,7 @@ int plan_bytes(const Variant& v, int stages, int num_k) {
   const int stage = parts * (ka + (v.b_res ? 0 : kb));
   const int warp_cols = (v.m_sub == 1 && v.epi == 8) ? v.bn / 2 : v.bn;
   const int epi = v.epi * (32 * warp_cols + warp_cols * 20);
-  const int bars = 8 * (2 * kMaxStages + 8) + 32;
+  const int bars = 8 * (2 * kMaxStages + 6) + 32;
   return 1024 + stages * stage + (v.b_res ? parts * num_k * kb : 0) + epi + bars;
 }
 
@@ -369,10 +369,10 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   a.y = y;
   a.y_ld = round_up(d->m, 16);
   if (a.out_mode == kOutU8 || a.out_mode == kOutS8) {
-    // the epilogue stores (128 * m_sub)-row x (64 or 128)-channel boxes through TMA
+    // the epilogue stores 32-row x (64 or 128)-channel boxes through TMA
     const int warp_cols = (su.v.m_sub == 1 && su.v.epi == 8) ? su.v.bn / 2 : su.v.bn;
     if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld,
-                        std::min(warp_cols, 128), 128 * su.v.m_sub)) != IE_OK) {
+                        std::min(warp_cols, 128), 32)) != IE_OK) {
       return rc;
     }
   } else {

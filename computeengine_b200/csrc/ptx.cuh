@@ -85,15 +85,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
-// Warp-uniform bounded wait: lane 0 waits, every lane gets the same answer,
-// so a timeout can never split a warp before a .sync.aligned instruction.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort_flag, unsigned int site) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, site) ? 1 : 0;
-  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
-}
-
 // ------------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -151,11 +142,6 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 // Waits until every committed bulk store has completed.
 __device__ __forceinline__ void bulk_wait_group0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-
-// Named barrier over `count` threads (multiple of 32), id 1..15.
-__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // --------------------------------------------------------------- tcgen05
