@@ -126,16 +126,18 @@ __device__ __forceinline__ int32_t requant_exact(int32_t t, RequantConst k, int3
   return static_cast<int32_t>(r);
 }
 
-// Fast path, valid when shift is in [32, 62], mant > 0 and zp_y <= qmin: the
-// results of negative products clamp to qmin anyway, so the sign correction of
-// the exact rounding can be dropped, and only the high word of the product is
-// shifted.  add = 2^(shift-1), shm32 = shift - 32.
+// Fast path.  All columns of a warp share one shift S in [32, 62]: each
+// channel's significand is aligned to it exactly (mant' = mult * 2^S, an
+// integer because mant carries 7 spare low bits and the channel's own shift
+// is within 7 of S).  The rounding half and the zero point fold into one
+// warp-uniform addend C = 2^(S-1) + zp * 2^S.  Valid when every mant' >= 0
+// and zp_y <= qmin: the results of negative products clamp to qmin anyway, so
+// the sign correction of the exact rounding can be dropped.  Only the high
+// word of the product is shifted.
 __device__ __forceinline__ int32_t requant_fast(int32_t t, int32_t mant, long long add,
-                                                int32_t shm32, int32_t zp, int32_t qmin,
-                                                int32_t qmax) {
+                                                int32_t shm32, int32_t qmin, int32_t qmax) {
   const long long p = static_cast<long long>(t) * mant + add;
-  int32_t r = static_cast<int32_t>(p >> 32) >> shm32;
-  r += zp;
+  const int32_t r = static_cast<int32_t>(p >> 32) >> shm32;
   return min(max(r, qmin), qmax);
 }
 
@@ -233,12 +235,13 @@ struct IgemmPlan {
   static constexpr int kA = kRows * BK_BYTES;
   static constexpr int kB = BN * BK_BYTES;  // one k-step of weights, one plane
   static constexpr int kStage = kParts * (kA + (B_RES ? 0 : kB));
-  static constexpr int kGroups = EPI_WARPS / 4;
-  // columns one epilogue warp covers (32 rows each)
-  static constexpr int kWarpCols = (M_SUB == 1 && kGroups == 2) ? BN / 2 : BN;
+  // Epilogue warps: 4 TMEM lane quarters x M_SUB sub-tiles x kColGroups
+  // column groups; each warp covers 32 rows x kWarpCols columns.
+  static constexpr int kColGroups = EPI_WARPS / (4 * M_SUB);
+  static constexpr int kWarpCols = BN / kColGroups;
   static constexpr int kOutWarpBytes = 32 * kWarpCols;
-  // per warp: output staging, then bias / mant / shm32 (int32) and add (int64)
-  static constexpr int kEpiWarpBytes = kOutWarpBytes + kWarpCols * 20;
+  // per warp: output staging, then per-column bias, significand and shift
+  static constexpr int kEpiWarpBytes = kOutWarpBytes + kWarpCols * 12;
   static constexpr int kEpiBytes = EPI_WARPS * kEpiWarpBytes;
   static constexpr int kBarBytes = 8 * (2 * kMaxStages + 6) + 32;
   static constexpr int kAccCols = M_SUB * BN;
@@ -247,7 +250,8 @@ struct IgemmPlan {
                                         : 2 * kAccCols <= 256 ? 256
                                                               : 512;
   static_assert(2 * kAccCols <= 512, "double-buffered accumulator exceeds TMEM");
-  static_assert(EPI_WARPS == 4 * M_SUB || (M_SUB == 1 && EPI_WARPS == 8), "epilogue warps");
+  static_assert(kColGroups >= 1 && EPI_WARPS == 4 * M_SUB * kColGroups, "epilogue warps");
+  static_assert(kWarpCols >= 32 && kWarpCols % 32 == 0, "epilogue columns per warp");
   // dynamic smem for `stages` pipeline stages and `num_k` resident weight steps
   static constexpr int bytes(int stages, int num_k) {
     return 1024 + stages * kStage + (B_RES ? kParts * num_k * kB : 0) + kEpiBytes + kBarBytes;
@@ -280,6 +284,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
   constexpr uint32_t kIdesc =
       KIND_I8 ? make_idesc_i8(128, BN, A_SIGNED, true) : make_idesc_bf16(128, BN);
   constexpr uint32_t kOutSwizzleMask = kWarpCols >= 128 ? 7u : kWarpCols == 64 ? 3u : 1u;
+  static_assert(kWarpCols <= 128, "TMA store box inner extent");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -484,21 +489,22 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     // ------------------------------------------------ epilogue warps
     const int ew = warp - 2;       // 0 .. EPI_WARPS-1
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int group = ew / 4;
-    const int sub = M_SUB == 2 ? group : 0;
-    const int col_lo = (M_SUB == 1 && P::kGroups == 2) ? group * kWarpCols : 0;
+    const int idx = ew / 4;
+    const int sub = idx / P::kColGroups;
+    const int col_lo = (idx % P::kColGroups) * kWarpCols;
     // 32 rows x kWarpCols bytes, swizzled: all warps' buffers first so each
-    // stays aligned to the 1024-byte swizzle period, then the constants
+    // stays aligned to the swizzle period, then the constants
     uint8_t* s_out = epi_base + ew * P::kOutWarpBytes;
     int32_t* s_bias = reinterpret_cast<int32_t*>(epi_base + EPI_WARPS * P::kOutWarpBytes +
-                                                 ew * kWarpCols * 20);
-    int32_t* s_mant = s_bias + kWarpCols;
-    int32_t* s_shm = s_mant + kWarpCols;
-    long long* s_add = reinterpret_cast<long long*>(s_shm + kWarpCols);
+                                                 ew * kWarpCols * 12);
+    int32_t* s_mant = s_bias + kWarpCols;   // fast path: aligned to the warp's shift
+    int32_t* s_shift = s_mant + kWarpCols;  // exact path: the column's own shift
     const bool tma_out = KIND_I8 && (args.out_mode == kOutU8 || args.out_mode == kOutS8);
     const bool sign_free = args.zp_y <= args.qmin;  // negative products clamp to qmin
     int loaded_n_tile = -1;
-    bool all_fast = true;  // every column of this warp can take requant_fast
+    bool all_fast = false;  // every column of this warp takes requant_fast
+    long long fast_add = 0;
+    int32_t fast_shm32 = 0;
     int m_tile, n_tile;
     for (int j = 0; tile_of(j, &m_tile, &n_tile); ++j) {
       const int buf = j & 1;
@@ -506,28 +512,55 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       const int32_t wcol0 = n_tile * BN + col_lo;  // first output channel of this warp
       if (n_tile != loaded_n_tile) {
         __syncwarp();
-        bool fast = true;
-        for (int c = lane; c < kWarpCols; c += 32) {
-          const int32_t ch = wcol0 + c;
-          const bool in = ch < args.m;
-          if constexpr (KIND_I8) {
+        if constexpr (KIND_I8) {
+          // per-column constants; the warp's common shift is the largest one
+          RequantConst rc[kWarpCols / 32];
+          int32_t smax = 0;
+          bool fast = true;
+#pragma unroll
+          for (int r = 0; r < kWarpCols / 32; ++r) {
+            const int c = lane + 32 * r;
+            const int32_t ch = wcol0 + c;
+            const bool in = ch < args.m;
             s_bias[c] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
-            const RequantConst rc =
-                split_multiplier((in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f);
-            s_mant[c] = rc.mant;
-            s_shm[c] = rc.shift - 32;
-            s_add[c] = (rc.shift >= 1 && rc.shift <= 62) ? (1ll << (rc.shift - 1)) : 0;
-            fast = fast && rc.shift >= 32 && rc.shift <= 62 && rc.mant >= 0;
-          } else {
+            rc[r] = split_multiplier((in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f);
+            if (rc[r].mant != 0) smax = max(smax, rc[r].shift);
+            fast = fast && rc[r].mant >= 0;
+          }
+          smax = __reduce_max_sync(0xFFFFFFFFu, smax);
+          if (smax < 32) fast = false;
+#pragma unroll
+          for (int r = 0; r < kWarpCols / 32; ++r) {
+            const int c = lane + 32 * r;
+            s_shift[c] = rc[r].shift;
+            const int d = smax - rc[r].shift;
+            if (rc[r].mant != 0 && (d < 0 || d > 7)) fast = false;
+          }
+          fast = fast && smax <= 62;
+          all_fast = __all_sync(0xFFFFFFFFu, fast) && sign_free;
+#pragma unroll
+          for (int r = 0; r < kWarpCols / 32; ++r) {
+            const int c = lane + 32 * r;
+            // fast: significand aligned to the common shift (exact: 7 spare
+            // low bits); exact path: the raw significand
+            s_mant[c] = (all_fast && rc[r].mant != 0) ? (rc[r].mant >> (smax - rc[r].shift))
+                                                      : rc[r].mant;
+          }
+          fast_shm32 = smax - 32;
+          fast_add = all_fast ? (1ll << (smax - 1)) + static_cast<long long>(args.zp_y) * (1ll << smax)
+                              : 0;
+        } else {
+          for (int c = lane; c < kWarpCols; c += 32) {
+            const int32_t ch = wcol0 + c;
+            const bool in = ch < args.m;
             s_bias[c] = __float_as_int((in && args.bias_f32 != nullptr)
                                            ? __ldg(args.bias_f32 + ch) : 0.0f);
           }
         }
-        all_fast = __all_sync(0xFFFFFFFFu, fast) && sign_free;
         loaded_n_tile = n_tile;
         __syncwarp();
       }
-      if (!mbar_wait(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
+      if (!mbar_wait_warp(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(m_tile) * P::kRows + sub * 128 + quarter * 32;
       const int64_t pixel = row0 + lane;
@@ -558,18 +591,15 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
             for (int q = 0; q < 8; ++q) {
               const int4 b4 = *reinterpret_cast<const int4*>(s_bias + cc + 4 * q);
               const int4 m4 = *reinterpret_cast<const int4*>(s_mant + cc + 4 * q);
-              const int4 h4 = *reinterpret_cast<const int4*>(s_shm + cc + 4 * q);
-              const longlong2 a01 = *reinterpret_cast<const longlong2*>(s_add + cc + 4 * q);
-              const longlong2 a23 = *reinterpret_cast<const longlong2*>(s_add + cc + 4 * q + 2);
               const uint32_t* ac = acc + 4 * q;
               const uint32_t q0 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[0] + static_cast<uint32_t>(b4.x)), m4.x, a01.x, h4.x, z, lo, hi));
+                  static_cast<int32_t>(ac[0] + static_cast<uint32_t>(b4.x)), m4.x, fast_add, fast_shm32, lo, hi));
               const uint32_t q1 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[1] + static_cast<uint32_t>(b4.y)), m4.y, a01.y, h4.y, z, lo, hi));
+                  static_cast<int32_t>(ac[1] + static_cast<uint32_t>(b4.y)), m4.y, fast_add, fast_shm32, lo, hi));
               const uint32_t q2 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[2] + static_cast<uint32_t>(b4.z)), m4.z, a23.x, h4.z, z, lo, hi));
+                  static_cast<int32_t>(ac[2] + static_cast<uint32_t>(b4.z)), m4.z, fast_add, fast_shm32, lo, hi));
               const uint32_t q3 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[3] + static_cast<uint32_t>(b4.w)), m4.w, a23.y, h4.w, z, lo, hi));
+                  static_cast<int32_t>(ac[3] + static_cast<uint32_t>(b4.w)), m4.w, fast_add, fast_shm32, lo, hi));
               packed[q] = pack4_bytes(q0, q1, q2, q3);
             }
           } else {
@@ -581,7 +611,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
                 const int c = cc + 4 * q + e;
                 RequantConst rc;
                 rc.mant = s_mant[c];
-                rc.shift = s_shm[c] + 32;
+                rc.shift = s_shift[c];
                 qv[e] = static_cast<uint32_t>(requant_exact(
                     static_cast<int32_t>(acc[4 * q + e] + static_cast<uint32_t>(s_bias[c])), rc,
                     z, lo, hi));

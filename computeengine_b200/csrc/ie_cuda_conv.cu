@@ -156,15 +156,17 @@ using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorM
 template <int BN, int BKB, bool I8, bool AS>
 LaunchFn pick_bn_bk(int m_sub, bool b_res) {
   if constexpr (I8) {
+    // 16 epilogue warps: the requantize epilogue is the limiter of the
+    // small-K layers, so it gets most of the SM's issue slots.
     if constexpr (BN <= 128) {
       if (m_sub == 2) {
-        return b_res ? launch_variant<BN, BKB, 8, 2, true, I8, AS>
-                     : launch_variant<BN, BKB, 8, 2, false, I8, AS>;
+        return b_res ? launch_variant<BN, BKB, 16, 2, true, I8, AS>
+                     : launch_variant<BN, BKB, 16, 2, false, I8, AS>;
       }
       return nullptr;
     } else {
-      return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
-                   : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
+      return b_res ? launch_variant<BN, BKB, 16, 1, true, I8, AS>
+                   : launch_variant<BN, BKB, 16, 1, false, I8, AS>;
     }
   } else {
     if (m_sub != 1 || b_res) return nullptr;
@@ -193,8 +195,8 @@ int plan_bytes(const Variant& v, int stages, int num_k) {
   const int rows = 128 * v.m_sub;
   const int ka = rows * v.bkb, kb = v.bn * v.bkb;
   const int stage = parts * (ka + (v.b_res ? 0 : kb));
-  const int warp_cols = (v.m_sub == 1 && v.epi == 8) ? v.bn / 2 : v.bn;
-  const int epi = v.epi * (32 * warp_cols + warp_cols * 20);
+  const int warp_cols = v.bn / (v.epi / (4 * v.m_sub));
+  const int epi = v.epi * (32 * warp_cols + warp_cols * 12);
   const int bars = 8 * (2 * kMaxStages + 6) + 32;
   return 1024 + stages * stage + (v.b_res ? parts * num_k * kb : 0) + epi + bars;
 }
@@ -218,7 +220,7 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   if (v.bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
                               static_cast<long long>(x_c_store));
   v.m_sub = (i8 && v.bn <= 128) ? 2 : 1;
-  v.epi = (v.m_sub == 2 || v.bn >= 256) ? 8 : 4;
+  v.epi = i8 ? 16 : (v.bn >= 256 ? 8 : 4);
   const int64_t bk_elems = v.bkb / elem_bytes;
   const int64_t cblocks = ceil_div(x_c_store, bk_elems);
   const int64_t taps = d->kh * d->kw;
@@ -369,10 +371,10 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   a.y = y;
   a.y_ld = round_up(d->m, 16);
   if (a.out_mode == kOutU8 || a.out_mode == kOutS8) {
-    // the epilogue stores 32-row x (64 or 128)-channel boxes through TMA
-    const int warp_cols = (su.v.m_sub == 1 && su.v.epi == 8) ? su.v.bn / 2 : su.v.bn;
+    // each epilogue warp stores a 32-row x warp_cols-channel box through TMA
+    const int warp_cols = su.v.bn / (su.v.epi / (4 * su.v.m_sub));
     if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld,
-                        std::min(warp_cols, 128), 32)) != IE_OK) {
+                        warp_cols, 32)) != IE_OK) {
       return rc;
     }
   } else {

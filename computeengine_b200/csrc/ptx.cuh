@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Warp-uniform bounded wait: lane 0 waits, every lane gets the same answer,
+// so a timeout can never split a warp before a .sync.aligned instruction.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, unsigned int site) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, site) ? 1 : 0;
+  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
+}
+
 // ------------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
