@@ -513,9 +513,11 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       if (n_tile != loaded_n_tile) {
         __syncwarp();
         if constexpr (KIND_I8) {
-          // per-column constants; the warp's common shift is the largest one
+          // per-column constants; the warp's common shift S is the smallest
+          // one (largest multiplier), every other significand shifts right by
+          // shift_c - S <= 7 bits, exactly (its 7 low bits are zero)
           RequantConst rc[kWarpCols / 32];
-          int32_t smax = 0;
+          int32_t smin = 1 << 20;
           bool fast = true;
 #pragma unroll
           for (int r = 0; r < kWarpCols / 32; ++r) {
@@ -524,28 +526,28 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
             const bool in = ch < args.m;
             s_bias[c] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
             rc[r] = split_multiplier((in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f);
-            if (rc[r].mant != 0) smax = max(smax, rc[r].shift);
+            if (rc[r].mant != 0) smin = min(smin, rc[r].shift);
             fast = fast && rc[r].mant >= 0;
           }
-          smax = __reduce_max_sync(0xFFFFFFFFu, smax);
-          if (smax < 32) fast = false;
+          smin = __reduce_min_sync(0xFFFFFFFFu, smin);
+          if (smin == (1 << 20)) smin = 32;  // all multipliers zero
+          if (smin < 32 || smin > 62) fast = false;
 #pragma unroll
           for (int r = 0; r < kWarpCols / 32; ++r) {
             const int c = lane + 32 * r;
             s_shift[c] = rc[r].shift;
-            const int d = smax - rc[r].shift;
-            if (rc[r].mant != 0 && (d < 0 || d > 7)) fast = false;
+            const int d = rc[r].shift - smin;
+            if (rc[r].mant != 0 && d > 7) fast = false;
           }
-          fast = fast && smax <= 62;
           all_fast = __all_sync(0xFFFFFFFFu, fast) && sign_free;
 #pragma unroll
           for (int r = 0; r < kWarpCols / 32; ++r) {
             const int c = lane + 32 * r;
-            // fast: significand aligned to the common shift (exact: 7 spare
-            // low bits); exact path: the raw significand
-            s_mant[c] = (all_fast && rc[r].mant != 0) ? (rc[r].mant >> (smax - rc[r].shift))
+            // fast: significand aligned to the common shift; exact path: raw
+            s_mant[c] = (all_fast && rc[r].mant != 0) ? (rc[r].mant >> (rc[r].shift - smin))
                                                       : rc[r].mant;
           }
+          const int32_t smax = smin;  // the common shift
           fast_shm32 = smax - 32;
           fast_add = all_fast ? (1ll << (smax - 1)) + static_cast<long long>(args.zp_y) * (1ll << smax)
                               : 0;
