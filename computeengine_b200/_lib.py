@@ -81,6 +81,8 @@ def _load() -> C.CDLL:
         "ie_cuda_conv2d_bf16x3": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _i32, _p]),
         "ie_cuda_conv2d_f32_workspace_bytes": (C.c_size_t, [P(ConvDesc)]),
         "ie_cuda_conv2d_f32": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p, C.c_size_t, _p]),
+        "ie_cuda_noalloc_scratch_bytes": (C.c_size_t, []),
+        "ie_cuda_conv2d_f32_noalloc": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p]),
         "ie_cuda_last_error": (C.c_char_p, []),
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),

@@ -389,6 +389,43 @@ int grid_1d(int64_t total, int block) {
 
 }  // namespace
 
+// ======================================================= no-allocation path
+//
+// Scratch for ie_cuda_conv2d_f32_noalloc: a fixed array in the library's own
+// device image, so that entry point never allocates.  Every GPU that loads
+// the library holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t{16} << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch on each device.  In host code the
+// array's name is only a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress with that device current; it is looked up on the first
+// call made on each device and cached.
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[64] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(IE_RUNTIME, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(IE_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      return fail(IE_RUNTIME, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return IE_OK;
+}
+
+}  // namespace
+
 // ===================================================================== ABI
 
 extern "C" {
@@ -763,6 +800,26 @@ int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x, 
   }
   if ((rc = ie_cuda_f32_pack_weights(desc, w, packed, stream)) != IE_OK) return rc;
   return ie_cuda_conv2d_bf16x3(desc, act, x_split, packed, bias, y, IE_Y_F32_NCHW, stream);
+}
+
+size_t ie_cuda_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int ie_cuda_conv2d_f32_noalloc(const ie_conv2d_desc* desc, int32_t act, const float* x,
+                               const float* w, const float* bias, float* y, void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  // the size check comes first and touches no device state
+  const size_t need = ie_cuda_conv2d_f32_workspace_bytes(desc);
+  if (need > kNoAllocScratchBytes) {
+    return fail(IE_INVALID_ARGUMENT,
+                "convolution needs %zu bytes of scratch; the no-allocation entry point has %zu "
+                "(use ie_cuda_conv2d_f32 with a caller-provided workspace)",
+                need, kNoAllocScratchBytes);
+  }
+  void* scratch = nullptr;
+  if (need > 0 && (rc = noalloc_scratch(&scratch)) != IE_OK) return rc;
+  return ie_cuda_conv2d_f32(desc, act, x, w, bias, y, scratch, need, stream);
 }
 
 }  // extern "C"

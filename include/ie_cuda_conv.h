@@ -214,6 +214,30 @@ int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x,
                        const float* w, const float* bias, float* y, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* No-allocation variant of ie_cuda_conv2d_f32.  It has no counterpart in the
+ * reference.  It is for callers that cannot allocate device memory or hand
+ * this library a workspace: an Op::forward that only receives the engine's
+ * host allocator, or code that must not call cudaMalloc / cudaFree (they
+ * synchronize the device and can break an owner's memory plan).  The caller
+ * still passes x, w, bias and y; the packed operands go to a fixed scratch
+ * array inside this library's device image (ie_cuda_noalloc_scratch_bytes(),
+ * 16 MiB, held on every GPU that loads the library until the process exits).
+ *   - Convolutions whose workspace (ie_cuda_conv2d_f32_workspace_bytes) is
+ *     larger than the scratch are rejected with IE_INVALID_ARGUMENT before
+ *     any device work.
+ *   - The first call on a device looks up the scratch's device address with
+ *     that device current (cudaGetSymbolAddress); make that first call before
+ *     any stream capture on that device.
+ *   - All calls share the one scratch array, which keeps the last call's
+ *     contents; every byte a call reads is rewritten by its own packing
+ *     kernels first, so nothing needs clearing.  Calls that overlap on the
+ *     GPU (different streams, or different host threads without ordering)
+ *     race on the scratch: serialize them.
+ * No cudaMalloc, cudaFree or allocating library routine is called. */
+size_t ie_cuda_noalloc_scratch_bytes(void);
+int ie_cuda_conv2d_f32_noalloc(const ie_conv2d_desc* desc, int32_t act, const float* x,
+                               const float* w, const float* bias, float* y, void* stream);
+
 /* ------------------------------------------------------------ errors */
 
 /* Human-readable detail of the last failing call on this host thread. */
