@@ -1,0 +1,81 @@
+"""Depthwise int8 convolution (CUDA cores, NHWC, 128-bit channel vectors)
+against the int8 oracle run as a grouped convolution with group == C
+(the reference's DepthwiseConv2DOp semantics, conv2d_op.h:53-67).
+Bit-exact, including any input zero point (padding is real 0)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def run_dw_gpu(x, w, bias, mult, *, stride, pad, zp_x, zp_y, qmin, qmax, y_signed=False):
+    import torch
+    from computeengine_b200 import _lib as L
+    from tests.qconv import desc_for
+    n, c, h, ww = x.shape
+    k = w.shape[2]
+    d = desc_for(L, n, c, h, ww, c, k, k, (stride, stride), (pad,) * 4, (1, 1), c, 0, 1)
+    s = L.ConvShape()
+    L.check(L.lib.ie_conv2d_resolve(d, c, s))
+    cs = (c + 15) // 16 * 16
+    stream = torch.cuda.current_stream().cuda_stream
+    xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    x_nhwc = torch.zeros((n, h, ww, cs), dtype=torch.uint8, device="cuda")
+    L.check(L.lib.ie_cuda_q8_pack_input(xd.data_ptr(), x_nhwc.data_ptr(), n, c, h, ww, cs, 0, stream))
+    packed = torch.zeros(int(L.lib.ie_cuda_dw_q8_packed_weight_bytes(d)), dtype=torch.uint8, device="cuda")
+    L.check(L.lib.ie_cuda_dw_q8_pack_weights(d, torch.from_numpy(w).cuda().data_ptr(),
+                                             packed.data_ptr(), stream))
+    q = L.Q8Params()
+    q.x_signed, q.zp_x, q.y_signed, q.zp_y, q.qmin, q.qmax = int(x.dtype == np.int8), zp_x, \
+        int(y_signed), zp_y, qmin, qmax
+    y = torch.full((n, s.out_h, s.out_w, cs), 99, dtype=torch.uint8, device="cuda")
+    bd, md = torch.from_numpy(bias).cuda(), torch.from_numpy(mult).cuda()
+    L.check(L.lib.ie_cuda_dwconv2d_q8(d, q, x_nhwc.data_ptr(), packed.data_ptr(), bd.data_ptr(),
+                                      md.data_ptr(), y.data_ptr(), stream))
+    torch.cuda.synchronize()
+    assert L.take_device_error() == 0
+    out = y[..., :c].permute(0, 3, 1, 2).contiguous().cpu().numpy()
+    return out.view(np.int8) if y_signed else out
+
+
+CASES = [
+    # (n, c, h, w, k, stride, pad, zp_x, signed_in)
+    (2, 32, 16, 16, 3, 1, 1, 128, False),
+    (2, 96, 15, 13, 3, 2, 1, 0, False),
+    (1, 144, 14, 14, 3, 1, 1, 0, False),
+    (1, 24, 9, 9, 3, 2, 1, 7, False),        # c not a multiple of 16, odd zero point
+    (3, 48, 8, 8, 5, 1, 2, 0, True),         # int8 input, 5x5
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c[:6])))
+def test_depthwise_bit_exact(oracle, case):
+    n, c, h, w, k, stride, pad, zp_x, signed_in = case
+    rng = np.random.default_rng(c * 7 + k)
+    if signed_in:
+        x = rng.integers(-100, 101, (n, c, h, w)).astype(np.int8)
+    else:
+        x = np.clip(np.rint(rng.normal(zp_x + 40, 40, (n, c, h, w))), 0, 255).astype(np.uint8)
+    wq = rng.integers(-127, 128, (c, 1, k, k)).astype(np.int8)
+    bias = rng.integers(-2000, 2000, c).astype(np.int32)
+    mult = rng.uniform(0.001, 0.01, c).astype(np.float32)
+    zp_y, qmin, qmax = 0, 0, 120  # ReLU6 at output scale 0.05
+    got = run_dw_gpu(x, wq, bias, mult, stride=stride, pad=pad, zp_x=zp_x, zp_y=zp_y, qmin=qmin,
+                     qmax=qmax)
+    want = oracle.conv2d_q8(x, wq, bias, mult, zp_x, zp_y, qmin, qmax, strides=(stride, stride),
+                            pads=(pad,) * 4, group=c, depthwise=True)
+    np.testing.assert_array_equal(got, want)
+    assert (want == qmax).any() and (want == qmin).any()
+
+
+def test_depthwise_signed_output_general_zero_point(oracle):
+    rng = np.random.default_rng(3)
+    x = rng.integers(0, 256, (2, 64, 12, 12)).astype(np.uint8)
+    wq = rng.integers(-127, 128, (64, 1, 3, 3)).astype(np.int8)
+    bias = rng.integers(-2000, 2000, 64).astype(np.int32)
+    mult = rng.uniform(0.0005, 0.004, 64).astype(np.float32)
+    got = run_dw_gpu(x, wq, bias, mult, stride=1, pad=1, zp_x=100, zp_y=-3, qmin=-128, qmax=127,
+                     y_signed=True)
+    want = oracle.conv2d_q8(x, wq, bias, mult, 100, -3, -128, 127, y_signed=True, pads=(1,) * 4,
+                            group=64, depthwise=True)
+    np.testing.assert_array_equal(got, want)
