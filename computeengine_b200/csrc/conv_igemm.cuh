@@ -568,6 +568,11 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       const int64_t pixel = row0 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              buf * P::kAccCols + sub * BN + col_lo;
+      if (tma_out) {
+        // The staging buffer is free once the previous tile's store has read it.
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int cc = 0; cc < kWarpCols; cc += 32) {
         uint32_t acc[32];
@@ -636,30 +641,15 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
         }
       }
       if (tma_out) {
-        // Read the staged 32 x kWarpCols tile back row-wise and write it with
-        // coalesced 16-byte stores (kWarpCols / 16 lanes per row segment):
-        // no TMA instructions, whose per-instruction cost dominated here.
+        fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the TMA unit
         __syncwarp();
-        constexpr int kChunksPerRow = kWarpCols / 16;
-        constexpr int kChunks = 32 * kChunksPerRow;
-        uint8_t* ybase = static_cast<uint8_t*>(args.y);
-#pragma unroll
-        for (int it = 0; it < kChunks / 32; ++it) {
-          const int id = it * 32 + lane;
-          const int r = id / kChunksPerRow;
-          const int c = id - r * kChunksPerRow;
-          const uint32_t off = r * kWarpCols + c * 16;
-          const uint32_t phys = off ^ (((off >> 7) & kOutSwizzleMask) << 4);
-          const uint4 v = *reinterpret_cast<const uint4*>(s_out + phys);
-          const int64_t row = row0 + r;
-          const int32_t col = wcol0 + c * 16;
-          if (row < args.m_total && col < args.y_ld) {
-            *reinterpret_cast<uint4*>(ybase + row * args.y_ld + col) = v;
-          }
+        if (lane == 0 && row0 < args.m_total && wcol0 < args.y_ld) {
+          tma_store_2d(&tmap_y, s_out, wcol0, static_cast<int32_t>(row0));
+          bulk_commit_group();
         }
-        __syncwarp();  // the staging tile is rewritten by the next tile
       }
     }
+    if (lane == 0) bulk_wait_group0();
   }
 
   tc_fence_before();
