@@ -46,6 +46,8 @@ enum : unsigned int {
   kErrWaitAccEmpty = 0x103,
   kErrWaitAccFull = 0x104,
   kErrWaitWeights = 0x105,
+  kErrWaitOutFull = 0x106,
+  kErrWaitOutFree = 0x107,
 };
 
 constexpr int kMaxStages = 12;
@@ -60,6 +62,7 @@ struct IgemmArgs {
   int32_t num_k;      // kh * kw * cblocks
   int32_t k_per_tap;  // packed weight K elements per tap (cblocks * BK elems)
   int32_t stages;     // pipeline depth (<= kMaxStages)
+  int32_t out_bufs;   // requantized output: staged tiles in flight (1 or 2)
   int64_t m_total;    // n * out_h * out_w
   int32_t m_tiles, n_tiles;
   // epilogue
@@ -71,7 +74,8 @@ struct IgemmArgs {
   int32_t act;               // fp32 path: 0 = no clamp (NaN propagates)
   int32_t out_mode;
   void* y;
-  int64_t y_ld;  // elements between consecutive output pixels
+  int64_t y_ld;       // elements between consecutive output pixels
+  int64_t acc_bound;  // int8 path: bound on |accumulator| (K * 255 * 128)
 };
 
 __host__ __device__ constexpr uint32_t swizzle_layout_code(int row_bytes) {
@@ -126,24 +130,146 @@ __device__ __forceinline__ int32_t requant_exact(int32_t t, RequantConst k, int3
   return static_cast<int32_t>(r);
 }
 
-// Fast path.  All columns of a warp share one shift S in [32, 62]: each
-// channel's significand is aligned to it exactly (mant' = mult * 2^S, an
-// integer because mant carries 7 spare low bits and the channel's own shift
-// is within 7 of S).  The rounding half and the zero point fold into one
-// warp-uniform addend C = 2^(S-1) + zp * 2^S.  Valid when every mant' >= 0
-// and zp_y <= qmin: the results of negative products clamp to qmin anyway, so
-// the sign correction of the exact rounding can be dropped.  Only the high
-// word of the product is shifted.
-__device__ __forceinline__ int32_t requant_fast(int32_t t, int32_t mant, long long add,
-                                                int32_t shm32, int32_t qmin, int32_t qmax) {
-  const long long p = static_cast<long long>(t) * mant + add;
-  const int32_t r = static_cast<int32_t>(p >> 32) >> shm32;
-  return min(max(r, qmin), qmax);
-}
-
 __device__ __forceinline__ uint32_t pack4_bytes(uint32_t q0, uint32_t q1, uint32_t q2,
                                                 uint32_t q3) {
   return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+}
+
+// Saturating pack of two int32 values into the low 16 bits (lo_byte first):
+// cvt.pack.sat clamps each value to the storage type.
+template <bool kS8>
+__device__ __forceinline__ uint32_t pack2_sat(int32_t lo_byte, int32_t hi_byte) {
+  uint32_t d;
+  if constexpr (kS8) {
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(hi_byte), "r"(lo_byte), "r"(0u));
+  } else {
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(hi_byte), "r"(lo_byte), "r"(0u));
+  }
+  return d;
+}
+
+// Requantize modes of the int8 epilogue, chosen per warp and output-channel
+// tile.  The fast modes share one shift S for the warp's columns: each
+// channel's significand is aligned to it exactly (mant' = mult * 2^S, an
+// integer because mant carries 7 spare low bits and the channel's own shift is
+// within 7 of S), and the rounding half and zero point form one warp-uniform
+// C = 2^(S-1) + zp * 2^S.  S <= 53 and |zp| <= 255 keep every sum below 2^63.
+enum : int {
+  // p = acc * mant' + (bias * mant' + C): one 64-bit multiply-add per value
+  // with a per-column 64-bit addend.  Valid when zp_y <= qmin (a negative
+  // product lands at or below zp, so the sign correction of half-away
+  // rounding cannot change the clamped result) and |bias| + |acc| < 2^31
+  // (acc + bias does not wrap, so folding it into the addend is exact).
+  kReqFold = 0,
+  // t = acc + bias (wrapping in int32 like the oracle), p = t * mant' + C -
+  // [t < 0]: exact half-away rounding for either sign.  Needs S >= 33 so that
+  // C's low word is zero and C - [t < 0] is {lo: t >> 31, hi: (C >> 32) +
+  // (t >> 31)}.
+  kReqSigned = 1,
+  // per-column shift and 64-bit rounding (requant_exact)
+  kReqExact = 2,
+};
+
+struct EpiQ8 {
+  const long long* s_add;  // kReqFold: bias * mant' + C per column
+  const int32_t* s_bias;   // kReqSigned / kReqExact (overlays s_add)
+  const int32_t* s_shift;  // kReqExact (overlays s_add)
+  const int32_t* s_mant;
+  int32_t hi_c, shm;       // C >> 32, S - 32
+  int32_t zp, lo, hi;
+  int lane;
+};
+
+// One warp's 32 rows x kCols columns of a requantized tile, TMEM -> the
+// CTA's staged output tile (panels of kPanelW bytes x kRows rows, swizzled
+// like the TMA store that reads them; row0 / col0 place the warp in the tile).
+// The 16x256b TMEM reads give this thread rows r and r + 8 of each 16-row half
+// (r = lane / 4) and the column pairs 8j + 2q, 8j + 2q + 1 (q = lane % 4):
+// 8 columns per 32-column chunk, whose constants are read from shared memory
+// once per chunk and serve all 4 of its rows.
+template <int kMode, bool kS8, bool kClamp, int kCols, int kRows, int kPanelW>
+__device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int row0, int col0,
+                                            const EpiQ8& e, uint64_t* acce) {
+  static_assert(kPanelW == 128 || kPanelW == 64, "staging panel width");
+  const int q4 = e.lane & 3, r8 = e.lane >> 2;
+  // TMA's 128 B (64 B) swizzle XORs the 16-byte chunk index with row % 8
+  // ((row / 2) % 4); the rows row0 + 8i + r8 this thread writes all share it.
+  const uint32_t xr = kPanelW == 128 ? (r8 << 4) : (((r8 >> 1) & 3) << 4);
+  uint32_t lo_part[4];  // column-within-32 part of the swizzled offset
+#pragma unroll
+  for (int j = 0; j < 4; ++j) lo_part[j] = (8 * j + 2 * q4) ^ (xr & 0x10u);
+  uint8_t* const tb = s_tile + (row0 + r8) * kPanelW;
+#pragma unroll 1
+  for (int cc = 0; cc < kCols; cc += 32) {
+    const int col = col0 + cc;
+    uint8_t* const cb = tb + (col / kPanelW) * (kRows * kPanelW) + ((col % kPanelW) ^ (xr & 0x60u));
+    uint32_t acc[2][16];
+    tmem_ld_16x256b_x4(t_q + cc, acc[0]);
+    tmem_ld_16x256b_x4(t_q + (16u << 16) + cc, acc[1]);
+    tmem_ld_wait();
+    if (cc + 32 >= kCols) {
+      // Last read of this accumulator buffer by this warp: hand it back so
+      // the MMA warp can start the next tile while we finish the epilogue.
+      tc_fence_before();
+      __syncwarp();
+      if (e.lane == 0) mbar_arrive(acce);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // constants of this thread's column pair 8j + 2q, 8j + 2q + 1
+      const int c = cc + 8 * j + 2 * q4;
+      long long ka[2] = {0, 0};
+      int32_t kb[2] = {0, 0}, km[2] = {0, 0};
+      if constexpr (kMode != kReqExact) {
+        const int2 m2 = *reinterpret_cast<const int2*>(e.s_mant + c);
+        km[0] = m2.x;
+        km[1] = m2.y;
+        if constexpr (kMode == kReqFold) {
+          const longlong2 a2 = *reinterpret_cast<const longlong2*>(e.s_add + c);
+          ka[0] = a2.x;
+          ka[1] = a2.y;
+        } else {
+          const int2 b2 = *reinterpret_cast<const int2*>(e.s_bias + c);
+          kb[0] = b2.x;
+          kb[1] = b2.y;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int rs = 0; rs < 2; ++rs) {
+          int32_t r[2];
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const uint32_t a = acc[h][4 * j + 2 * rs + x];
+            if constexpr (kMode == kReqExact) {
+              RequantConst k;
+              k.mant = e.s_mant[c + x];
+              k.shift = e.s_shift[c + x];
+              r[x] = requant_exact(static_cast<int32_t>(a + static_cast<uint32_t>(e.s_bias[c + x])),
+                                   k, e.zp, e.lo, e.hi);
+            } else {
+              long long p;
+              if constexpr (kMode == kReqFold) {
+                p = static_cast<long long>(static_cast<int32_t>(a)) * km[x] + ka[x];
+              } else {
+                const int32_t t = static_cast<int32_t>(a + static_cast<uint32_t>(kb[x]));
+                const int32_t sg = t >> 31;
+                const long long cs = static_cast<long long>(
+                    (static_cast<unsigned long long>(static_cast<uint32_t>(e.hi_c + sg)) << 32) |
+                    static_cast<uint32_t>(sg));
+                p = static_cast<long long>(t) * km[x] + cs;
+              }
+              r[x] = static_cast<int32_t>(p >> 32) >> e.shm;
+              if constexpr (kClamp) r[x] = min(max(r[x], e.lo), e.hi);
+            }
+          }
+          *reinterpret_cast<uint16_t*>(cb + lo_part[j] + (h * 16 + rs * 8) * kPanelW) =
+              static_cast<uint16_t>(pack2_sat<kS8>(r[0], r[1]));
+        }
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------ fp32 / raw stores
@@ -239,11 +365,15 @@ struct IgemmPlan {
   // column groups; each warp covers 32 rows x kWarpCols columns.
   static constexpr int kColGroups = EPI_WARPS / (4 * M_SUB);
   static constexpr int kWarpCols = BN / kColGroups;
-  static constexpr int kOutWarpBytes = 32 * kWarpCols;
-  // per warp: output staging, then per-column bias, significand and shift
-  static constexpr int kEpiWarpBytes = kOutWarpBytes + kWarpCols * 12;
-  static constexpr int kEpiBytes = EPI_WARPS * kEpiWarpBytes;
-  static constexpr int kBarBytes = 8 * (2 * kMaxStages + 6) + 32;
+  // Requantized int8 output: the epilogue warps stage the whole tile (kRows x
+  // BN bytes) as panels kPanelW bytes wide (the widest TMA swizzle is 128 B);
+  // the store warp writes it with one TMA store per panel.
+  static constexpr int kPanelW = BN < 128 ? BN : 128;
+  static constexpr int kPanels = BN / kPanelW;
+  static constexpr int kOutTile = KIND_I8 ? kRows * BN : 0;
+  // per epilogue warp: per-column bias, significand and shift
+  static constexpr int kConstBytes = EPI_WARPS * kWarpCols * 12;
+  static constexpr int kBarBytes = 8 * (2 * kMaxStages + 10) + 32;
   static constexpr int kAccCols = M_SUB * BN;
   static constexpr uint32_t kTmemCols = 2 * kAccCols <= 64    ? 64
                                         : 2 * kAccCols <= 128 ? 128
@@ -253,8 +383,9 @@ struct IgemmPlan {
   static_assert(kColGroups >= 1 && EPI_WARPS == 4 * M_SUB * kColGroups, "epilogue warps");
   static_assert(kWarpCols >= 32 && kWarpCols % 32 == 0, "epilogue columns per warp");
   // dynamic smem for `stages` pipeline stages and `num_k` resident weight steps
-  static constexpr int bytes(int stages, int num_k) {
-    return 1024 + stages * kStage + (B_RES ? kParts * num_k * kB : 0) + kEpiBytes + kBarBytes;
+  static constexpr int bytes(int stages, int num_k, int out_bufs) {
+    return 1024 + stages * kStage + (B_RES ? kParts * num_k * kB : 0) + out_bufs * kOutTile +
+           kConstBytes + kBarBytes;
   }
 };
 
@@ -266,7 +397,7 @@ struct IgemmPlan {
 //          tap [hi (Ck) | lo (Ck)]; every K block issues A_hi*B_hi, A_hi*B_lo
 //          and A_lo*B_hi into the same f32 accumulator.
 template <int BN, int BK_BYTES, int EPI_WARPS, int M_SUB, bool B_RES, bool KIND_I8, bool A_SIGNED>
-__global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
+__global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
     conv_igemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_y, const IgemmArgs args) {
@@ -283,8 +414,6 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
   constexpr int kBkElems = BK_BYTES / kElemBytes;
   constexpr uint32_t kIdesc =
       KIND_I8 ? make_idesc_i8(128, BN, A_SIGNED, true) : make_idesc_bf16(128, BN);
-  constexpr uint32_t kOutSwizzleMask = kWarpCols >= 128 ? 7u : kWarpCols == 64 ? 3u : 1u;
-  static_assert(kWarpCols <= 128, "TMA store box inner extent");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -292,14 +421,17 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
   const int stages = args.stages;
   uint8_t* stage_base = smem;
   uint8_t* b_res = stage_base + stages * kStage;  // resident weights (B_RES)
-  uint8_t* epi_base = b_res + (B_RES ? kParts * args.num_k * kB : 0);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_base + P::kEpiBytes);
+  uint8_t* out_stage = b_res + (B_RES ? kParts * args.num_k * kB : 0);  // [out_bufs]
+  uint8_t* const_base = out_stage + args.out_bufs * P::kOutTile;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(const_base + P::kConstBytes);
   uint64_t* empty_bar = full_bar + kMaxStages;
   uint64_t* accf_bar = empty_bar + kMaxStages;  // [2]
   uint64_t* acce_bar = accf_bar + 2;            // [2]
   uint64_t* drain_bar = acce_bar + 2;           // [1]
   uint64_t* bres_bar = drain_bar + 1;           // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
+  uint64_t* ofull_bar = bres_bar + 1;           // [2] staged output tile written
+  uint64_t* ofree_bar = ofull_bar + 2;          // [2] staged output tile read by its store
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ofree_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* kiter_issued = tmem_slot + 2;
   uint32_t* kiter_consumed = tmem_slot + 3;
@@ -341,6 +473,10 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     }
     mbar_init(drain_bar, 1);
     mbar_init(bres_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ofull_bar[b], EPI_WARPS);
+      mbar_init(&ofree_bar[b], 1);
+    }
     *abort_flag = 0;
     *kiter_issued = 0;
     *kiter_consumed = 0;
@@ -485,6 +621,30 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       int dummy_abort = 0;
       mbar_wait(drain_bar, 0, &dummy_abort, kErrWaitFull);
     }
+  } else if (warp == 2 + EPI_WARPS) {
+    // ------------------------------------------------ output store warp
+    // One TMA store per panel of each staged tile, so the TMA unit sees
+    // kPanels stores per tile rather than one per epilogue warp.
+    const bool tma_out = KIND_I8 && (args.out_mode == kOutU8 || args.out_mode == kOutS8);
+    if (tma_out && lane == 0) {
+      int m_tile, n_tile;
+      for (int j = 0; tile_of(j, &m_tile, &n_tile); ++j) {
+        const int ob = args.out_bufs == 2 ? (j & 1) : 0;
+        const uint32_t oph = args.out_bufs == 2 ? ((j >> 1) & 1) : (j & 1);
+        if (!mbar_wait(&ofull_bar[ob], oph, abort_flag, kErrWaitOutFull)) break;
+        const uint8_t* s_tile = out_stage + ob * P::kOutTile;
+        const int32_t row0 = m_tile * P::kRows;
+#pragma unroll
+        for (int p = 0; p < P::kPanels; ++p) {
+          const int32_t col = n_tile * BN + p * P::kPanelW;
+          if (col < args.y_ld) tma_store_2d(&tmap_y, s_tile + p * P::kRows * P::kPanelW, col, row0);
+        }
+        bulk_commit_group();
+        bulk_wait_group_read0();  // the staged tile may be overwritten
+        mbar_arrive(&ofree_bar[ob]);
+      }
+      bulk_wait_group0();
+    }
   } else {
     // ------------------------------------------------ epilogue warps
     const int ew = warp - 2;       // 0 .. EPI_WARPS-1
@@ -492,19 +652,30 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
     const int idx = ew / 4;
     const int sub = idx / P::kColGroups;
     const int col_lo = (idx % P::kColGroups) * kWarpCols;
-    // 32 rows x kWarpCols bytes, swizzled: all warps' buffers first so each
-    // stays aligned to the swizzle period, then the constants
-    uint8_t* s_out = epi_base + ew * P::kOutWarpBytes;
-    int32_t* s_bias = reinterpret_cast<int32_t*>(epi_base + EPI_WARPS * P::kOutWarpBytes +
-                                                 ew * kWarpCols * 12);
-    int32_t* s_mant = s_bias + kWarpCols;   // fast path: aligned to the warp's shift
-    int32_t* s_shift = s_mant + kWarpCols;  // exact path: the column's own shift
+    // 12 bytes of constants per column: kReqFold's 64-bit addends overlay
+    // bias + shift (fp32 bias in the bf16 path), then the significands
+    uint8_t* s_const = const_base + ew * kWarpCols * 12;
+    long long* s_add = reinterpret_cast<long long*>(s_const);
+    int32_t* s_bias = reinterpret_cast<int32_t*>(s_const);
+    int32_t* s_shift = s_bias + kWarpCols;
+    int32_t* s_mant = reinterpret_cast<int32_t*>(s_const + 8 * kWarpCols);
     const bool tma_out = KIND_I8 && (args.out_mode == kOutU8 || args.out_mode == kOutS8);
+    const bool y_s8 = args.out_mode == kOutS8;
     const bool sign_free = args.zp_y <= args.qmin;  // negative products clamp to qmin
+    // clamp range equal to the storage type: the saturating pack is the clamp
+    const bool clamp_free = args.qmin == (y_s8 ? -128 : 0) && args.qmax == (y_s8 ? 127 : 255);
     int loaded_n_tile = -1;
-    bool all_fast = false;  // every column of this warp takes requant_fast
-    long long fast_add = 0;
-    int32_t fast_shm32 = 0;
+    int req_mode = kReqExact;
+    EpiQ8 eq;
+    eq.s_add = s_add;
+    eq.s_bias = s_bias;
+    eq.s_mant = s_mant;
+    eq.s_shift = s_shift;
+    eq.hi_c = eq.shm = 0;
+    eq.zp = args.zp_y;
+    eq.lo = args.qmin;
+    eq.hi = args.qmax;
+    eq.lane = lane;
     int m_tile, n_tile;
     for (int j = 0; tile_of(j, &m_tile, &n_tile); ++j) {
       const int buf = j & 1;
@@ -517,40 +688,57 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
           // one (largest multiplier), every other significand shifts right by
           // shift_c - S <= 7 bits, exactly (its 7 low bits are zero)
           RequantConst rc[kWarpCols / 32];
+          int32_t bias[kWarpCols / 32];
           int32_t smin = 1 << 20;
-          bool fast = true;
+          bool fast = true, bias_fits = true;
 #pragma unroll
           for (int r = 0; r < kWarpCols / 32; ++r) {
-            const int c = lane + 32 * r;
-            const int32_t ch = wcol0 + c;
+            const int32_t ch = wcol0 + lane + 32 * r;
             const bool in = ch < args.m;
-            s_bias[c] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
+            bias[r] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
             rc[r] = split_multiplier((in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f);
             if (rc[r].mant != 0) smin = min(smin, rc[r].shift);
             fast = fast && rc[r].mant >= 0;
+            const long long b = bias[r];
+            bias_fits = bias_fits && (b < 0 ? -b : b) + args.acc_bound < (1ll << 31);
           }
+          // the common shift S is the smallest one (largest multiplier); every
+          // other significand shifts right by shift_c - S <= 7 bits, exactly
           smin = __reduce_min_sync(0xFFFFFFFFu, smin);
-          if (smin == (1 << 20)) smin = 32;  // all multipliers zero
-          if (smin < 32 || smin > 62) fast = false;
+          if (smin == (1 << 20)) smin = 33;  // all multipliers zero: any S works
+#pragma unroll
+          for (int r = 0; r < kWarpCols / 32; ++r) {
+            if (rc[r].mant != 0 && rc[r].shift - smin > 7) fast = false;
+          }
+          fast = __all_sync(0xFFFFFFFFu, fast) && smin >= 32 && smin <= 53;
+          bias_fits = __all_sync(0xFFFFFFFFu, bias_fits);
+          // raw int32 output reads the plain bias: exact mode's layout
+          req_mode = !tma_out ? kReqExact
+                              : (fast && sign_free && bias_fits)
+                                    ? kReqFold
+                                    : ((fast && smin >= 33) ? kReqSigned : kReqExact);
+          const long long c_add =
+              (1ll << (smin - 1)) + static_cast<long long>(args.zp_y) * (1ll << smin);
 #pragma unroll
           for (int r = 0; r < kWarpCols / 32; ++r) {
             const int c = lane + 32 * r;
-            s_shift[c] = rc[r].shift;
-            const int d = rc[r].shift - smin;
-            if (rc[r].mant != 0 && d > 7) fast = false;
+            const int32_t m_al = (req_mode != kReqExact && rc[r].mant != 0)
+                                     ? (rc[r].mant >> (rc[r].shift - smin)) : 0;
+            if (req_mode == kReqFold) {
+              s_add[c] = static_cast<long long>(bias[r]) * m_al + c_add;
+              s_mant[c] = m_al;
+            } else {
+              s_bias[c] = bias[r];
+              if (req_mode == kReqSigned) {
+                s_mant[c] = m_al;
+              } else {
+                s_mant[c] = rc[r].mant;
+                s_shift[c] = rc[r].shift;
+              }
+            }
           }
-          all_fast = __all_sync(0xFFFFFFFFu, fast) && sign_free;
-#pragma unroll
-          for (int r = 0; r < kWarpCols / 32; ++r) {
-            const int c = lane + 32 * r;
-            // fast: significand aligned to the common shift; exact path: raw
-            s_mant[c] = (all_fast && rc[r].mant != 0) ? (rc[r].mant >> (rc[r].shift - smin))
-                                                      : rc[r].mant;
-          }
-          const int32_t smax = smin;  // the common shift
-          fast_shm32 = smax - 32;
-          fast_add = all_fast ? (1ll << (smax - 1)) + static_cast<long long>(args.zp_y) * (1ll << smax)
-                              : 0;
+          eq.hi_c = static_cast<int32_t>(c_add >> 32);
+          eq.shm = smin - 32;
         } else {
           for (int c = lane; c < kWarpCols; c += 32) {
             const int32_t ch = wcol0 + c;
@@ -569,9 +757,33 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              buf * P::kAccCols + sub * BN + col_lo;
       if (tma_out) {
-        // The staging buffer is free once the previous tile's store has read it.
-        if (lane == 0) bulk_wait_group_read0();
+        // the staged tile buffer is free once its previous store has read it
+        const int ob = args.out_bufs == 2 ? (j & 1) : 0;
+        const uint32_t oph = args.out_bufs == 2 ? ((j >> 1) & 1) : (j & 1);
+        if (!mbar_wait_warp(&ofree_bar[ob], oph ^ 1u, abort_flag, kErrWaitOutFree)) break;
+        uint8_t* s_tile = out_stage + ob * P::kOutTile;
+        const int r0 = sub * 128 + quarter * 32;
+        const uint32_t t_q = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             buf * P::kAccCols + sub * BN + col_lo;
+        uint64_t* ae = &acce_bar[buf];
+        constexpr int W = kWarpCols, R = P::kRows, Z = P::kPanelW;
+        switch (req_mode * 4 + (y_s8 ? 2 : 0) + (clamp_free ? 0 : 1)) {
+          case 0: epi_q8_tile<kReqFold, false, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 1: epi_q8_tile<kReqFold, false, true, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 2: epi_q8_tile<kReqFold, true, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 3: epi_q8_tile<kReqFold, true, true, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 4: epi_q8_tile<kReqSigned, false, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 5: epi_q8_tile<kReqSigned, false, true, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 6: epi_q8_tile<kReqSigned, true, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 7: epi_q8_tile<kReqSigned, true, true, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          case 8:
+          case 9: epi_q8_tile<kReqExact, false, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+          default: epi_q8_tile<kReqExact, true, false, W, R, Z>(t_q, s_tile, r0, col_lo, eq, ae); break;
+        }
+        fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the TMA unit
         __syncwarp();
+        if (lane == 0) mbar_arrive(&ofull_bar[ob]);
+        continue;
       }
 #pragma unroll 1
       for (int cc = 0; cc < kWarpCols; cc += 32) {
@@ -585,51 +797,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acce_bar[buf]);
         }
-        if (tma_out) {
-          uint32_t packed[8];
-          const int32_t z = args.zp_y, lo = args.qmin, hi = args.qmax;
-          if (all_fast) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const int4 b4 = *reinterpret_cast<const int4*>(s_bias + cc + 4 * q);
-              const int4 m4 = *reinterpret_cast<const int4*>(s_mant + cc + 4 * q);
-              const uint32_t* ac = acc + 4 * q;
-              const uint32_t q0 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[0] + static_cast<uint32_t>(b4.x)), m4.x, fast_add, fast_shm32, lo, hi));
-              const uint32_t q1 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[1] + static_cast<uint32_t>(b4.y)), m4.y, fast_add, fast_shm32, lo, hi));
-              const uint32_t q2 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[2] + static_cast<uint32_t>(b4.z)), m4.z, fast_add, fast_shm32, lo, hi));
-              const uint32_t q3 = static_cast<uint32_t>(requant_fast(
-                  static_cast<int32_t>(ac[3] + static_cast<uint32_t>(b4.w)), m4.w, fast_add, fast_shm32, lo, hi));
-              packed[q] = pack4_bytes(q0, q1, q2, q3);
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              uint32_t qv[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int c = cc + 4 * q + e;
-                RequantConst rc;
-                rc.mant = s_mant[c];
-                rc.shift = s_shift[c];
-                qv[e] = static_cast<uint32_t>(requant_exact(
-                    static_cast<int32_t>(acc[4 * q + e] + static_cast<uint32_t>(s_bias[c])), rc,
-                    z, lo, hi));
-              }
-              packed[q] = pack4_bytes(qv[0], qv[1], qv[2], qv[3]);
-            }
-          }
-          // two 16-byte chunks of this lane's row, at swizzled positions
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t off = lane * kWarpCols + cc + 16 * h;
-            const uint32_t phys = off ^ (((off >> 7) & kOutSwizzleMask) << 4);
-            *reinterpret_cast<uint4*>(s_out + phys) =
-                make_uint4(packed[4 * h], packed[4 * h + 1], packed[4 * h + 2], packed[4 * h + 3]);
-          }
-        } else {
+        {
           int32_t sb[32];
           float sbf[32];
 #pragma unroll
@@ -640,16 +808,7 @@ __global__ void __launch_bounds__(64 + EPI_WARPS * 32, 1)
           store_chunk_direct(args, acc, pixel, wcol0 + cc, sb, sbf);
         }
       }
-      if (tma_out) {
-        fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the TMA unit
-        __syncwarp();
-        if (lane == 0 && row0 < args.m_total && wcol0 < args.y_ld) {
-          tma_store_2d(&tmap_y, s_out, wcol0, static_cast<int32_t>(row0));
-          bulk_commit_group();
-        }
-      }
     }
-    if (lane == 0) bulk_wait_group0();
   }
 
   tc_fence_before();

@@ -128,6 +128,7 @@ constexpr int kSmemLimit = 227 * 1024;
 // One compiled variant of the implicit-GEMM kernel.
 struct Variant {
   int bn, bkb, m_sub, epi;
+  int out_bufs;  // staged requantized output tiles (int8 path), 0 otherwise
   bool b_res, i8, a_signed;
 };
 
@@ -136,7 +137,7 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
                    const IgemmArgs& args, int grid, cudaStream_t st) {
   using P = IgemmPlan<BN, BKB, EPI, MSUB, BRES, I8>;
   auto kern = conv_igemm_kernel<BN, BKB, EPI, MSUB, BRES, I8, AS>;
-  const int smem = P::bytes(args.stages, args.num_k);
+  const int smem = P::bytes(args.stages, args.num_k, args.out_bufs);
   if (smem > kSmemLimit) return fail(IE_UNSUPPORTED, "shared memory plan too large (%d)", smem);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -146,7 +147,8 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   if (attr_err != cudaSuccess) {
     return fail(IE_RUNTIME, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
   }
-  kern<<<grid, 64 + EPI * 32, smem, st>>>(ta, tb, ty, args);
+  // producer, MMA issuer, EPI epilogue warps, output store warp
+  kern<<<grid, 96 + EPI * 32, smem, st>>>(ta, tb, ty, args);
   return check_launch("conv_igemm_kernel");
 }
 
@@ -196,9 +198,11 @@ int plan_bytes(const Variant& v, int stages, int num_k) {
   const int ka = rows * v.bkb, kb = v.bn * v.bkb;
   const int stage = parts * (ka + (v.b_res ? 0 : kb));
   const int warp_cols = v.bn / (v.epi / (4 * v.m_sub));
-  const int epi = v.epi * (32 * warp_cols + warp_cols * 12);
-  const int bars = 8 * (2 * kMaxStages + 6) + 32;
-  return 1024 + stages * stage + (v.b_res ? parts * num_k * kb : 0) + epi + bars;
+  const int out_tile = v.i8 ? rows * v.bn : 0;
+  const int consts = v.epi * warp_cols * 12;
+  const int bars = 8 * (2 * kMaxStages + 10) + 32;
+  return 1024 + stages * stage + (v.b_res ? parts * num_k * kb : 0) + v.out_bufs * out_tile +
+         consts + bars;
 }
 
 struct IgemmSetup {
@@ -232,14 +236,30 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
     return fail(IE_UNSUPPORTED, "tensor too large");
   }
   // Weights resident in shared memory when the CTA's slice fits beside a
-  // pipeline of at least 4 activation stages.
+  // pipeline of at least 4 activation stages; two staged output tiles (the
+  // epilogue never waits for a store) unless that costs pipeline depth below 4.
+  v.out_bufs = i8 ? 2 : 0;
   v.b_res = false;
   if (i8) {
     v.b_res = true;
-    if (plan_bytes(v, 4, static_cast<int>(num_k)) > kSmemLimit) v.b_res = false;
+    if (plan_bytes(v, 4, static_cast<int>(num_k)) > kSmemLimit) {
+      v.out_bufs = 1;
+      if (plan_bytes(v, 4, static_cast<int>(num_k)) > kSmemLimit) {
+        v.out_bufs = 2;
+        v.b_res = false;
+      }
+    }
   }
-  int stages = kMaxStages;
-  while (stages > 2 && plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) --stages;
+  auto max_stages = [&] {
+    int st = kMaxStages;
+    while (st > 2 && plan_bytes(v, st, static_cast<int>(num_k)) > kSmemLimit) --st;
+    return st;
+  };
+  int stages = max_stages();
+  if (i8 && v.out_bufs == 2 && stages < 4) {
+    v.out_bufs = 1;
+    stages = max_stages();
+  }
   if (plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) {
     return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
   }
@@ -289,7 +309,10 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   a.num_k = static_cast<int32_t>(num_k);
   a.k_per_tap = static_cast<int32_t>(ck);
   a.stages = stages;
+  a.out_bufs = v.out_bufs;
   a.m_total = m_total;
+  // |x| <= 255 (uint8) or 128 (int8), |w| <= 128: |acc| <= K * 255 * 128
+  a.acc_bound = d->kh * d->kw * d->c * 255 * 128;
   a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128 * v.m_sub));
   a.n_tiles = static_cast<int32_t>(ceil_div(d->m, v.bn));
   const int sms = num_sms();
@@ -371,10 +394,11 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   a.y = y;
   a.y_ld = round_up(d->m, 16);
   if (a.out_mode == kOutU8 || a.out_mode == kOutS8) {
-    // each epilogue warp stores a 32-row x warp_cols-channel box through TMA
-    const int warp_cols = su.v.bn / (su.v.epi / (4 * su.v.m_sub));
-    if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld,
-                        warp_cols, 32)) != IE_OK) {
+    // the store warp writes each staged tile as panels of up to 128 channels
+    // x 128 * m_sub rows
+    const int panel = std::min(su.v.bn, 128);
+    if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld, panel,
+                        128 * su.v.m_sub)) != IE_OK) {
       return rc;
     }
   } else {

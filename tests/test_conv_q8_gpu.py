@@ -71,22 +71,13 @@ def test_relu6_clamp_and_unsigned_input(oracle):
     assert want.min() == zp_y and want.max() == qmax
 
 
-@pytest.mark.parametrize("y_signed,zp_y,qmin,qmax", [(False, 0, 0, 255), (True, 0, -128, 127),
-                                                      (False, 10, 10, 200), (True, -5, -100, 90)])
-def test_requantize_ties_and_saturation(oracle, y_signed, zp_y, qmin, qmax):
-    """Multipliers 2^-k and 3*2^-k make many requantized values exact .5 ties
-    (round half away from zero), others saturate; the epilogue's fast
-    saturating path and the general clamp path must both match the oracle."""
+def _run_1x1_signed_input(x, wq, bias, mult, y_signed, zp_y, qmin, qmax):
+    """int8 NHWC input, 1x1 convolution, requantized output as NCHW numpy."""
     import torch
     from computeengine_b200 import _lib as L
     from tests.qconv import desc_for
-    rng = np.random.default_rng(11)
-    n, c, h, w, m = 2, 32, 9, 9, 64
-    x = rng.integers(-60, 61, (n, c, h, w)).astype(np.int8)
-    wq = rng.integers(-127, 128, (m, c, 1, 1)).astype(np.int8)
-    bias = rng.integers(-3000, 3000, m).astype(np.int32)
-    cands = [0.5, 0.25, 0.125, 1.5, 0.75, 0.375, 2.0 ** -10, 3 * 2.0 ** -9, 0.0009765625, 0.01]
-    mult = np.array([cands[i % len(cands)] for i in range(m)], np.float32)
+    n, c, h, w = x.shape
+    m = wq.shape[0]
     d = desc_for(L, n, c, h, w, m, 1, 1)
     stream = torch.cuda.current_stream().cuda_stream
     x_nhwc = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 3, 1))).cuda()
@@ -99,11 +90,86 @@ def test_requantize_ties_and_saturation(oracle, y_signed, zp_y, qmin, qmax):
     L.check(L.lib.ie_cuda_conv2d_q8(d, q, x_nhwc.data_ptr(), packed.data_ptr(), bd.data_ptr(),
                                     md.data_ptr(), y.data_ptr(), stream))
     torch.cuda.synchronize()
-    got = y.cpu().numpy().view(np.int8 if y_signed else np.uint8).transpose(0, 3, 1, 2)
+    assert L.take_device_error() == 0
+    return y.cpu().numpy().view(np.int8 if y_signed else np.uint8).transpose(0, 3, 1, 2)
+
+
+def _tie_fraction(acc, bias, mult):
+    v = (acc.astype(np.float64) + bias.reshape(1, -1, 1, 1)) * mult.astype(np.float64).reshape(1, -1, 1, 1)
+    return np.mean(np.abs(v - np.trunc(v)) == 0.5)
+
+
+@pytest.mark.parametrize("y_signed,zp_y,qmin,qmax", [(False, 0, 0, 255), (True, 0, -128, 127),
+                                                      (False, 10, 10, 200), (True, -5, -100, 90)])
+def test_requantize_ties_and_saturation(oracle, y_signed, zp_y, qmin, qmax):
+    """Multipliers 2^-k and 3*2^-k make many requantized values exact .5 ties
+    (round half away from zero), others saturate.  Multipliers of 0.25 and
+    above put every warp on the epilogue's exact per-column path."""
+    rng = np.random.default_rng(11)
+    n, c, h, w, m = 2, 32, 9, 9, 64
+    x = rng.integers(-60, 61, (n, c, h, w)).astype(np.int8)
+    wq = rng.integers(-127, 128, (m, c, 1, 1)).astype(np.int8)
+    bias = rng.integers(-3000, 3000, m).astype(np.int32)
+    cands = [0.5, 0.25, 0.125, 1.5, 0.75, 0.375, 2.0 ** -10, 3 * 2.0 ** -9, 0.0009765625, 0.01]
+    mult = np.array([cands[i % len(cands)] for i in range(m)], np.float32)
+    got = _run_1x1_signed_input(x, wq, bias, mult, y_signed, zp_y, qmin, qmax)
     want, acc = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, qmin, qmax, y_signed=y_signed,
                                  want_acc=True)
     np.testing.assert_array_equal(got, want)
-    v = (acc + bias.reshape(1, -1, 1, 1)).astype(np.float32) * mult.reshape(1, -1, 1, 1)
-    ties = np.mean(np.abs(v - np.trunc(v)) == 0.5)
-    assert ties > 0.05, ties
+    assert _tie_fraction(acc, bias, mult) > 0.05
     assert (want == qmin).any() and (want == qmax).any()
+
+
+# (y_signed, zp_y, qmin, qmax): the output formats and clamp ranges that select
+# each fast requantize mode (bias folded into a 64-bit addend when zp_y <= qmin,
+# sign-corrected rounding otherwise; saturating pack alone when the clamp range
+# is the storage type's)
+FAST_MODE_CASES = [
+    (False, 0, 0, 255),      # folded addend, no extra clamp
+    (False, 10, 10, 200),    # folded addend, clamp
+    (True, -128, -128, 127),  # folded addend, int8 output
+    (True, 0, -128, 127),    # sign-corrected, no extra clamp
+    (True, -5, -100, 90),    # sign-corrected, clamp
+    (False, 20, 0, 255),     # sign-corrected, uint8 output
+]
+
+
+@pytest.mark.parametrize("y_signed,zp_y,qmin,qmax", FAST_MODE_CASES)
+def test_requantize_fast_modes_ties(oracle, y_signed, zp_y, qmin, qmax):
+    """Multipliers below 0.25 whose shifts lie within 7 of each other keep every
+    warp on a fast mode; small operands and multipliers such as 1/8 and 1/16
+    make many products exact .5 ties of either sign."""
+    rng = np.random.default_rng(23)
+    n, c, h, w, m = 2, 32, 11, 9, 192
+    x = rng.integers(-12, 13, (n, c, h, w)).astype(np.int8)
+    wq = rng.integers(-12, 13, (m, c, 1, 1)).astype(np.int8)
+    bias = rng.integers(-1500, 1500, m).astype(np.int32)
+    cands = [0.125, 0.0625, 0.09375, 2.0 ** -9, 0.1, 0.07, 0.2, 0.015625]
+    mult = np.array([cands[i % len(cands)] for i in range(m)], np.float32)
+    got = _run_1x1_signed_input(x, wq, bias, mult, y_signed, zp_y, qmin, qmax)
+    want, acc = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, qmin, qmax, y_signed=y_signed,
+                                 want_acc=True)
+    np.testing.assert_array_equal(got, want)
+    assert _tie_fraction(acc, bias, mult) > 0.02
+    assert (want == qmin).any() and (want == qmax).any()
+    assert ((want > qmin) & (want < qmax)).mean() > 0.3
+
+
+def test_requantize_bias_near_int32_limit(oracle):
+    """A bias within the accumulator bound of 2^31 cannot be folded into the
+    64-bit addend; acc + bias then wraps in int32 exactly as the oracle's does."""
+    rng = np.random.default_rng(5)
+    n, c, h, w, m = 1, 32, 8, 8, 64
+    x = rng.integers(-100, 101, (n, c, h, w)).astype(np.int8)
+    wq = rng.integers(-127, 128, (m, c, 1, 1)).astype(np.int8)
+    bias = rng.integers(-1000, 1000, m).astype(np.int32)
+    bias[::3] = np.int32(2 ** 31 - 1 - 50)
+    bias[1::7] = np.int32(-(2 ** 31) + 40)
+    mult = np.full(m, 2.0 ** -20, np.float32)
+    for y_signed, zp_y, qmin, qmax in ((False, 0, 0, 255), (True, 3, -128, 127)):
+        got = _run_1x1_signed_input(x, wq, bias, mult, y_signed, zp_y, qmin, qmax)
+        want, acc = oracle.conv2d_q8(x, wq, bias, mult, 0, zp_y, qmin, qmax, y_signed=y_signed,
+                                     want_acc=True)
+        np.testing.assert_array_equal(got, want)
+        t = acc.astype(np.int64) + bias.astype(np.int64).reshape(1, -1, 1, 1)
+        assert (t > 2 ** 31 - 1).any() and (t < -(2 ** 31)).any()  # both wraps occur
