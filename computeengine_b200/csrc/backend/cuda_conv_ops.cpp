@@ -1,0 +1,607 @@
+// CUDA convolution ops for the reference engine's Op interface; see
+// cuda_conv_ops.h for the contract.
+#include "cuda_conv_ops.h"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <utility>
+
+namespace ie_b200 {
+namespace {
+
+// ------------------------------------------------ attribute readers
+// Same names, accepted alternatives and messages as attrs_util.h:31-107.
+
+struct IntListAttr {
+  bool found = false;
+  std::vector<int64_t> values;
+};
+
+ie::Status read_int_list(const ie::Attrs& attrs, const char* key, IntListAttr& out) {
+  out = IntListAttr{};
+  const auto it = attrs.find(key);
+  if (it == attrs.end()) return {};
+  const auto* values = std::get_if<std::vector<int64_t>>(&it->second);
+  if (values == nullptr) {
+    return ie::Error::invalid_argument(std::string("attribute '") + key + "' must be an int list");
+  }
+  out.found = true;
+  out.values = *values;
+  return {};
+}
+
+ie::Status read_int(const ie::Attrs& attrs, const char* key, bool* found, int64_t* value) {
+  *found = false;
+  const auto it = attrs.find(key);
+  if (it == attrs.end()) return {};
+  if (const auto* v = std::get_if<int64_t>(&it->second)) {
+    *found = true;
+    *value = *v;
+    return {};
+  }
+  if (const auto* v = std::get_if<bool>(&it->second)) {
+    *found = true;
+    *value = *v ? 1 : 0;
+    return {};
+  }
+  return ie::Error::invalid_argument(std::string("attribute '") + key + "' must be an int");
+}
+
+ie::Status read_double_list(const ie::Attrs& attrs, const char* key, bool* found,
+                            std::vector<double>* out) {
+  *found = false;
+  const auto it = attrs.find(key);
+  if (it == attrs.end()) return {};
+  if (const auto* v = std::get_if<std::vector<double>>(&it->second)) {
+    *found = true;
+    *out = *v;
+    return {};
+  }
+  if (const auto* v = std::get_if<std::vector<int64_t>>(&it->second)) {
+    *found = true;
+    out->assign(v->begin(), v->end());
+    return {};
+  }
+  return ie::Error::invalid_argument(std::string("attribute '") + key + "' must be a float list");
+}
+
+ie::Status read_pair(const ie::Attrs& attrs, const char* key, std::array<int64_t, 2>& out) {
+  IntListAttr value;
+  if (auto st = read_int_list(attrs, key, value); !st.has_value()) return st;
+  if (!value.found) return {};
+  if (value.values.size() != 2) {
+    return ie::Error::invalid_argument(std::string(key) + " must contain 2 values");
+  }
+  if (value.values[0] <= 0 || value.values[1] <= 0) {
+    return ie::Error::invalid_argument(std::string(key) + " values must be positive");
+  }
+  out = {value.values[0], value.values[1]};
+  return {};
+}
+
+ie::Status read_pads(const ie::Attrs& attrs, std::array<int64_t, 4>& pads) {
+  pads = {0, 0, 0, 0};
+  IntListAttr value;
+  if (auto st = read_int_list(attrs, "pads", value); !st.has_value()) return st;
+  if (!value.found || value.values.empty()) return {};
+  if (value.values.size() == 2) {
+    pads = {value.values[0], value.values[1], value.values[0], value.values[1]};
+  } else if (value.values.size() == 4) {
+    pads = {value.values[0], value.values[1], value.values[2], value.values[3]};
+  } else {
+    return ie::Error::invalid_argument("pads must contain 2 or 4 values");
+  }
+  for (int64_t p : pads) {
+    if (p < 0) return ie::Error::invalid_argument("pads must be non-negative");
+  }
+  return {};
+}
+
+ie::Status read_auto_pad(const ie::Attrs& attrs, AutoPad& out) {
+  out = AutoPad::NotSet;
+  const auto it = attrs.find("auto_pad");
+  if (it == attrs.end()) return {};
+  const auto* value = std::get_if<std::string>(&it->second);
+  if (value == nullptr) return ie::Error::invalid_argument("attribute 'auto_pad' must be a string");
+  if (value->empty() || *value == "NOTSET") return {};
+  if (*value == "VALID") {
+    out = AutoPad::Valid;
+  } else if (*value == "SAME_UPPER") {
+    out = AutoPad::SameUpper;
+  } else if (*value == "SAME_LOWER") {
+    out = AutoPad::SameLower;
+  } else {
+    return ie::Error::invalid_argument("unsupported auto_pad: " + *value);
+  }
+  return {};
+}
+
+// ------------------------------------------------ forward helpers
+
+ie::Status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return {};
+  if (e == cudaErrorMemoryAllocation) {
+    return ie::Error::out_of_memory(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+  return ie::Error::runtime(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+ie::Status require_device() {
+  int count = 0;
+  const cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();  // clear the sticky "no device" error
+    return ie::Error::runtime("no CUDA device: the CUDA convolution ops have no CPU fallback");
+  }
+  return {};
+}
+
+// Validation shared by the fp32 and int8 ops, in the reference's order
+// (conv2d_op.cpp:77-123): argument counts, allocator, null tensors, dtypes,
+// ranks, kernel_shape; the remaining shape rules run in ie_conv2d_resolve.
+ie::Status validate(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                    const ie::ExecutionContext& context, size_t min_in, size_t max_in,
+                    const char* name) {
+  if (inputs.size() < min_in || inputs.size() > max_in || outputs.size() != 1 ||
+      outputs[0] == nullptr) {
+    return ie::Error::invalid_argument(std::string(name) +
+                                       (max_in == 3 ? " expects two or three inputs and one output"
+                                                    : " expects two inputs and one output"));
+  }
+  if (context.allocator == nullptr) {
+    return ie::Error::invalid_argument(std::string(name) + " requires an allocator");
+  }
+  for (const ie::Tensor* t : inputs) {
+    if (t == nullptr || t->buffer == nullptr) return ie::Error::invalid_argument("null tensor or buffer");
+  }
+  return {};
+}
+
+ie::Status check_ranks(const ie::Tensor& x, const ie::Tensor& w, const ConvConfig& cfg,
+                       const char* name) {
+  if (x.shape.dims.size() != 4 || w.shape.dims.size() != 4) {
+    return ie::Error::invalid_argument(std::string(name) + " expects 4D NCHW tensors");
+  }
+  if (cfg.has_kernel_shape &&
+      (cfg.kernel_shape[0] != w.shape.dims[2] || cfg.kernel_shape[1] != w.shape.dims[3])) {
+    return ie::Error::invalid_argument("kernel_shape does not match the weight tensor");
+  }
+  return {};
+}
+
+ie_conv2d_desc make_desc(const ConvConfig& cfg, const ie::Tensor& x, const ie::Tensor& w,
+                         bool depthwise) {
+  ie_conv2d_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.n = x.shape.dims[0];
+  d.c = x.shape.dims[1];
+  d.h = x.shape.dims[2];
+  d.w = x.shape.dims[3];
+  d.m = w.shape.dims[0];
+  d.kh = w.shape.dims[2];
+  d.kw = w.shape.dims[3];
+  d.stride_h = cfg.strides[0];
+  d.stride_w = cfg.strides[1];
+  d.dil_h = cfg.dilations[0];
+  d.dil_w = cfg.dilations[1];
+  d.pad_top = cfg.pads[0];
+  d.pad_left = cfg.pads[1];
+  d.pad_bottom = cfg.pads[2];
+  d.pad_right = cfg.pads[3];
+  d.group = cfg.group;
+  d.auto_pad = cfg.auto_pad == AutoPad::Valid       ? IE_PAD_VALID
+               : cfg.auto_pad == AutoPad::SameUpper ? IE_PAD_SAME_UPPER
+               : cfg.auto_pad == AutoPad::SameLower ? IE_PAD_SAME_LOWER
+                                                    : IE_PAD_NOTSET;
+  d.depthwise = depthwise ? 1 : 0;
+  // The C ABI's weight-channel check reads C/group from the desc; a weight
+  // tensor whose dim 1 differs is rejected here with the reference's message.
+  return d;
+}
+
+// Host or device source -> device pointer (uploads host data into `slot`).
+ie::Result<const void*> to_device(DeviceBuffers& dev, int slot, const ie::Tensor& t,
+                                  cudaStream_t st) {
+  if (t.device == ie::Device::CUDA) return static_cast<const void*>(t.buffer);
+  auto buf = dev.scratch(slot, t.bytes());
+  if (!buf.has_value()) return buf.error();
+  if (auto s = cuda_status(cudaMemcpyAsync(*buf, t.buffer, t.bytes(), cudaMemcpyHostToDevice, st),
+                           "cudaMemcpyAsync H2D");
+      !s.has_value()) {
+    return s.error();
+  }
+  return static_cast<const void*>(*buf);
+}
+
+ie::Status finish(cudaStream_t st) {
+  if (auto s = cuda_status(cudaStreamSynchronize(st), "cudaStreamSynchronize"); !s.has_value()) {
+    return s;
+  }
+  uint32_t code = 0;
+  if (ie_cuda_take_device_error(&code) != IE_OK || code != 0) {
+    return ie::Error::runtime("device-side wait timed out (site 0x" + std::to_string(code) + ")");
+  }
+  return {};
+}
+
+enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork };
+enum CacheKind { kCacheW = 0, kCacheWPacked, kCacheBias, kCacheMult, kCacheBiasI32 };
+
+}  // namespace
+
+// ------------------------------------------------ public helpers
+
+ie::Status parse_conv_config(const ie::Attrs& attrs, ConvConfig& config) {
+  config = ConvConfig{};
+  if (auto st = read_pair(attrs, "strides", config.strides); !st.has_value()) return st;
+  if (auto st = read_pair(attrs, "dilations", config.dilations); !st.has_value()) return st;
+  if (auto st = read_pads(attrs, config.pads); !st.has_value()) return st;
+  bool found = false;
+  int64_t group = 0;
+  if (auto st = read_int(attrs, "group", &found, &group); !st.has_value()) return st;
+  if (found) {
+    if (group <= 0) return ie::Error::invalid_argument("group must be positive");
+    config.group = group;
+  }
+  if (auto st = read_auto_pad(attrs, config.auto_pad); !st.has_value()) return st;
+  IntListAttr kernel;
+  if (auto st = read_int_list(attrs, "kernel_shape", kernel); !st.has_value()) return st;
+  if (kernel.found) {
+    if (kernel.values.size() != 2) return ie::Error::invalid_argument("kernel_shape must contain 2 values");
+    if (kernel.values[0] <= 0 || kernel.values[1] <= 0) {
+      return ie::Error::invalid_argument("kernel_shape values must be positive");
+    }
+    config.has_kernel_shape = true;
+    config.kernel_shape = {kernel.values[0], kernel.values[1]};
+  }
+  return {};
+}
+
+ie::Status to_status(int rc) {
+  if (rc == IE_OK) return {};
+  const char* msg = ie_cuda_last_error();
+  std::string m = msg != nullptr ? msg : "";
+  switch (rc) {
+    case IE_INVALID_ARGUMENT: return ie::Error::invalid_argument(m);
+    case IE_UNSUPPORTED: return ie::Error::unsupported(m);
+    case IE_NOT_FOUND: return ie::Error::not_found(m);
+    case IE_ALREADY_EXISTS: return ie::Error::already_exists(m);
+    case IE_OUT_OF_MEMORY: return ie::Error::out_of_memory(m);
+    default: return ie::Error::runtime(m);
+  }
+}
+
+DeviceBuffers::~DeviceBuffers() {
+  for (auto& kv : scratch_) cudaFree(kv.second.ptr);
+  for (auto& kv : cache_) cudaFree(kv.second.ptr);
+}
+
+ie::Result<void*> DeviceBuffers::scratch(int slot, size_t bytes) {
+  Block& b = scratch_[slot];
+  if (b.bytes < bytes || b.ptr == nullptr) {
+    if (b.ptr != nullptr) cudaFree(b.ptr);
+    b = Block{};
+    void* p = nullptr;
+    if (auto s = cuda_status(cudaMalloc(&p, bytes == 0 ? 256 : bytes), "cudaMalloc");
+        !s.has_value()) {
+      return s.error();
+    }
+    b.ptr = p;
+    b.bytes = bytes;
+  }
+  return b.ptr;
+}
+
+ie::Result<void*> DeviceBuffers::cached(const void* host_key, size_t bytes, int kind, bool* fresh) {
+  const Key k{host_key, bytes, kind};
+  auto it = cache_.find(k);
+  if (it != cache_.end()) {
+    *fresh = false;
+    return it->second.ptr;
+  }
+  void* p = nullptr;
+  if (auto s = cuda_status(cudaMalloc(&p, bytes == 0 ? 256 : bytes), "cudaMalloc"); !s.has_value()) {
+    return s.error();
+  }
+  cache_[k] = Block{p, bytes};
+  *fresh = true;
+  return p;
+}
+
+// ------------------------------------------------ fp32 Conv2D / DepthwiseConv2D
+
+ie::Status CudaConv2DOp::configure(const ie::Attrs& attrs) {
+  return parse_conv_config(attrs, config_);
+}
+
+ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                 std::vector<ie::Tensor*>& outputs,
+                                 ie::ExecutionContext& context) {
+  const char* name = depthwise_ ? "DepthwiseConv2D" : "Conv2D";
+  if (auto st = validate(inputs, outputs, context, 2, 3, "Conv2D"); !st.has_value()) return st;
+  for (const ie::Tensor* t : inputs) {
+    if (t->dtype != ie::DType::F32) return ie::Error::unsupported("P0 kernels support F32 only");
+  }
+  const ie::Tensor& x = *inputs[0];
+  const ie::Tensor& w = *inputs[1];
+  const ie::Tensor* b = inputs.size() == 3 ? inputs[2] : nullptr;
+  if (auto st = check_ranks(x, w, config_, "Conv2D"); !st.has_value()) return st;
+  ie_conv2d_desc d = make_desc(config_, x, w, depthwise_);
+  if (d.group > 0 && d.c % d.group == 0 && w.shape.dims[1] != d.c / d.group) {
+    return ie::Error::invalid_argument("Conv2D weight channels do not match C/group");
+  }
+  int64_t bias_len = -1;
+  if (b != nullptr) {
+    if (b->shape.dims.size() != 1) return ie::Error::invalid_argument("Conv2D bias must have shape [M]");
+    bias_len = b->shape.dims[0];
+  }
+  ie_conv2d_shape s;
+  if (auto st = to_status(ie_conv2d_resolve(&d, bias_len, &s)); !st.has_value()) return st;
+  (void)name;
+  if (auto st = require_device(); !st.has_value()) return st;
+
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  // weights (and bias) stay on the device for the op's lifetime, keyed by the
+  // host buffer; the dense path also keeps them in packed bf16 hi/lo form
+  const bool dense = d.group == 1;
+  const void* wdev = nullptr;
+  if (w.device == ie::Device::CUDA && !dense) {
+    wdev = w.buffer;
+  } else {
+    bool fresh = false;
+    const size_t bytes = dense ? ie_cuda_f32_packed_weight_bytes(&d) : w.bytes();
+    auto slot = dev_.cached(w.buffer, bytes, dense ? kCacheWPacked : kCacheW, &fresh);
+    if (!slot.has_value()) return slot.error();
+    if (fresh) {
+      const void* wsrc = w.buffer;
+      if (w.device != ie::Device::CUDA) {
+        auto tmp = dev_.scratch(kSlotWork, w.bytes());
+        if (!tmp.has_value()) return tmp.error();
+        if (auto e = cuda_status(cudaMemcpyAsync(dense ? *tmp : *slot, w.buffer, w.bytes(),
+                                                 cudaMemcpyHostToDevice, st),
+                                 "cudaMemcpyAsync H2D");
+            !e.has_value()) {
+          return e;
+        }
+        wsrc = dense ? *tmp : *slot;
+      }
+      if (dense) {
+        if (auto e = to_status(ie_cuda_f32_pack_weights(&d, static_cast<const float*>(wsrc), *slot, st));
+            !e.has_value()) {
+          return e;
+        }
+      }
+    }
+    wdev = *slot;
+  }
+  const float* bdev = nullptr;
+  if (b != nullptr) {
+    if (b->device == ie::Device::CUDA) {
+      bdev = b->data<float>();
+    } else {
+      bool fresh = false;
+      auto slot = dev_.cached(b->buffer, b->bytes(), kCacheBias, &fresh);
+      if (!slot.has_value()) return slot.error();
+      if (fresh) {
+        if (auto e = cuda_status(cudaMemcpyAsync(*slot, b->buffer, b->bytes(), cudaMemcpyHostToDevice, st),
+                                 "cudaMemcpyAsync H2D");
+            !e.has_value()) {
+          return e;
+        }
+      }
+      bdev = static_cast<const float*>(*slot);
+    }
+  }
+  const size_t y_bytes = static_cast<size_t>(d.n * d.m * s.out_h * s.out_w) * sizeof(float);
+  auto ydev = dev_.scratch(kSlotY, y_bytes);
+  if (!ydev.has_value()) return ydev.error();
+  int rc;
+  if (dense) {
+    // activations split into bf16 hi/lo NHWC planes, then the bf16x3
+    // tensor-core GEMM writes NCHW fp32 directly
+    const int64_t c_store = (d.c + 15) / 16 * 16;
+    auto xs = dev_.scratch(kSlotXPacked, static_cast<size_t>(d.n * d.h * d.w * c_store) * 4);
+    if (!xs.has_value()) return xs.error();
+    rc = ie_cuda_f32_pack_input(static_cast<const float*>(*xd), *xs, d.n, d.c, d.h, d.w, c_store, st);
+    if (rc == IE_OK) {
+      rc = ie_cuda_conv2d_bf16x3(&d, IE_ACT_NONE, *xs, wdev, bdev, *ydev, IE_Y_F32_NCHW, st);
+    }
+  } else {
+    rc = ie_cuda_conv2d_f32(&d, IE_ACT_NONE, static_cast<const float*>(*xd),
+                            static_cast<const float*>(wdev), bdev, static_cast<float*>(*ydev),
+                            nullptr, 0, st);
+  }
+  if (auto e = to_status(rc); !e.has_value()) return e;
+
+  auto out = ie::Tensor::allocate(ie::Shape{{d.n, d.m, s.out_h, s.out_w}}, ie::DType::F32,
+                                  context.allocator);
+  if (!out.has_value()) return out.error();
+  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, *ydev, y_bytes, cudaMemcpyDeviceToHost, st),
+                           "cudaMemcpyAsync D2H");
+      !e.has_value()) {
+    return e;
+  }
+  if (auto e = finish(st); !e.has_value()) return e;
+  *outputs[0] = std::move(*out);
+  return {};
+}
+
+// ------------------------------------------------ int8 QLinearConv2D
+
+ie::Status CudaQLinearConv2DOp::configure(const ie::Attrs& attrs) {
+  if (auto st = parse_conv_config(attrs, config_); !st.has_value()) return st;
+  bool found = false;
+  std::vector<double> mult;
+  if (auto st = read_double_list(attrs, "multiplier", &found, &mult); !st.has_value()) return st;
+  if (!found || mult.empty()) {
+    return ie::Error::invalid_argument("attribute 'multiplier' must be a float list");
+  }
+  mult_.assign(mult.size(), 0.0f);
+  for (size_t i = 0; i < mult.size(); ++i) {
+    if (!std::isfinite(mult[i])) return ie::Error::invalid_argument("multiplier must be finite");
+    mult_[i] = static_cast<float>(mult[i]);
+  }
+  IntListAttr bias;
+  if (auto st = read_int_list(attrs, "bias", bias); !st.has_value()) return st;
+  bias_.clear();
+  for (int64_t v : bias.values) {
+    if (v < INT32_MIN || v > INT32_MAX) return ie::Error::invalid_argument("bias values must fit int32");
+    bias_.push_back(static_cast<int32_t>(v));
+  }
+  int64_t v = 0;
+  if (auto st = read_int(attrs, "x_zero_point", &found, &v); !st.has_value()) return st;
+  zp_x_ = found ? v : 0;
+  if (auto st = read_int(attrs, "y_zero_point", &found, &v); !st.has_value()) return st;
+  zp_y_ = found ? v : 0;
+  if (auto st = read_int(attrs, "y_signed", &found, &v); !st.has_value()) return st;
+  y_signed_ = found && v != 0;
+  if (auto st = read_int(attrs, "qmin", &has_qmin_, &qmin_); !st.has_value()) return st;
+  if (auto st = read_int(attrs, "qmax", &has_qmax_, &qmax_); !st.has_value()) return st;
+  return {};
+}
+
+ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                        std::vector<ie::Tensor*>& outputs,
+                                        ie::ExecutionContext& context) {
+  if (auto st = validate(inputs, outputs, context, 2, 2, "QLinearConv2D"); !st.has_value()) return st;
+  const ie::Tensor& x = *inputs[0];
+  const ie::Tensor& w = *inputs[1];
+  if ((x.dtype != ie::DType::U8 && x.dtype != ie::DType::I8) || w.dtype != ie::DType::I8) {
+    return ie::Error::unsupported("QLinearConv2D takes U8/I8 activations and I8 weights");
+  }
+  if (auto st = check_ranks(x, w, config_, "QLinearConv2D"); !st.has_value()) return st;
+  const bool depthwise = config_.group > 1;
+  ie_conv2d_desc d = make_desc(config_, x, w, depthwise);
+  if (d.group > 0 && d.c % d.group == 0 && w.shape.dims[1] != d.c / d.group) {
+    return ie::Error::invalid_argument("Conv2D weight channels do not match C/group");
+  }
+  ie_conv2d_shape s;
+  const int64_t bias_len = bias_.empty() ? -1 : static_cast<int64_t>(bias_.size());
+  if (auto st = to_status(ie_conv2d_resolve(&d, bias_len, &s)); !st.has_value()) return st;
+  if (static_cast<int64_t>(mult_.size()) != d.m) {
+    return ie::Error::invalid_argument("multiplier must have M values");
+  }
+  ie_q8_params q;
+  q.x_signed = x.dtype == ie::DType::I8 ? 1 : 0;
+  q.zp_x = static_cast<int32_t>(zp_x_);
+  q.y_signed = y_signed_ ? 1 : 0;
+  q.zp_y = static_cast<int32_t>(zp_y_);
+  q.qmin = has_qmin_ ? static_cast<int32_t>(qmin_) : (y_signed_ ? -128 : 0);
+  q.qmax = has_qmax_ ? static_cast<int32_t>(qmax_) : (y_signed_ ? 127 : 255);
+  uint32_t xor_mask = 0;
+  if (!depthwise) {
+    if (d.group != 1) return ie::Error::unsupported("grouped int8 convolution (1 < group < C)");
+    if (q.zp_x != 0) {
+      // uint8 with zero point 128 is int8 with zero point 0 after flipping
+      // the top bit; other zero points are not on the tensor-core path
+      if (q.x_signed == 0 && q.zp_x == 128) {
+        xor_mask = 0x80;
+        q.zp_x = 0;
+        q.x_signed = 1;
+      } else {
+        return ie::Error::unsupported("dense int8 path takes zero point 0, or 128 for uint8");
+      }
+    }
+  } else if (!(d.group == d.c && d.c == d.m && w.shape.dims[1] == 1)) {
+    return ie::Error::unsupported("grouped int8 convolution (1 < group < C)");
+  }
+  if (auto st = require_device(); !st.has_value()) return st;
+
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  const int64_t c_store = (d.c + 15) / 16 * 16, m_store = (d.m + 15) / 16 * 16;
+  auto xn = dev_.scratch(kSlotXPacked, static_cast<size_t>(d.n * d.h * d.w * c_store));
+  if (!xn.has_value()) return xn.error();
+  if (auto e = to_status(ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st));
+      !e.has_value()) {
+    return e;
+  }
+  // packed weights, bias and multipliers: uploaded once per host buffer
+  bool fresh = false;
+  const size_t wbytes = depthwise ? ie_cuda_dw_q8_packed_weight_bytes(&d)
+                                  : ie_cuda_q8_packed_weight_bytes(&d);
+  auto wp = dev_.cached(w.buffer, wbytes, kCacheWPacked, &fresh);
+  if (!wp.has_value()) return wp.error();
+  if (fresh) {
+    const void* wsrc = w.buffer;
+    if (w.device != ie::Device::CUDA) {
+      auto tmp = dev_.scratch(kSlotWork, w.bytes());
+      if (!tmp.has_value()) return tmp.error();
+      if (auto e = cuda_status(cudaMemcpyAsync(*tmp, w.buffer, w.bytes(), cudaMemcpyHostToDevice, st),
+                               "cudaMemcpyAsync H2D");
+          !e.has_value()) {
+        return e;
+      }
+      wsrc = *tmp;
+    }
+    const int rc = depthwise ? ie_cuda_dw_q8_pack_weights(&d, static_cast<const int8_t*>(wsrc), *wp, st)
+                             : ie_cuda_q8_pack_weights(&d, static_cast<const int8_t*>(wsrc), *wp, st);
+    if (auto e = to_status(rc); !e.has_value()) return e;
+  }
+  auto md = dev_.cached(mult_.data(), mult_.size() * sizeof(float), kCacheMult, &fresh);
+  if (!md.has_value()) return md.error();
+  if (fresh) {
+    if (auto e = cuda_status(cudaMemcpyAsync(*md, mult_.data(), mult_.size() * sizeof(float),
+                                             cudaMemcpyHostToDevice, st),
+                             "cudaMemcpyAsync H2D");
+        !e.has_value()) {
+      return e;
+    }
+  }
+  const int32_t* bd = nullptr;
+  if (!bias_.empty()) {
+    auto bp = dev_.cached(bias_.data(), bias_.size() * sizeof(int32_t), kCacheBiasI32, &fresh);
+    if (!bp.has_value()) return bp.error();
+    if (fresh) {
+      if (auto e = cuda_status(cudaMemcpyAsync(*bp, bias_.data(), bias_.size() * sizeof(int32_t),
+                                               cudaMemcpyHostToDevice, st),
+                               "cudaMemcpyAsync H2D");
+          !e.has_value()) {
+        return e;
+      }
+    }
+    bd = static_cast<const int32_t*>(*bp);
+  }
+  auto yn = dev_.scratch(kSlotYPacked, static_cast<size_t>(d.n * s.out_h * s.out_w * m_store));
+  if (!yn.has_value()) return yn.error();
+  const int rc = depthwise
+                     ? ie_cuda_dwconv2d_q8(&d, &q, *xn, *wp, bd, static_cast<const float*>(*md), *yn, st)
+                     : ie_cuda_conv2d_q8(&d, &q, *xn, *wp, bd, static_cast<const float*>(*md), *yn, st);
+  if (auto e = to_status(rc); !e.has_value()) return e;
+  const size_t y_bytes = static_cast<size_t>(d.n * d.m * s.out_h * s.out_w);
+  auto yd = dev_.scratch(kSlotY, y_bytes);
+  if (!yd.has_value()) return yd.error();
+  if (auto e = to_status(ie_cuda_q8_unpack_output(*yn, *yd, d.n, d.m, s.out_h, s.out_w, m_store, st));
+      !e.has_value()) {
+    return e;
+  }
+  auto out = ie::Tensor::allocate(ie::Shape{{d.n, d.m, s.out_h, s.out_w}},
+                                  y_signed_ ? ie::DType::I8 : ie::DType::U8, context.allocator);
+  if (!out.has_value()) return out.error();
+  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, *yd, y_bytes, cudaMemcpyDeviceToHost, st),
+                           "cudaMemcpyAsync D2H");
+      !e.has_value()) {
+    return e;
+  }
+  if (auto e = finish(st); !e.has_value()) return e;
+  *outputs[0] = std::move(*out);
+  return {};
+}
+
+ie::Status register_cuda_ops(ie::OpRegistry& registry) {
+  if (auto st = registry.register_op(ie::OpType::Conv2D,
+                                     [] { return std::make_unique<CudaConv2DOp>(false); });
+      !st.has_value()) {
+    return st;
+  }
+  return registry.register_op(ie::OpType::DepthwiseConv2D,
+                              [] { return std::make_unique<CudaConv2DOp>(true); });
+}
+
+}  // namespace ie_b200

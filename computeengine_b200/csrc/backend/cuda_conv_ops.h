@@ -1,0 +1,134 @@
+// CUDA convolution ops behind the reference engine's Op / OpRegistry
+// interface (src/core/ops/op.h:27-54, op_registry.h:15-30).
+//
+//   CudaConv2DOp(false)  replaces Conv2DOp            (conv2d_op.h:36-51)
+//   CudaConv2DOp(true)   replaces DepthwiseConv2DOp   (conv2d_op.h:53-67)
+//   CudaQLinearConv2DOp  int8 convolution the reference plans but does not
+//                        implement (src/converter/quantization/quant_plugins.h:7-22)
+//
+// configure() parses the same attributes with the same error codes as the
+// reference's parse_conv_config (conv2d_op.cpp:26-71).  forward() takes the
+// reference's host NCHW tensors, runs the convolution on the current CUDA
+// device through the C ABI (include/ie_cuda_conv.h), allocates outputs[0]
+// with Tensor::allocate on context.allocator (conv2d_op.cpp:167) and returns
+// only after the result is in host memory.  There is no CPU fallback: without
+// a CUDA device forward() returns Error::Code::Runtime.
+#pragma once
+
+#include <array>
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "ie_cuda_conv.h"
+#include "ie_op_iface.h"
+
+namespace ie_b200 {
+
+enum class AutoPad { NotSet, Valid, SameUpper, SameLower };
+
+// Fields and defaults of the reference ConvConfig (conv2d_op.h:13-21).
+struct ConvConfig {
+  std::array<int64_t, 2> strides{1, 1};
+  std::array<int64_t, 2> dilations{1, 1};
+  std::array<int64_t, 4> pads{0, 0, 0, 0};  // top, left, bottom, right
+  int64_t group{1};
+  AutoPad auto_pad{AutoPad::NotSet};
+  bool has_kernel_shape{false};
+  std::array<int64_t, 2> kernel_shape{0, 0};
+};
+
+// The reference's parse_conv_config with the attrs_util.h readers
+// (read_pair :165-184, read_pads :134-158, read_int, read_auto_pad :109-132,
+// read_int_list): "strides", "dilations", "pads" (2 or 4 values), "group",
+// "auto_pad", "kernel_shape".
+ie::Status parse_conv_config(const ie::Attrs& attrs, ConvConfig& config);
+
+// C ABI status (1 + ie::Error::Code, 0 = OK) -> ie::Status with the library's
+// last error message.
+ie::Status to_status(int rc);
+
+// Device memory owned by one op: weights uploaded (and packed) once per host
+// buffer, scratch buffers that only grow.
+class DeviceBuffers {
+ public:
+  DeviceBuffers() = default;
+  DeviceBuffers(const DeviceBuffers&) = delete;
+  DeviceBuffers& operator=(const DeviceBuffers&) = delete;
+  ~DeviceBuffers();
+  // Scratch slot `slot` with at least `bytes` bytes (256-byte aligned).
+  ie::Result<void*> scratch(int slot, size_t bytes);
+  // Cached device copy for a host buffer; `fresh` tells whether it was just
+  // allocated (and must be filled by the caller).
+  ie::Result<void*> cached(const void* host_key, size_t bytes, int kind, bool* fresh);
+
+ private:
+  struct Block {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+  };
+  std::unordered_map<int, Block> scratch_;
+  struct Key {
+    const void* host;
+    size_t bytes;
+    int kind;
+    bool operator==(const Key& o) const {
+      return host == o.host && bytes == o.bytes && kind == o.kind;
+    }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.host) ^ (k.bytes * 1315423911u) ^ static_cast<size_t>(k.kind);
+    }
+  };
+  std::unordered_map<Key, Block, KeyHash> cache_;
+};
+
+class CudaConv2DOp final : public ie::Op {
+ public:
+  explicit CudaConv2DOp(bool depthwise = false) : depthwise_(depthwise) {}
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+  const ConvConfig& config() const { return config_; }
+
+ private:
+  ConvConfig config_{};
+  bool depthwise_;
+  DeviceBuffers dev_;
+};
+
+// int8 Conv2D (dense or depthwise).  Inputs [x, w]: x U8 or I8 NCHW, w I8
+// [M, C/group, kH, kW].  Attributes: the Conv2D ones plus "multiplier"
+// (per-channel s_x * s_w[m] / s_y, rounded to fp32), "bias" (int32 values as
+// an int list; the reference has no I32 dtype), "x_zero_point",
+// "y_zero_point", "y_signed" and the output clamp "qmin" / "qmax" (ReLU /
+// ReLU6 folded in).  Output U8 or I8 NCHW, bit-exact with the int8 oracle:
+// y = clamp(round_half_away((acc + bias) * multiplier) + y_zero_point).
+class CudaQLinearConv2DOp final : public ie::Op {
+ public:
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  ConvConfig config_{};
+  std::vector<float> mult_;
+  std::vector<int32_t> bias_;
+  int64_t zp_x_ = 0, zp_y_ = 0;
+  bool y_signed_ = false;
+  bool has_qmin_ = false, has_qmax_ = false;
+  int64_t qmin_ = 0, qmax_ = 0;
+  DeviceBuffers dev_;
+};
+
+// Registers CudaConv2DOp for OpType::Conv2D and OpType::DepthwiseConv2D.  Like
+// the reference registry it fails with AlreadyExists when a type is taken, so
+// call it on a fresh (backend-private) registry or before
+// register_builtin_ops, which skips types already present
+// (op_registry.cpp:62-66).
+ie::Status register_cuda_ops(ie::OpRegistry& registry);
+
+}  // namespace ie_b200

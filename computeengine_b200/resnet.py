@@ -234,3 +234,29 @@ class ResNet50Q8:
 
     def replay(self):
         self.graph.replay()
+
+
+def main():
+    """Runs the int8 stack `--steps` times on cuda:0 (uncaptured launches, so a
+    profiler sees each kernel with its own name) and prints one JSON line."""
+    import argparse
+    import json
+
+    import torch
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--steps", type=int, default=1)
+    a = ap.parse_args()
+    layers = resnet50_layers()
+    net = ResNet50Q8(a.batch, make_q8_params(layers))
+    x = torch.from_numpy(make_input_u8(a.batch)).cuda()
+    launches = 0
+    for _ in range(a.steps):
+        launches += net.run(x)
+    torch.cuda.synchronize()
+    print(json.dumps({"batch": a.batch, "steps": a.steps, "launches": launches,
+                      "device_error": net.L.take_device_error()}))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,36 @@
+"""The C++ ops (CudaConv2DOp, its depthwise form, CudaQLinearConv2DOp) driven
+through the reference-shaped Op / OpRegistry interface on host tensors, checked
+against the oracle: fp32 within max|err| <= 1e-3 * max|ref|, int8 bit-exact."""
+import subprocess
+
+import numpy as np
+import pytest
+
+from tests.backend_cpp import driver, read_dump
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+
+
+def test_cpp_ops_match_oracle(oracle, tmp_path):
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+
+    want = oracle.conv2d_f32(t["f32_x"], t["f32_w"], t["f32_b"], pads=(1, 1, 1, 1))
+    err = float(np.abs(t["f32_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
+
+    want = oracle.conv2d_f32(t["dw_x"], t["dw_w"], None, strides=(2, 2), group=32,
+                             auto_pad="SAME_UPPER", depthwise=True)
+    assert t["dw_y"].shape == want.shape
+    err = float(np.abs(t["dw_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
+
+    bias = t["q8_bias"].astype(np.int32)
+    want = oracle.conv2d_q8(t["q8_x"], t["q8_w"], bias, t["q8_mult"], 128, 0, 0, 255,
+                            pads=(1, 1, 1, 1))
+    np.testing.assert_array_equal(t["q8_y"], want)
+    assert (want == 0).any() and (want > 0).mean() > 0.2
