@@ -46,6 +46,11 @@ class Q8Params(C.Structure):
     _fields_ = [(n, _i32) for n in ("x_signed", "zp_x", "y_signed", "zp_y", "qmin", "qmax")]
 
 
+class ConvPlan(C.Structure):
+    _fields_ = [(n, _i32) for n in ("bn", "bk_bytes", "m_sub", "stages", "resident_weights",
+                                    "out_bufs", "row_band", "grid")]
+
+
 class CudaConvError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"{STATUS_NAMES.get(code, code)}: {message}")
@@ -86,6 +91,7 @@ def _load() -> C.CDLL:
         "ie_cuda_last_error": (C.c_char_p, []),
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
+        "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -111,3 +117,10 @@ def take_device_error() -> int:
 
 def launch_count(reset: bool = False) -> int:
     return int(lib.ie_cuda_launch_count(1 if reset else 0))
+
+
+def last_plan() -> ConvPlan:
+    """Tile plan of this thread's last implicit-GEMM launch."""
+    p = ConvPlan()
+    check(lib.ie_cuda_last_plan(p))
+    return p

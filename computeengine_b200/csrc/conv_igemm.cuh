@@ -76,6 +76,17 @@ struct IgemmArgs {
   void* y;
   int64_t y_ld;       // elements between consecutive output pixels
   int64_t acc_bound;  // int8 path: bound on |accumulator| (K * 255 * 128)
+  // Row-band mode (int8, stride 1, resident weights): a tile is rows_t whole
+  // output rows of a position space whose rows are wp = w + pad_l + pad_r wide,
+  // so every filter tap reads the same input band shifted by
+  // ky * dil_h * wp + kx * dil_w positions; one tiled TMA load per channel
+  // block brings the band (rows_box input rows, padding read as zero) and the
+  // taps become shifted MMA operand descriptors.  Positions with
+  // ox >= out_w are computed and never stored.
+  int32_t halo;
+  int32_t wp, rows_t, rows_box, tiles_img;
+  int32_t stage_bytes;  // shared memory per stage (band + slack for the shifted reads)
+  int32_t band_bytes;   // bytes one band load delivers
 };
 
 __host__ __device__ constexpr uint32_t swizzle_layout_code(int row_bytes) {
@@ -383,8 +394,9 @@ struct IgemmPlan {
   static_assert(kColGroups >= 1 && EPI_WARPS == 4 * M_SUB * kColGroups, "epilogue warps");
   static_assert(kWarpCols >= 32 && kWarpCols % 32 == 0, "epilogue columns per warp");
   // dynamic smem for `stages` pipeline stages and `num_k` resident weight steps
-  static constexpr int bytes(int stages, int num_k, int out_bufs) {
-    return 1024 + stages * kStage + (B_RES ? kParts * num_k * kB : 0) + out_bufs * kOutTile +
+  // stage_bytes: kStage, or the row-band mode's per-stage size
+  static constexpr int bytes(int stages, int num_k, int out_bufs, int stage_bytes) {
+    return 1024 + stages * stage_bytes + (B_RES ? kParts * num_k * kB : 0) + out_bufs * kOutTile +
            kConstBytes + kBarBytes;
   }
 };
@@ -419,8 +431,10 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = args.stages;
+  const bool halo = KIND_I8 && B_RES && args.halo != 0;
+  const int stage_bytes = halo ? args.stage_bytes : kStage;
   uint8_t* stage_base = smem;
-  uint8_t* b_res = stage_base + stages * kStage;  // resident weights (B_RES)
+  uint8_t* b_res = stage_base + stages * stage_bytes;  // resident weights (B_RES)
   uint8_t* out_stage = b_res + (B_RES ? kParts * args.num_k * kB : 0);  // [out_bufs]
   uint8_t* const_base = out_stage + args.out_bufs * P::kOutTile;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(const_base + P::kConstBytes);
@@ -515,6 +529,27 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       bool ok = true;
       int m_tile, n_tile;
       for (int j = 0; ok && tile_of(j, &m_tile, &n_tile); ++j) {
+        if constexpr (KIND_I8 && B_RES) {
+          if (halo) {
+            const int32_t img = m_tile / args.tiles_img;
+            const int32_t oy0 = (m_tile - img * args.tiles_img) * args.rows_t;
+            for (int cb = 0; cb < args.cblocks; ++cb, ++kiter) {
+              if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, kErrWaitEmpty)) {
+                ok = false;
+                break;
+              }
+              uint8_t* st = stage_base + s * stage_bytes;
+              mbar_arrive_expect_tx(&full_bar[s], args.band_bytes);
+              tma_load_4d(st, &tmap_a, &full_bar[s], cb * kBkElems, -args.pad_l,
+                          oy0 - args.pad_t, img);
+              if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+            continue;
+          }
+        }
         const int64_t p0 = static_cast<int64_t>(m_tile) * P::kRows;
         const int32_t img = static_cast<int32_t>(p0 / hw_out);
         const int32_t rem = static_cast<int32_t>(p0 - static_cast<int64_t>(img) * hw_out);
@@ -528,7 +563,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
             ok = false;
             break;
           }
-          uint8_t* st = stage_base + s * kStage;
+          uint8_t* st = stage_base + s * stage_bytes;
           mbar_arrive_expect_tx(&full_bar[s], kStage);
           const uint16_t offw = static_cast<uint16_t>(kx * args.dil_w);
           const uint16_t offh = static_cast<uint16_t>(ky * args.dil_h);
@@ -565,6 +600,9 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
+      // Operand descriptors are built once per buffer and advanced by adding
+      // (byte offset >> 4) to their address field (shared-memory addresses
+      // stay below 2^18, so the 14-bit field never carries).
       uint32_t kiter = 0;
       int s = 0;
       uint32_t ph = 0;
@@ -572,6 +610,8 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       if constexpr (B_RES) {
         ok = mbar_wait(bres_bar, 0, abort_flag, kErrWaitWeights);
       }
+      const uint64_t stage_desc0 = make_smem_desc(smem_u32(stage_base), 16, kSbo, kLayout);
+      const uint64_t bres_desc0 = make_smem_desc(smem_u32(b_res), 16, kSbo, kLayout);
       int m_tile, n_tile;
       for (int j = 0; ok && tile_of(j, &m_tile, &n_tile); ++j) {
         const int buf = j & 1;
@@ -579,27 +619,75 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
         if (!mbar_wait(&acce_bar[buf], aph ^ 1u, abort_flag, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * P::kAccCols;
+        if constexpr (KIND_I8 && B_RES) {
+          if (halo) {
+            // Tap (ky, kx) reads the band shifted by ky * dil_h * wp + kx *
+            // dil_w rows.  Such a start is in general not a multiple of 8
+            // rows: the tensor core applies the swizzle XOR from the absolute
+            // shared-memory address bits, as the TMA unit wrote them, so the
+            // plain start address places the operand (matrix base offset 0;
+            // measured on B200 for the 32-, 64- and 128-byte swizzles, at
+            // full MMA rate).
+            const int taps = args.kh * args.kw;
+            const int row_jump = args.dil_h * args.wp - args.kw * args.dil_w;
+            const uint64_t tap_b_step = static_cast<uint64_t>(args.cblocks * kB) >> 4;
+            for (int cb = 0; cb < args.cblocks; ++cb, ++kiter) {
+              if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t a_st = stage_desc0 + (static_cast<uint64_t>(s * stage_bytes) >> 4);
+              uint64_t b_tap = bres_desc0 + (static_cast<uint64_t>(cb * kB) >> 4);
+              int shift = 0, kx = 0;
+              for (int tap = 0; tap < taps; ++tap) {
+                const uint64_t a_tap = a_st + static_cast<uint64_t>(shift * (BK_BYTES / 16));
+#pragma unroll
+                for (int kk = 0; kk < BK_BYTES / kKStep; ++kk) {
+#pragma unroll
+                  for (int sub = 0; sub < M_SUB; ++sub) {
+                    mma_i8(d_tmem + sub * BN, a_tap + ((sub * 128 * BK_BYTES + kk * kKStep) >> 4),
+                           b_tap + ((kk * kKStep) >> 4), kIdesc, kk != 0 || ((cb | tap) != 0));
+                  }
+                }
+                b_tap += tap_b_step;
+                shift += args.dil_w;
+                if (++kx == args.kw) {
+                  kx = 0;
+                  shift += row_jump;
+                }
+              }
+              tc_commit(&empty_bar[s]);
+              if (++s == stages) {
+                s = 0;
+                ph ^= 1u;
+              }
+            }
+            if (ok) tc_commit(&accf_bar[buf]);
+            continue;
+          }
+        }
         for (int k = 0; k < args.num_k; ++k, ++kiter) {
           if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(stage_base + s * kStage);
-          const uint32_t sb = B_RES ? smem_u32(b_res + k * kParts * kB) : sa + kParts * kA;
+          const uint64_t a_st = stage_desc0 + (static_cast<uint64_t>(s * stage_bytes) >> 4);
+          const uint64_t b_k = B_RES ? bres_desc0 + (static_cast<uint64_t>(k * kParts * kB) >> 4)
+                                     : a_st + ((kParts * kA) >> 4);
 #pragma unroll
           for (int kk = 0; kk < BK_BYTES / kKStep; ++kk) {
-            const uint64_t bd = make_smem_desc(sb + kk * kKStep, 16, kSbo, kLayout);
+            const uint64_t bd = b_k + ((kk * kKStep) >> 4);
 #pragma unroll
             for (int sub = 0; sub < M_SUB; ++sub) {
-              const uint32_t a_off = sa + sub * 128 * BK_BYTES + kk * kKStep;
-              const uint64_t ad = make_smem_desc(a_off, 16, kSbo, kLayout);
+              const uint64_t ad = a_st + ((sub * 128 * BK_BYTES + kk * kKStep) >> 4);
               const uint32_t d = d_tmem + sub * BN;
               if constexpr (KIND_I8) {
                 mma_i8(d, ad, bd, kIdesc, (k | kk) != 0);
               } else {
-                const uint64_t adl = make_smem_desc(a_off + kA, 16, kSbo, kLayout);
-                const uint64_t bdl = make_smem_desc(sb + kB + kk * kKStep, 16, kSbo, kLayout);
+                const uint64_t adl = ad + (kA >> 4);
+                const uint64_t bdl = bd + (kB >> 4);
                 mma_f16(d, ad, bd, kIdesc, (k | kk) != 0);
                 mma_f16(d, ad, bdl, kIdesc, 1);
                 mma_f16(d, adl, bd, kIdesc, 1);
@@ -634,10 +722,20 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
         if (!mbar_wait(&ofull_bar[ob], oph, abort_flag, kErrWaitOutFull)) break;
         const uint8_t* s_tile = out_stage + ob * P::kOutTile;
         const int32_t row0 = m_tile * P::kRows;
+        const int32_t img = halo ? m_tile / args.tiles_img : 0;
+        const int32_t oy0 = halo ? (m_tile - img * args.tiles_img) * args.rows_t : 0;
 #pragma unroll
         for (int p = 0; p < P::kPanels; ++p) {
           const int32_t col = n_tile * BN + p * P::kPanelW;
-          if (col < args.y_ld) tma_store_2d(&tmap_y, s_tile + p * P::kRows * P::kPanelW, col, row0);
+          if (col >= args.y_ld) continue;
+          const uint8_t* panel = s_tile + p * P::kRows * P::kPanelW;
+          if (halo) {
+            // rows_t x wp positions; columns ox >= out_w fall outside the
+            // tensor and are not written
+            tma_store_4d(&tmap_y, panel, col, 0, oy0, img);
+          } else {
+            tma_store_2d(&tmap_y, panel, col, row0);
+          }
         }
         bulk_commit_group();
         bulk_wait_group_read0();  // the staged tile may be overwritten

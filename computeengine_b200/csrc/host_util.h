@@ -123,6 +123,33 @@ inline int encode_im2col(CUtensorMap* map, const void* base, CUtensorMapDataType
   return IE_OK;
 }
 
+// 4D tiled descriptor over an NHWC tensor [n, h, w, c_elems]; box = box_c x
+// box_w x box_h x 1 (channels innermost), swizzled by the box's channel bytes.
+inline int encode_nhwc_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                          int elem_bytes, int64_t n, int64_t h, int64_t w, int64_t c_elems,
+                          int box_c, int box_w, int box_h) {
+  const DriverFns& f = driver_fns();
+  if (!f.ok) return fail(IE_RUNTIME, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(c_elems), static_cast<cuuint64_t>(w),
+                              static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(n)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(c_elems * elem_bytes),
+                                 static_cast<cuuint64_t>(w * c_elems * elem_bytes),
+                                 static_cast<cuuint64_t>(h * w * c_elems * elem_bytes)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(box_c), static_cast<cuuint32_t>(box_w),
+                             static_cast<cuuint32_t>(box_h), 1};
+  const cuuint32_t estrides[4] = {1, 1, 1, 1};
+  const CUresult r = f.tiled(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estrides,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_c * elem_bytes),
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(IE_RUNTIME,
+                "cuTensorMapEncodeTiled (4D) failed (%d): n=%lld h=%lld w=%lld c=%lld box=%dx%dx%d",
+                static_cast<int>(r), static_cast<long long>(n), static_cast<long long>(h),
+                static_cast<long long>(w), static_cast<long long>(c_elems), box_c, box_w, box_h);
+  }
+  return IE_OK;
+}
+
 // 2D tiled descriptor over a row-major [rows, cols] matrix; box = box_rows x
 // box_cols elements.
 inline int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,

@@ -128,7 +128,8 @@ constexpr int kSmemLimit = 227 * 1024;
 // One compiled variant of the implicit-GEMM kernel.
 struct Variant {
   int bn, bkb, m_sub, epi;
-  int out_bufs;  // staged requantized output tiles (int8 path), 0 otherwise
+  int out_bufs;    // staged requantized output tiles (int8 path), 0 otherwise
+  int halo_stage;  // row-band mode: bytes per stage; 0 = im2col mode
   bool b_res, i8, a_signed;
 };
 
@@ -137,7 +138,9 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
                    const IgemmArgs& args, int grid, cudaStream_t st) {
   using P = IgemmPlan<BN, BKB, EPI, MSUB, BRES, I8>;
   auto kern = conv_igemm_kernel<BN, BKB, EPI, MSUB, BRES, I8, AS>;
-  const int smem = P::bytes(args.stages, args.num_k, args.out_bufs);
+  if (args.halo && !(I8 && BRES)) return fail(IE_RUNTIME, "row-band mode needs resident int8 weights");
+  const int smem = P::bytes(args.stages, args.num_k, args.out_bufs,
+                            args.halo ? args.stage_bytes : P::kStage);
   if (smem > kSmemLimit) return fail(IE_UNSUPPORTED, "shared memory plan too large (%d)", smem);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -196,7 +199,7 @@ int plan_bytes(const Variant& v, int stages, int num_k) {
   const int parts = v.i8 ? 1 : 2;
   const int rows = 128 * v.m_sub;
   const int ka = rows * v.bkb, kb = v.bn * v.bkb;
-  const int stage = parts * (ka + (v.b_res ? 0 : kb));
+  const int stage = v.halo_stage > 0 ? v.halo_stage : parts * (ka + (v.b_res ? 0 : kb));
   const int warp_cols = v.bn / (v.epi / (4 * v.m_sub));
   const int out_tile = v.i8 ? rows * v.bn : 0;
   const int consts = v.epi * warp_cols * 12;
@@ -214,10 +217,14 @@ struct IgemmSetup {
 
 // Shared set-up of the implicit GEMM for both element kinds.
 //   elem_bytes: 1 (int8) or 2 (bf16; activation and weights hold hi|lo planes)
+//   allow_halo: the caller's output goes through the staged TMA store (int8
+//   requantized), so the row-band mode may be used
 int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
-                int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out) {
+                int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out,
+                bool allow_halo = false) {
   const bool i8 = elem_bytes == 1;
   Variant& v = out->v;
+  v = Variant{};
   v.i8 = i8;
   v.bn = choose_bn(d->m);
   v.bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(v.bn, i8));
@@ -263,26 +270,73 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   if (plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) {
     return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
   }
-  // TMA im2col corner limits for 4D tensors: [-128, 127]; offsets < 256.
-  const int64_t lower_w = -s.pad_left, lower_h = -s.pad_top;
-  const int64_t upper_w = s.pad_right - (d->kw - 1) * d->dil_w;
-  const int64_t upper_h = s.pad_bottom - (d->kh - 1) * d->dil_h;
-  for (int64_t val : {lower_w, lower_h, upper_w, upper_h}) {
-    if (val < -128 || val > 127) {
-      return fail(IE_UNSUPPORTED, "padding / kernel extent too large for TMA im2col");
-    }
-  }
-  if ((d->kw - 1) * d->dil_w > 255 || (d->kh - 1) * d->dil_h > 255 || d->stride_h > 8 ||
-      d->stride_w > 8) {
-    return fail(IE_UNSUPPORTED, "kernel extent or stride too large for TMA im2col");
+  // Row-band mode for stride-1 multi-tap int8 convolutions: tiles of whole
+  // output rows in a (w + pad_l + pad_r)-wide position space, one band load
+  // per channel block.  Used when the rows fill the tiles well and the
+  // natural tile width keeps the weights resident with at least 3 stages
+  // (measured: narrowing the tiles to make the weights fit costs more than
+  // the band saves).
+  int64_t h_wp = 0, h_rows_t = 0, h_rows_box = 0, h_tiles_img = 0, h_band = 0;
+  if (allow_halo && i8 && d->stride_h == 1 && d->stride_w == 1 && taps > 1) {
+    const int64_t wp = d->w + s.pad_left + s.pad_right;
+    do {
+      Variant hv = v;
+      hv.b_res = true;
+      hv.out_bufs = 2;
+      const int64_t rows = 128 * hv.m_sub;
+      const int64_t rows_t = rows / wp;
+      if (rows_t < 1 || wp > 256) break;
+      const int64_t tiles_img = ceil_div(s.out_h, rows_t);
+      const double fill = static_cast<double>(s.out_h * s.out_w) / static_cast<double>(tiles_img * rows);
+      const int64_t rows_box = rows_t + (d->kh - 1) * d->dil_h;
+      const int64_t slack = (d->kh - 1) * d->dil_h * wp + (d->kw - 1) * d->dil_w;
+      hv.halo_stage = static_cast<int>(round_up(round_up(rows + slack, 8) * v.bkb, 1024));
+      if (fill < 0.7 || rows_box > 256) break;
+      int st = kMaxStages;
+      while (st > 3 && plan_bytes(hv, st, static_cast<int>(num_k)) > kSmemLimit) --st;
+      if (plan_bytes(hv, st, static_cast<int>(num_k)) > kSmemLimit) {
+        hv.out_bufs = 1;
+        st = kMaxStages;
+        while (st > 3 && plan_bytes(hv, st, static_cast<int>(num_k)) > kSmemLimit) --st;
+        if (plan_bytes(hv, st, static_cast<int>(num_k)) > kSmemLimit) break;
+      }
+      v = hv;
+      stages = st;
+      h_wp = wp;
+      h_rows_t = rows_t;
+      h_rows_box = rows_box;
+      h_tiles_img = tiles_img;
+      h_band = rows_box * wp * v.bkb;
+    } while (false);
   }
   const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t a_chan = i8 ? x_c_store : 2 * x_c_store;
-  int rc = encode_im2col(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
-                         static_cast<int>(bk_elems), 128 * v.m_sub, static_cast<int>(lower_w),
-                         static_cast<int>(lower_h), static_cast<int>(upper_w),
-                         static_cast<int>(upper_h), static_cast<int>(d->stride_w),
-                         static_cast<int>(d->stride_h));
+  int rc;
+  if (h_wp > 0) {
+    // band box: bk channels x wp columns (from -pad_left) x rows_box rows
+    rc = encode_nhwc_4d(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
+                        static_cast<int>(bk_elems), static_cast<int>(h_wp),
+                        static_cast<int>(h_rows_box));
+  } else {
+    // TMA im2col corner limits for 4D tensors: [-128, 127]; offsets < 256.
+    const int64_t lower_w = -s.pad_left, lower_h = -s.pad_top;
+    const int64_t upper_w = s.pad_right - (d->kw - 1) * d->dil_w;
+    const int64_t upper_h = s.pad_bottom - (d->kh - 1) * d->dil_h;
+    for (int64_t val : {lower_w, lower_h, upper_w, upper_h}) {
+      if (val < -128 || val > 127) {
+        return fail(IE_UNSUPPORTED, "padding / kernel extent too large for TMA im2col");
+      }
+    }
+    if ((d->kw - 1) * d->dil_w > 255 || (d->kh - 1) * d->dil_h > 255 || d->stride_h > 8 ||
+        d->stride_w > 8) {
+      return fail(IE_UNSUPPORTED, "kernel extent or stride too large for TMA im2col");
+    }
+    rc = encode_im2col(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
+                       static_cast<int>(bk_elems), 128 * v.m_sub, static_cast<int>(lower_w),
+                       static_cast<int>(lower_h), static_cast<int>(upper_w),
+                       static_cast<int>(upper_h), static_cast<int>(d->stride_w),
+                       static_cast<int>(d->stride_h));
+  }
   if (rc != IE_OK) return rc;
   const int64_t b_cols = taps * ck * (i8 ? 1 : 2);
   rc = encode_2d(&out->tb, packed, dt, elem_bytes, d->m, b_cols, static_cast<int>(bk_elems), v.bn);
@@ -315,6 +369,16 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   a.acc_bound = d->kh * d->kw * d->c * 255 * 128;
   a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128 * v.m_sub));
   a.n_tiles = static_cast<int32_t>(ceil_div(d->m, v.bn));
+  if (h_wp > 0) {
+    a.halo = 1;
+    a.wp = static_cast<int32_t>(h_wp);
+    a.rows_t = static_cast<int32_t>(h_rows_t);
+    a.rows_box = static_cast<int32_t>(h_rows_box);
+    a.tiles_img = static_cast<int32_t>(h_tiles_img);
+    a.stage_bytes = v.halo_stage;
+    a.band_bytes = static_cast<int32_t>(h_band);
+    a.m_tiles = static_cast<int32_t>(d->n * h_tiles_img);
+  }
   const int sms = num_sms();
   if (v.b_res) {
     // each CTA keeps one n_tile: the grid is a multiple of n_tiles
@@ -350,7 +414,17 @@ int check_ptr(const void* p, const char* what, size_t align) {
   return IE_OK;
 }
 
+thread_local ie_conv_plan g_last_plan{};
+
 int launch_setup(IgemmSetup& su, bool a_signed, cudaStream_t st) {
+  g_last_plan.bn = su.v.bn;
+  g_last_plan.bk_bytes = su.v.bkb;
+  g_last_plan.m_sub = su.v.m_sub;
+  g_last_plan.stages = su.args.stages;
+  g_last_plan.resident_weights = su.v.b_res ? 1 : 0;
+  g_last_plan.out_bufs = su.v.out_bufs;
+  g_last_plan.row_band = su.args.halo;
+  g_last_plan.grid = su.grid;
   LaunchFn fn = su.v.i8 ? (a_signed ? pick_launch<true, true>(su.v) : pick_launch<true, false>(su.v))
                         : pick_launch<false, false>(su.v);
   if (fn == nullptr) {
@@ -383,7 +457,9 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   if (out_mode != kOutS32 && mult == nullptr) return fail(IE_INVALID_ARGUMENT, "mult is null");
   const int64_t c_store = round_up(d->c, 16);
   IgemmSetup su;
-  if ((rc = setup_igemm(d, s, 1, c_store, x, packed, &su)) != IE_OK) return rc;
+  if ((rc = setup_igemm(d, s, 1, c_store, x, packed, &su, out_mode != kOutS32)) != IE_OK) {
+    return rc;
+  }
   IgemmArgs& a = su.args;
   a.bias_i32 = bias;
   a.mult = mult;
@@ -397,8 +473,16 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
     // the store warp writes each staged tile as panels of up to 128 channels
     // x 128 * m_sub rows
     const int panel = std::min(su.v.bn, 128);
-    if ((rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld, panel,
-                        128 * su.v.m_sub)) != IE_OK) {
+    if (a.halo) {
+      // rows_t output rows x wp positions per tile; positions past out_w are
+      // outside the tensor and the TMA store skips them
+      rc = encode_nhwc_4d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, d->n, s.out_h, s.out_w,
+                          a.y_ld, panel, a.wp, a.rows_t);
+    } else {
+      rc = encode_2d(&su.ty, y, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m_total, a.y_ld, panel,
+                     128 * su.v.m_sub);
+    }
+    if (rc != IE_OK) {
       return rc;
     }
   } else {
@@ -459,6 +543,12 @@ int ie_conv2d_resolve(const ie_conv2d_desc* desc, int64_t bias_len, ie_conv2d_sh
 }
 
 const char* ie_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int ie_cuda_last_plan(ie_conv_plan* out) {
+  if (out == nullptr) return fail(IE_INVALID_ARGUMENT, "null plan");
+  *out = g_last_plan;
+  return IE_OK;
+}
 
 uint64_t ie_cuda_launch_count(int reset) {
   const uint64_t v = g_launches;

@@ -252,6 +252,22 @@ int ie_cuda_take_device_error(uint32_t* code);
  * since the last reset (for the benchmark's launch count). */
 uint64_t ie_cuda_launch_count(int reset);
 
+/* Tile plan of the last implicit-GEMM launch issued on the calling host thread
+ * (performance introspection; no counterpart in the reference).  row_band is 1
+ * when the stride-1 row-band mode ran: tiles of whole output rows, one input
+ * band load per channel block, filter taps as shifted operand reads. */
+typedef struct {
+  int32_t bn;             /* output channels per tile */
+  int32_t bk_bytes;       /* K bytes per pipeline step */
+  int32_t m_sub;          /* 128-row sub-tiles per tile */
+  int32_t stages;         /* pipeline depth */
+  int32_t resident_weights;
+  int32_t out_bufs;       /* staged output tiles (int8 requantized output) */
+  int32_t row_band;
+  int32_t grid;           /* CTAs launched */
+} ie_conv_plan;
+int ie_cuda_last_plan(ie_conv_plan* out);
+
 #ifdef __cplusplus
 }
 #endif

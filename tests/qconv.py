@@ -34,7 +34,8 @@ def desc_for(L, n, c, h, w, m, kh, kw, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1,
 
 
 def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1),
-                    zp_x=128, zp_y=0, qmin=0, qmax=255, raw_acc=False, device="cuda"):
+                    zp_x=128, zp_y=0, qmin=0, qmax=255, raw_acc=False, device="cuda",
+                    y_signed=False):
     """Runs ie_cuda_conv2d_q8 (or _acc) on NCHW host arrays, returns NCHW host output."""
     import torch
     from computeengine_b200 import _lib as L
@@ -50,7 +51,7 @@ def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=
     x_dev = torch.from_numpy(np.ascontiguousarray(x)).to(device)
     x_nhwc = torch.zeros((n, h, w, c_store), dtype=torch.uint8, device=device)
     q = L.Q8Params()
-    q.y_signed, q.zp_y, q.qmin, q.qmax = 0, zp_y, qmin, qmax
+    q.y_signed, q.zp_y, q.qmin, q.qmax = int(y_signed), zp_y, qmin, qmax
     if x.dtype == np.uint8 and zp_x == 128:
         xor, q.x_signed, q.zp_x = 0x80, 1, 0
     else:
@@ -75,4 +76,5 @@ def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=
                                         m_dev.data_ptr(), y.data_ptr(), stream))
     torch.cuda.synchronize()
     assert L.take_device_error() == 0
-    return y[..., :m].permute(0, 3, 1, 2).contiguous().cpu().numpy()
+    out = y[..., :m].permute(0, 3, 1, 2).contiguous().cpu().numpy()
+    return out.view(np.int8) if (y_signed and not raw_acc) else out
