@@ -225,12 +225,50 @@ def benchmark(batch: int = 64, iters: int = 50) -> dict:
             "algorithmic_gbs": by["all"] * batch / ms / 1e6, "launches": net.launches}
 
 
+def layer_times(batch: int = 64, iters: int = 20) -> List[dict]:
+    """Times every launch of the sweep on its own (CUDA events around each
+    launch, averaged over `iters` passes); bytes are the algorithmic bytes of
+    that layer (input + output once)."""
+    import torch
+    layers = mobilenetv2_layers()
+    net = MobileNetV2Q8(batch, make_params(layers))
+    x = torch.from_numpy(make_input(batch)).cuda()
+    L = net.L
+    stream = torch.cuda.current_stream().cuda_stream
+    net.run(x)
+    torch.cuda.synchronize()
+    out = []
+    for l in layers:
+        src = net.x_nhwc if l.src == "input" else net.acts[l.src]
+        fn = L.lib.ie_cuda_dwconv2d_q8 if l.kind == "dw" else L.lib.ie_cuda_conv2d_q8
+        args = (net.descs[l.name], net.qp[l.name], src.data_ptr(), net.packed[l.name].data_ptr(),
+                net.bias[l.name].data_ptr(), net.mult[l.name].data_ptr(),
+                net.acts[l.name].data_ptr(), stream)
+        for _ in range(3):
+            L.check(fn(*args))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            L.check(fn(*args))
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / iters
+        by = batch * (l.h * l.h * _c16(l.cin) + l.out_h * l.out_h * _c16(l.cout))
+        out.append({"layer": l.name, "kind": l.kind, "cin": l.cin, "cout": l.cout, "h": l.h,
+                    "stride": l.stride, "us": us, "gbs": by / us / 1e3})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--layers", action="store_true", help="also time each launch on its own")
     a = ap.parse_args()
     print(json.dumps(benchmark(a.batch, a.iters)))
+    if a.layers:
+        for r in layer_times(a.batch):
+            print(json.dumps(r))
 
 
 if __name__ == "__main__":

@@ -79,3 +79,55 @@ def test_depthwise_signed_output_general_zero_point(oracle):
     want = oracle.conv2d_q8(x, wq, bias, mult, 100, -3, -128, 127, y_signed=True, pads=(1,) * 4,
                             group=64, depthwise=True)
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("mult_range,zp_y,qmin,qmax,y_signed", [
+    ((0.25, 0.9), 0, 0, 255, False),       # shifts <= 32: exact per-column requantize
+    ((0.001, 0.01), 0, -128, 127, True),    # zp_y > qmin: sign-corrected rounding
+    ((0.001, 0.01), 3, 3, 100, False),      # folded addend with a narrower clamp
+])
+def test_depthwise_requantize_modes(oracle, mult_range, zp_y, qmin, qmax, y_signed):
+    rng = np.random.default_rng(17)
+    c = 80
+    x = rng.integers(0, 256, (2, c, 17, 19)).astype(np.uint8)
+    wq = rng.integers(-127, 128, (c, 1, 3, 3)).astype(np.int8)
+    bias = rng.integers(-3000, 3000, c).astype(np.int32)
+    mult = rng.uniform(*mult_range, c).astype(np.float32)
+    mult[::7] = 0.125  # exact .5 ties
+    scale = 0.02 if mult_range[0] >= 0.25 else 1.0
+    mult = (mult * scale).astype(np.float32)
+    got = run_dw_gpu(x, wq, bias, mult, stride=1, pad=1, zp_x=20, zp_y=zp_y, qmin=qmin, qmax=qmax,
+                     y_signed=y_signed)
+    want = oracle.conv2d_q8(x, wq, bias, mult, 20, zp_y, qmin, qmax, y_signed=y_signed,
+                            pads=(1,) * 4, group=c, depthwise=True)
+    np.testing.assert_array_equal(got, want)
+    assert (want == qmin).any() and (want == qmax).any()
+
+
+def test_depthwise_zero_point_outside_input_type(oracle):
+    """A zero point no uint8 value can hold takes the general per-pixel kernel."""
+    rng = np.random.default_rng(4)
+    c = 48
+    x = rng.integers(0, 256, (1, c, 10, 12)).astype(np.uint8)
+    wq = rng.integers(-127, 128, (c, 1, 3, 3)).astype(np.int8)
+    bias = rng.integers(-2000, 2000, c).astype(np.int32)
+    mult = rng.uniform(0.0005, 0.002, c).astype(np.float32)
+    got = run_dw_gpu(x, wq, bias, mult, stride=2, pad=1, zp_x=-20, zp_y=0, qmin=0, qmax=255)
+    want = oracle.conv2d_q8(x, wq, bias, mult, -20, 0, 0, 255, strides=(2, 2), pads=(1,) * 4,
+                            group=c, depthwise=True)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_depthwise_wide_rows_5x5_stride2(oracle):
+    """Several 4-pixel steps per row, a ragged last step, 5x5 stride 2."""
+    rng = np.random.default_rng(8)
+    c = 112
+    x = rng.integers(-128, 128, (2, c, 31, 45)).astype(np.int8)
+    wq = rng.integers(-127, 128, (c, 1, 5, 5)).astype(np.int8)
+    bias = rng.integers(-2000, 2000, c).astype(np.int32)
+    mult = rng.uniform(0.0005, 0.004, c).astype(np.float32)
+    got = run_dw_gpu(x, wq, bias, mult, stride=2, pad=2, zp_x=-7, zp_y=0, qmin=0, qmax=120)
+    want = oracle.conv2d_q8(x, wq, bias, mult, -7, 0, 0, 120, strides=(2, 2), pads=(2,) * 4,
+                            group=c, depthwise=True)
+    np.testing.assert_array_equal(got, want)
+    assert (want == 0).any() and (want == 120).any()
