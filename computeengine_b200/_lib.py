@@ -92,6 +92,7 @@ def _load() -> C.CDLL:
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
         "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
+        "ie_cuda_f32x2_maxpool2d": (C.c_int, [_p, _p] + [_i64] * 7 + [_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

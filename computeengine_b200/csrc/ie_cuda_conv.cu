@@ -776,6 +776,27 @@ int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w
   return check_launch("maxpool_q8_nhwc");
 }
 
+int ie_cuda_f32x2_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,
+                            int64_t c_store, int64_t k, int64_t stride, int64_t pad,
+                            void* stream) {
+  int rc;
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  if (n <= 0 || h <= 0 || w <= 0 || c_store <= 0 || c_store % 16 || k <= 0 || stride <= 0 ||
+      pad < 0 || pad >= k) {
+    return fail(IE_INVALID_ARGUMENT, "bad pooling shape");
+  }
+  const int64_t oh = (h + 2 * pad - k) / stride + 1, ow = (w + 2 * pad - k) / stride + 1;
+  if (oh <= 0 || ow <= 0) return fail(IE_INVALID_ARGUMENT, "pooling produces an empty output");
+  const int64_t total = n * oh * ow * (c_store / 8);
+  maxpool_f32x2_nhwc<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y),
+      static_cast<int32_t>(n), static_cast<int32_t>(h), static_cast<int32_t>(w),
+      static_cast<int32_t>(c_store), static_cast<int32_t>(oh), static_cast<int32_t>(ow),
+      static_cast<int32_t>(k), static_cast<int32_t>(stride), static_cast<int32_t>(pad));
+  return check_launch("maxpool_f32x2_nhwc");
+}
+
 // -------------------------------------------------------------- fp32
 
 size_t ie_cuda_f32_packed_weight_bytes(const ie_conv2d_desc* desc) {

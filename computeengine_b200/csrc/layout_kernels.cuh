@@ -210,6 +210,56 @@ __global__ void stem_pack_weights_q8(const int8_t* __restrict__ w, int8_t* __res
 
 // Max pooling over 8-bit NHWC activations, 16 channels per thread; windows
 // only cover real pixels (padding never wins).
+// Max pooling over split fp32 activations: bf16 NHWC with [hi plane (c_store)
+// | lo plane (c_store)] per pixel.  The pair with the largest hi + lo (exact
+// in fp32) is copied, so the pool keeps the stored values bit for bit.  One
+// thread per output pixel x 8 channels; padding never wins.
+__global__ void maxpool_f32x2_nhwc(const __nv_bfloat16* __restrict__ x,
+                                   __nv_bfloat16* __restrict__ y, int32_t n, int32_t h, int32_t w,
+                                   int32_t c_store, int32_t oh, int32_t ow, int32_t k,
+                                   int32_t stride, int32_t pad) {
+  const int32_t groups = c_store >> 3;
+  const int64_t total = static_cast<int64_t>(n) * oh * ow * groups;
+  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= total) return;
+  const int32_t g = static_cast<int32_t>(idx % groups);
+  const int64_t pix = idx / groups;
+  const int32_t ox = static_cast<int32_t>(pix % ow);
+  const int32_t oy = static_cast<int32_t>((pix / ow) % oh);
+  const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(ow) * oh));
+  float best[8];
+  uint4 bh = make_uint4(0, 0, 0, 0), bl = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) best[j] = -INFINITY;
+  for (int ky = 0; ky < k; ++ky) {
+    const int32_t iy = oy * stride - pad + ky;
+    if (iy < 0 || iy >= h) continue;
+    for (int kx = 0; kx < k; ++kx) {
+      const int32_t ix = ox * stride - pad + kx;
+      if (ix < 0 || ix >= w) continue;
+      const __nv_bfloat16* px = x + ((static_cast<int64_t>(img) * h + iy) * w + ix) * 2 * c_store;
+      const uint4 vh = __ldg(reinterpret_cast<const uint4*>(px + g * 8));
+      const uint4 vl = __ldg(reinterpret_cast<const uint4*>(px + c_store + g * 8));
+      const __nv_bfloat16* hh = reinterpret_cast<const __nv_bfloat16*>(&vh);
+      const __nv_bfloat16* ll = reinterpret_cast<const __nv_bfloat16*>(&vl);
+      __nv_bfloat16* bhh = reinterpret_cast<__nv_bfloat16*>(&bh);
+      __nv_bfloat16* bll = reinterpret_cast<__nv_bfloat16*>(&bl);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = __bfloat162float(hh[j]) + __bfloat162float(ll[j]);
+        if (v > best[j]) {
+          best[j] = v;
+          bhh[j] = hh[j];
+          bll[j] = ll[j];
+        }
+      }
+    }
+  }
+  __nv_bfloat16* out = y + pix * 2 * c_store;
+  *reinterpret_cast<uint4*>(out + g * 8) = bh;
+  *reinterpret_cast<uint4*>(out + c_store + g * 8) = bl;
+}
+
 __global__ void maxpool_q8_nhwc(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
                                 int32_t n, int32_t h, int32_t w, int32_t c_store, int32_t oh,
                                 int32_t ow, int32_t k, int32_t stride, int32_t pad,

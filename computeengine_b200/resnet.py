@@ -236,9 +236,143 @@ class ResNet50Q8:
         self.graph.replay()
 
 
+def make_f32_params(layers: List[ConvLayer], seed: int = 0) -> Dict[str, tuple]:
+    """He-normal fp32 weights N(0, sqrt(2 / fan_in)) and biases N(0, 0.01): the
+    folded weights and biases of a BN network (w' = w * gain, b' = b * gain +
+    shift, folded on the host)."""
+    out = {}
+    for i, l in enumerate(layers):
+        rng = np.random.default_rng([seed, 13, i])
+        fan_in = l.cin * l.k * l.k
+        w = rng.normal(0.0, np.sqrt(2.0 / fan_in), (l.cout, l.cin, l.k, l.k)).astype(np.float32)
+        b = rng.normal(0.0, 0.01, l.cout).astype(np.float32)
+        out[l.name] = (w, b)
+    return out
+
+
+def _c16(c: int) -> int:
+    return (c + 15) // 16 * 16
+
+
+class ResNet50F32:
+    """fp32 ResNet-50 conv stack on the bf16x3 tensor-core path, resident on
+    one GPU: activations stay as split bf16 hi/lo NHWC planes between layers
+    (x = hi + lo, the IE_Y_BF16X2_NHWC layout), every conv has its ReLU fused,
+    the stem output goes through the 3x3/2 max pool.  ``run(x)`` takes an fp32
+    NCHW device tensor [batch, 3, image, image]."""
+
+    def __init__(self, batch: int, params: Dict[str, tuple], device="cuda", image: int = 224):
+        import torch
+
+        from . import _lib as L
+        self.L, self.torch = L, torch
+        self.batch, self.image = batch, image
+        self.device = torch.device(device)
+        self.layers = resnet50_layers(image)
+        dev = self.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        self.descs, self.packed, self.bias, self.acts = {}, {}, {}, {}
+        for l in self.layers:
+            w, b = params[l.name]
+            d = L.ConvDesc()
+            d.n, d.c, d.h, d.w, d.m, d.kh, d.kw = batch, l.cin, l.h, l.h, l.cout, l.k, l.k
+            d.stride_h = d.stride_w = l.stride
+            d.dil_h = d.dil_w = 1
+            d.pad_top = d.pad_left = d.pad_bottom = d.pad_right = l.pad
+            d.group = 1
+            packed = torch.zeros(int(L.lib.ie_cuda_f32_packed_weight_bytes(d)), dtype=torch.uint8,
+                                 device=dev)
+            L.check(L.lib.ie_cuda_f32_pack_weights(d, torch.from_numpy(w).to(dev).data_ptr(),
+                                                   packed.data_ptr(), stream))
+            self.descs[l.name], self.packed[l.name] = d, packed
+            self.bias[l.name] = torch.from_numpy(b).to(dev)
+            self.acts[l.name] = torch.empty((batch, l.out_h, l.out_h, 2 * _c16(l.cout)),
+                                            dtype=torch.bfloat16, device=dev)
+        self.x_split = torch.empty((batch, image, image, 2 * 16), dtype=torch.bfloat16, device=dev)
+        stem = self.layers[0]
+        ph = (stem.out_h + 2 - 3) // 2 + 1
+        self.acts["pool"] = torch.empty((batch, ph, ph, 2 * 64), dtype=torch.bfloat16, device=dev)
+        self.graph = None
+        torch.cuda.synchronize(dev)
+
+    @property
+    def output(self):
+        return self.acts[self.layers[-1].name]
+
+    def to_nchw_f32(self, name: str):
+        """A layer's output (or "pool") as fp32 NCHW, hi + lo, on the device."""
+        t = self.acts[name]
+        half = t.shape[3] // 2
+        cout = 64 if name == "pool" else next(l.cout for l in self.layers if l.name == name)
+        v = t[..., :half].float() + t[..., half:].float()
+        return v[..., :cout].permute(0, 3, 1, 2).contiguous()
+
+    def run(self, x_f32_nchw) -> int:
+        L = self.L
+        stream = self.torch.cuda.current_stream(self.device).cuda_stream
+        b, img = self.batch, self.image
+        L.check(L.lib.ie_cuda_f32_pack_input(x_f32_nchw.data_ptr(), self.x_split.data_ptr(), b, 3,
+                                             img, img, 16, stream))
+        n = 1
+        for l in self.layers:
+            src = self.x_split if l.src == "input" else self.acts[l.src]
+            L.check(L.lib.ie_cuda_conv2d_bf16x3(self.descs[l.name], L.IE_ACT_RELU, src.data_ptr(),
+                                                self.packed[l.name].data_ptr(),
+                                                self.bias[l.name].data_ptr(),
+                                                self.acts[l.name].data_ptr(), L.IE_Y_BF16X2_NHWC,
+                                                stream))
+            n += 1
+            if l.name == "stem":
+                s = self.acts["stem"]
+                L.check(L.lib.ie_cuda_f32x2_maxpool2d(s.data_ptr(), self.acts["pool"].data_ptr(), b,
+                                                      s.shape[1], s.shape[2], 64, 3, 2, 1, stream))
+                n += 1
+        return n
+
+    def capture(self, x):
+        torch = self.torch
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.launches = self.run(x)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.run(x)
+        torch.cuda.synchronize(self.device)
+
+
+def bench_f32(batch: int = 32, iters: int = 20) -> dict:
+    """Times the fp32 (bf16x3) stack from a CUDA graph with inputs resident;
+    FLOPs are the algorithmic fp32 ones (2 per MAC, stem as the real 7x7x3)."""
+    import torch
+    layers = resnet50_layers()
+    net = ResNet50F32(batch, make_f32_params(layers))
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.uniform(-1, 1, (batch, 3, 224, 224)).astype(np.float32)).cuda()
+    net.capture(x)
+    for _ in range(3):
+        net.graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        net.graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    flops = 2 * macs_per_image(layers) * batch
+    return {"workload": "ResNet-50 v1.5 fp32 conv stack on bf16x3 (53 convs + max pool)",
+            "batch": batch, "ms_per_step": ms, "tflops": flops / ms / 1e9,
+            "images_per_s": batch / ms * 1e3, "launches": net.launches,
+            "device_error": net.L.take_device_error()}
+
+
 def main():
     """Runs the int8 stack `--steps` times on cuda:0 (uncaptured launches, so a
-    profiler sees each kernel with its own name) and prints one JSON line."""
+    profiler sees each kernel with its own name) and prints one JSON line;
+    `--dtype f32` times the fp32 (bf16x3) stack instead."""
     import argparse
     import json
 
@@ -246,7 +380,11 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--dtype", choices=["int8", "f32"], default="int8")
     a = ap.parse_args()
+    if a.dtype == "f32":
+        print(json.dumps(bench_f32(a.batch, max(a.steps, 5))))
+        return
     layers = resnet50_layers()
     net = ResNet50Q8(a.batch, make_q8_params(layers))
     x = torch.from_numpy(make_input_u8(a.batch)).cuda()

@@ -176,6 +176,13 @@ int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w
                          int64_t c_store, int64_t k, int64_t stride, int64_t pad,
                          int32_t is_signed, void* stream);
 
+/* The same pooling over split fp32 activations (the IE_Y_BF16X2_NHWC layout:
+ * bf16 [hi plane (c_store) | lo plane (c_store)] per pixel); the pair with the
+ * largest hi + lo is kept bit for bit. */
+int ie_cuda_f32x2_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,
+                            int64_t c_store, int64_t k, int64_t stride, int64_t pad,
+                            void* stream);
+
 /* ------------------------------------------------------------ fp32 path */
 
 /* Output formats of ie_cuda_conv2d_bf16x3. */
