@@ -94,6 +94,91 @@ def bench_layer(l: ConvLayer, batch: int, iters: int, dtype: str = "int8", seed:
             "bound_us": max(2 * macs / (peak * 1e12) * 1e6, bytes_io / (hbm * 1e9) * 1e6)}
 
 
+def _time(fn, iters: int) -> float:
+    """Microseconds per call, CUDA events on the current stream after warm-up."""
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    assert L.take_device_error() == 0
+    return a.elapsed_time(b) * 1e3 / iters
+
+
+def bench_configs(iters: int = 200) -> list:
+    """The single-convolution workloads, each as its drop-in call on device
+    tensors in the reference layout (NCHW), plus the int8 kernel alone:
+      config 1: fp32 x U(-1,1) [1,64,56,56], w N(0, sqrt(2/576)) [64,64,3,3],
+                bias N(0, 0.01), stride 1, pad 1, ReLU (ie_cuda_conv2d_f32);
+      config 2: int8 x uint8 N(128,30) zp 128 [8,128,28,28], w U{-127..127}
+                [128,128,3,3], per-channel multipliers, ReLU (pack input +
+                ie_cuda_conv2d_q8 + unpack output, and the kernel alone)."""
+    hbm, bf16 = _peaks()
+    stream = torch.cuda.current_stream().cuda_stream
+    dev = torch.device("cuda")
+    out = []
+    rng = np.random.default_rng(0)
+    # config 1
+    d = L.ConvDesc()
+    d.n, d.c, d.h, d.w, d.m, d.kh, d.kw = 1, 64, 56, 56, 64, 3, 3
+    d.stride_h = d.stride_w = d.dil_h = d.dil_w = 1
+    d.pad_top = d.pad_left = d.pad_bottom = d.pad_right = 1
+    d.group = 1
+    x = torch.from_numpy(rng.uniform(-1, 1, (1, 64, 56, 56)).astype(np.float32)).to(dev)
+    w = torch.from_numpy(rng.normal(0, np.sqrt(2 / 576), (64, 64, 3, 3)).astype(np.float32)).to(dev)
+    b = torch.from_numpy(rng.normal(0, 0.01, 64).astype(np.float32)).to(dev)
+    y = torch.empty((1, 64, 56, 56), device=dev)
+    ws = torch.empty(int(L.lib.ie_cuda_conv2d_f32_workspace_bytes(d)), dtype=torch.uint8, device=dev)
+    us = _time(lambda: L.check(L.lib.ie_cuda_conv2d_f32(d, L.IE_ACT_RELU, x.data_ptr(), w.data_ptr(),
+                                                        b.data_ptr(), y.data_ptr(), ws.data_ptr(),
+                                                        ws.numel(), stream)), iters)
+    flops = 2 * 64 * 64 * 9 * 56 * 56
+    out.append({"config": 1, "workload": "fp32 conv [1,64,56,56] 3x3 -> 64, ReLU, NCHW drop-in "
+                "(pack input + pack weights + bf16x3 conv)", "us": us,
+                "gflops": flops / us / 1e3, "frac_of_bf16_peak_over_3": flops / us / 1e6 / (bf16 / 3)})
+    # config 2
+    d2 = L.ConvDesc()
+    d2.n, d2.c, d2.h, d2.w, d2.m, d2.kh, d2.kw = 8, 128, 28, 28, 128, 3, 3
+    d2.stride_h = d2.stride_w = d2.dil_h = d2.dil_w = 1
+    d2.pad_top = d2.pad_left = d2.pad_bottom = d2.pad_right = 1
+    d2.group = 1
+    xq = torch.from_numpy(np.clip(np.rint(rng.normal(128, 30, (8, 128, 28, 28))), 0, 255)
+                          .astype(np.uint8)).to(dev)
+    wq = torch.from_numpy(rng.integers(-127, 128, (128, 128, 3, 3)).astype(np.int8)).to(dev)
+    packed = torch.zeros(int(L.lib.ie_cuda_q8_packed_weight_bytes(d2)), dtype=torch.uint8, device=dev)
+    L.check(L.lib.ie_cuda_q8_pack_weights(d2, wq.data_ptr(), packed.data_ptr(), stream))
+    bq = torch.from_numpy(np.rint(rng.normal(0, 500, 128)).astype(np.int32)).to(dev)
+    mult = torch.from_numpy((0.02 * rng.uniform(0.001, 0.01, 128) / 0.05).astype(np.float32)).to(dev)
+    x_nhwc = torch.empty((8, 28, 28, 128), dtype=torch.uint8, device=dev)
+    y_nhwc = torch.empty((8, 28, 28, 128), dtype=torch.uint8, device=dev)
+    y_nchw = torch.empty((8, 128, 28, 28), dtype=torch.uint8, device=dev)
+    q = L.Q8Params()
+    q.x_signed, q.zp_x, q.y_signed, q.zp_y, q.qmin, q.qmax = 1, 0, 0, 0, 0, 255
+
+    def conv_only():
+        L.check(L.lib.ie_cuda_conv2d_q8(d2, q, x_nhwc.data_ptr(), packed.data_ptr(), bq.data_ptr(),
+                                        mult.data_ptr(), y_nhwc.data_ptr(), stream))
+
+    def drop_in():
+        L.check(L.lib.ie_cuda_q8_pack_input(xq.data_ptr(), x_nhwc.data_ptr(), 8, 128, 28, 28, 128,
+                                            0x80, stream))
+        conv_only()
+        L.check(L.lib.ie_cuda_q8_unpack_output(y_nhwc.data_ptr(), y_nchw.data_ptr(), 8, 128, 28, 28,
+                                               128, stream))
+    ops = 2 * 8 * 128 * 128 * 9 * 28 * 28
+    us_k = _time(conv_only, iters)
+    us_d = _time(drop_in, iters)
+    out.append({"config": 2, "workload": "int8 conv [8,128,28,28] 3x3 -> 128, requantized, ReLU",
+                "kernel_us": us_k, "kernel_tops": ops / us_k / 1e6,
+                "frac_of_2x_bf16_peak": ops / us_k / 1e6 / (2 * bf16),
+                "drop_in_us": us_d, "drop_in_tops": ops / us_d / 1e6})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layer", action="append", default=[])
@@ -104,7 +189,13 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--dtype", choices=["int8", "f32"], default="int8")
+    ap.add_argument("--configs", action="store_true",
+                    help="time the single-convolution workloads (configs 1 and 2)")
     a = ap.parse_args()
+    if a.configs:
+        for r in bench_configs():
+            print(json.dumps(r), flush=True)
+        return
     layers = {l.name: l for l in resnet50_layers()}
     todo = []
     if a.shape:
