@@ -16,7 +16,9 @@ larger than L2, so no flush is needed between steps.
 
 ``--impl reference`` times the reference engine's own CPU convolution
 (Conv2DOp compiled from its sources, fp32, run on the dequantized stack, one
-image per host thread) on a bounded sample of the same workload.
+image per host thread) on a bounded sample of the same workload: each step is
+a window of consecutive layers, rotating through the stack, sized so that all
+K steps take about REFERENCE_ARM_BUDGET_S of host time.
 """
 from __future__ import annotations
 
@@ -42,7 +44,7 @@ PROFILE_JSON = ROOT / "profiles" / "conv_igemm_q8_resnet50_traffic.json"
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH_PER_GPU)
@@ -63,15 +65,22 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.skip = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a few hundred ms to print its first line: wait for
+            # it so that the samples fall inside the timed region that follows.
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.01)
+            self.skip = len(self.lines)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -91,7 +100,13 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = self.lines[self.skip:]
+        note = None
+        if not lines and self.lines:
+            # the timed region ended before the next sample: report the one
+            # taken as it started (the warm-up had the GPU busy then)
+            lines, note = self.lines[-1:], "timed region shorter than the sampling period"
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -105,8 +120,11 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm)}
+        if note:
+            out["note"] = note
+        return out
 
 
 # ------------------------------------------------------------ distributed
@@ -213,36 +231,111 @@ def cpu_model() -> str:
     return "unknown"
 
 
+class CpuLayerRunner:
+    """The stack's convolutions run one layer at a time on the host cores: the
+    reference's fp32 Conv2DOp on the dequantized stack when its library is
+    built, else the int8 oracle port.  Each layer reads a fixed synthetic input
+    of its own shape (`images` images, one per thread), so any contiguous
+    window of layers can be timed on its own; a dense convolution's time does
+    not depend on its values."""
+
+    def __init__(self, images: int, threads: int):
+        from computeengine_b200.resnet import make_q8_params, resnet50_layers
+        from oracle.oracle import Oracle, RefConv
+
+        self.layers = resnet50_layers(IMAGE)
+        self.params = make_q8_params(self.layers, seed=0)
+        self.images, self.threads = images, threads
+        rng = np.random.default_rng(7)
+        self.inputs = {}
+        if RefConv.available():
+            self.kind, self.ref = "reference", RefConv()
+            self.row_kernel = self.ref.row_kernel()
+            self.fp = _dequant_stack(self.layers, self.params)
+            for l in self.layers:
+                key = (l.cin, l.h)
+                if key not in self.inputs:
+                    x = rng.integers(0, 40, (images, l.cin, l.h, l.h), dtype=np.uint8)
+                    self.inputs[key] = x.astype(np.float32) * np.float32(0.05)
+        else:
+            self.kind, self.orc, self.row_kernel = "port", Oracle(), "c-oracle"
+            for l in self.layers:
+                key = (l.cin, l.h)
+                if key not in self.inputs:
+                    self.inputs[key] = rng.integers(0, 40, (images, l.cin, l.h, l.h),
+                                                    dtype=np.uint8)
+
+    def run_layer(self, i: int) -> float:
+        """Runs layer i on its synthetic input; returns seconds."""
+        l = self.layers[i]
+        x = self.inputs[(l.cin, l.h)]
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            w, b = self.fp[l.name]
+            rc, y = self.ref.conv2d(x, w, b, strides=(l.stride, l.stride), pads=(l.pad,) * 4,
+                                    nthreads=self.threads)
+            if rc != 0:
+                raise RuntimeError(f"reference conv failed on {l.name}: {rc}")
+            np.maximum(y, 0.0, out=y)
+        else:
+            p = self.params[l.name]
+            self.orc.conv2d_q8(x, p.w, p.bias, p.mult, p.zp_x, 0, 0, 255,
+                               strides=(l.stride, l.stride), pads=(l.pad,) * 4,
+                               nthreads=self.threads)
+        return time.perf_counter() - t0
+
+
+# Host seconds the reference arm's timed steps may take in total, whatever K is.
+REFERENCE_ARM_BUDGET_S = 150.0
+
+
 def run_reference_arm(args, world, rank):
-    from computeengine_b200.resnet import macs_per_image, resnet50_layers
+    """The reference's CPU path timed over K steps.  A full step (53 convs on one
+    image per host thread) takes several seconds, so each step is a window of
+    consecutive layers sized from an untimed calibration pass to keep all K
+    steps within REFERENCE_ARM_BUDGET_S; the windows rotate through the stack,
+    and the value is the operations done over the time taken.  With K small
+    enough every step is the whole stack."""
     if rank != 0:
         return
-    ops_img = 2 * macs_per_image(resnet50_layers(IMAGE))
     threads = cpu_threads()
     images = threads
-    # one untimed warm step on a single image (page-in, thread start-up)
-    cpu_reference_stack(1, 1)
-    times = []
-    kind = cores = rk = None
+    runner = CpuLayerRunner(images, threads)
+    nl = len(runner.layers)
+    layer_ops = [2 * l.macs_per_image * images for l in runner.layers]
+    calib = [runner.run_layer(i) for i in range(nl)]  # untimed: page-in, thread start-up
+    step_budget = min(sum(calib), REFERENCE_ARM_BUDGET_S / max(args.steps, 1))
+    for _ in range(args.warmup):
+        runner.run_layer(0)
+    cursor, tot, ops, layers_run = 0, 0.0, 0, 0
     for _ in range(args.steps):
-        dt, kind, cores, rk = cpu_reference_stack(images, threads)
-        times.append(dt)
-    tot = float(np.sum(times))
-    value = ops_img * images * args.steps / tot / 1e12
+        est, window = 0.0, []
+        while len(window) < nl and (not window or est + calib[cursor] <= step_budget * 1.05):
+            window.append(cursor)
+            est += calib[cursor]
+            cursor = (cursor + 1) % nl
+        for i in window:
+            tot += runner.run_layer(i)
+            ops += layer_ops[i]
+        layers_run += len(window)
+    value = ops / tot / 1e12
+    sample = (f"{images} images (one per host thread); {layers_run} layer runs over "
+              f"{args.steps} steps, rotating through the 53 convs "
+              f"({layers_run / nl:.2f} passes of the stack)")
     line = {
         "metric": "int8 conv TOPS (ResNet-50 conv stack, 53 convs)",
         "value": value, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32" if kind == "reference" else "int8",
+        "vs_baseline": None, "dtype": "f32" if runner.kind == "reference" else "int8",
         "data": "synthetic (seeded)",
-        "images_per_s": images * args.steps / tot,
+        "images_per_s": value * 1e12 / sum(layer_ops) * images,
         "config": {"workload": "ResNet-50 v1.5 conv stack, reference Conv2DOp on the "
                                "dequantized int8 stack (fp32), one image per host thread",
-                   "batch_per_step": images, "image": IMAGE, "row_kernel": rk,
+                   "batch_per_step": images, "image": IMAGE, "row_kernel": runner.row_kernel,
                    "cpu": cpu_model()},
-        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": kind,
-                         "sample": f"{images} images x 53 convs per step"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": runner.kind,
+                         "sample": sample},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -355,12 +448,17 @@ def run_ours(args, world, rank, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
-        dt, kind, cores, rk = cpu_reference_stack(threads, threads)
-        cpu = {"value": ops_img * threads / dt / 1e12, "unit": "TOPS", "cores": cores,
+        cpu_reference_stack(1, 1)  # untimed: page-in, thread start-up
+        dt, passes = 0.0, 0
+        while dt < 10.0 and passes < 30:  # about 10 s of host work
+            t, kind, cores, rk = cpu_reference_stack(threads, threads)
+            dt += t
+            passes += 1
+        cpu = {"value": ops_img * threads * passes / dt / 1e12, "unit": "TOPS", "cores": cores,
                "kind": kind,
-               "sample": f"{threads} images through the 53-conv stack, one image per thread "
-                         f"({rk} row kernel, {cpu_model()})",
-               "images_per_s": threads / dt}
+               "sample": f"{passes} passes of {threads} images through the 53-conv stack, "
+                         f"one image per thread ({rk} row kernel, {cpu_model()})",
+               "images_per_s": threads * passes / dt}
 
     if rank != 0:
         return

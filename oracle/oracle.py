@@ -158,6 +158,24 @@ class RefConv:
     def row_kernel(self) -> str:
         return ["scalar", "sse2", "avx2", "avx512"][self.lib.ref_row_kernel()]
 
+    @staticmethod
+    def _explicit_dims(xs, ws, strides, dilations, pads, auto_pad):
+        """Output dims for explicit padding, by the reference's own rule
+        (conv2d_op.cpp:151-162): (H + pt + pb - (d*(k-1)+1)) / s + 1.  None
+        when the library has to answer (auto_pad, an empty batch, a shape the
+        op rejects), so its error codes stay the reference's."""
+        if auto_pad != "NOTSET" or len(xs) != 4 or len(ws) != 4 or xs[0] <= 0:
+            return None
+        if min(strides) <= 0 or min(dilations) <= 0 or min(pads) < 0:
+            return None
+        eh = dilations[0] * (ws[2] - 1) + 1
+        ew = dilations[1] * (ws[3] - 1) + 1
+        hp = xs[2] + pads[0] + pads[2]
+        wp = xs[3] + pads[1] + pads[3]
+        if hp < eh or wp < ew:
+            return None
+        return (xs[0], ws[0], (hp - eh) // strides[0] + 1, (wp - ew) // strides[1] + 1)
+
     def conv2d(self, x, w, b=None, strides=(1, 1), dilations=(1, 1), pads=(0, 0, 0, 0),
                group=1, auto_pad="NOTSET", depthwise=False, kernel_choice=-1,
                nthreads=1):
@@ -170,11 +188,15 @@ class RefConv:
         d = np.array(dilations, np.int64)
         p = np.array(pads, np.int64)
         dims = np.zeros(4, np.int64)
-        rc = self.lib.ref_conv2d_f32(_ptr(x), *x.shape, _ptr(w), *w.shape, _ptr(b), _ptr(s),
-                                     _ptr(d), _ptr(p), group, AUTO_PAD[auto_pad],
-                                     int(depthwise), kernel_choice, 1, None, _ptr(dims))
-        if rc != OK:
-            return rc, None
+        known = self._explicit_dims(x.shape, w.shape, strides, dilations, pads, auto_pad)
+        if known is not None:
+            dims[:] = known
+        else:
+            rc = self.lib.ref_conv2d_f32(_ptr(x), *x.shape, _ptr(w), *w.shape, _ptr(b), _ptr(s),
+                                         _ptr(d), _ptr(p), group, AUTO_PAD[auto_pad],
+                                         int(depthwise), kernel_choice, 1, None, _ptr(dims))
+            if rc != OK:
+                return rc, None
         y = np.empty(tuple(int(v) for v in dims), np.float32)
         rc = self.lib.ref_conv2d_f32(_ptr(x), *x.shape, _ptr(w), *w.shape, _ptr(b), _ptr(s),
                                      _ptr(d), _ptr(p), group, AUTO_PAD[auto_pad],

@@ -48,6 +48,10 @@ int code_of(const ie::Error& e) {
     return 1 + static_cast<int>(e.code);  // InvalidArgument -> 1, ...
 }
 
+// The op's output dims differ from the dims the caller sized y by (not a
+// reference error code: those are 1 + Error::Code, all below 100).
+constexpr int kShapeMismatch = 100;
+
 ie::Tensor host_tensor(std::vector<int64_t> dims, const float* data,
                        const std::shared_ptr<ie::Allocator>& alloc) {
     auto t = ie::Tensor::allocate(ie::Shape{dims}, ie::DType::F32, alloc);
@@ -119,7 +123,12 @@ int run_one(const RunArgs& a, int64_t first, int64_t count) {
         return code_of(st.error());
     }
     const auto& d = out[0].shape.dims;
-    if (a.out_dims != nullptr && first == 0) {
+    if (a.y != nullptr && a.out_dims != nullptr) {
+        // y was sized from out_dims by the caller: copy only into a match.
+        for (int i = 1; i < 4; ++i) {
+            if (a.out_dims[i] != d[i]) return kShapeMismatch;
+        }
+    } else if (a.out_dims != nullptr && first == 0) {
         for (int i = 0; i < 4; ++i) a.out_dims[i] = d[i];
     }
     if (a.y != nullptr) {
@@ -158,6 +167,13 @@ int ref_conv2d_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
                    float* y, int64_t* out_dims) {
     RunArgs a{x, n, c, h, w, wt, m, cg, kh, kw, bias, strides, dilations, pads,
               group, auto_pad, depthwise, kernel_choice, y, out_dims};
+    if (y == nullptr && n > 1) {
+        // Shape query: the output dims do not depend on the batch, so one
+        // image answers it (and reports the same argument errors).
+        const int rc = run_one(a, 0, 1);
+        if (rc == 0 && out_dims != nullptr) out_dims[0] = n;
+        return rc;
+    }
     if (nthreads <= 1 || n <= 1 || y == nullptr) return run_one(a, 0, n);
     if (nthreads > n) nthreads = static_cast<int>(n);
     std::vector<int> rc(static_cast<size_t>(nthreads), 0);

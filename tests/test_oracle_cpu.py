@@ -78,6 +78,44 @@ def test_fp32_matches_reference_conv(oracle, refconv, g):
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("g", GEOMETRIES, ids=range(len(GEOMETRIES)))
+def test_reference_wrapper_dims_and_threads(refconv, g):
+    """The wrapper's output dims for explicit padding (the reference's own
+    formula) equal the library's shape query, and a threaded batch call
+    (one image per thread) equals the images run one by one."""
+    from oracle.oracle import RefConv
+    rng = np.random.default_rng(5)
+    xs = (3,) + tuple(g["x"][1:])
+    x = rng.normal(size=xs).astype(np.float32)
+    w = rng.normal(size=g["w"]).astype(np.float32)
+    kw = {k: v for k, v in g.items() if k not in ("x", "w")}
+    full = dict(strides=(1, 1), dilations=(1, 1), pads=(0, 0, 0, 0), auto_pad="NOTSET")
+    full.update({k: v for k, v in kw.items() if k in full})
+    known = RefConv._explicit_dims(x.shape, w.shape, full["strides"], full["dilations"],
+                                   full["pads"], full["auto_pad"])
+    rc, whole = refconv.conv2d(x, w, None, nthreads=3, **kw)
+    assert rc == 0
+    if known is not None:
+        assert tuple(whole.shape) == tuple(known)
+    parts = []
+    for i in range(x.shape[0]):
+        rc, y = refconv.conv2d(x[i:i + 1], w, None, **kw)
+        assert rc == 0
+        parts.append(y)
+    np.testing.assert_array_equal(whole, np.concatenate(parts))
+
+
+def test_reference_wrapper_keeps_error_codes(refconv):
+    """Shapes the formula cannot vouch for go to the library, which answers
+    with the reference's own error code."""
+    from oracle.oracle import INVALID_ARGUMENT
+    x = np.zeros((2, 3, 4, 4), np.float32)
+    rc, y = refconv.conv2d(x, np.zeros((4, 3, 7, 7), np.float32))  # kernel > padded input
+    assert rc == INVALID_ARGUMENT and y is None
+    rc, y = refconv.conv2d(x, np.zeros((4, 5, 3, 3), np.float32))  # channel mismatch
+    assert rc == INVALID_ARGUMENT and y is None
+
+
 @pytest.mark.parametrize("g", GEOMETRIES[:4], ids=range(4))
 def test_int8_accumulators_match_reference_conv(oracle, refconv, g):
     """Integer-valued fp32 through the reference conv is exact below 2^24, so
