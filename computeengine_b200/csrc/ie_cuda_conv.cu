@@ -736,12 +736,23 @@ int ie_cuda_q8_stem_pack_input(const void* x_nchw, void* x_packed, int64_t n, in
   if (x_nchw == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
   if ((rc = check_ptr(x_packed, "x_packed", 16)) != IE_OK) return rc;
   const int64_t blocks = n * (h / 2);
-  const size_t smem = static_cast<size_t>(c * 2 * w);
-  if (blocks > INT32_MAX || smem > 48 * 1024) return fail(IE_UNSUPPORTED, "stem input too large");
-  stem_pack_s2d_u8<<<static_cast<unsigned>(blocks), 256, smem, as_stream(stream)>>>(
-      static_cast<const uint8_t*>(x_nchw), static_cast<uint8_t*>(x_packed),
-      static_cast<int32_t>(n), static_cast<int32_t>(c), static_cast<int32_t>(h),
-      static_cast<int32_t>(w), static_cast<uint8_t>(xor_mask & 0xFF));
+  const size_t smem = static_cast<size_t>(c * 2 * stem_row_stride(static_cast<int>(w))) +
+                      static_cast<size_t>(w / 2) * 64;
+  if (blocks > INT32_MAX || w > 2048 || smem > 48 * 1024) {
+    return fail(IE_UNSUPPORTED, "stem input too large");
+  }
+  const int threads = static_cast<int>(std::min<int64_t>(256, ((w / 2 + 31) / 32) * 32));
+  const auto xp = static_cast<const uint8_t*>(x_nchw);
+  const auto yp = static_cast<uint8_t*>(x_packed);
+  const auto hh = static_cast<int32_t>(h), ww = static_cast<int32_t>(w);
+  const auto m8 = static_cast<uint8_t>(xor_mask & 0xFF);
+  const dim3 grid(static_cast<unsigned>(blocks));
+  switch (c) {
+    case 1: stem_pack_s2d_u8<1><<<grid, threads, smem, as_stream(stream)>>>(xp, yp, hh, ww, m8); break;
+    case 2: stem_pack_s2d_u8<2><<<grid, threads, smem, as_stream(stream)>>>(xp, yp, hh, ww, m8); break;
+    case 3: stem_pack_s2d_u8<3><<<grid, threads, smem, as_stream(stream)>>>(xp, yp, hh, ww, m8); break;
+    default: stem_pack_s2d_u8<4><<<grid, threads, smem, as_stream(stream)>>>(xp, yp, hh, ww, m8); break;
+  }
   return check_launch("stem_pack_s2d_u8");
 }
 

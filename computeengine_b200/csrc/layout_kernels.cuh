@@ -138,50 +138,109 @@ namespace ie_cuda {
 // same implicit-GEMM kernel as every other layer:
 //   out[i][j][((b*2+dy)*2+dx)*c + ch] = x[ch][2i+dy][2(j+b-2)+dx]   (0 if j+b-2
 //   is outside [0, w/2)), i in [0, h/2), j in [0, w/2)
-// One block per (image, output row i): input rows 2i and 2i+1 of every
-// channel are staged in shared memory with coalesced loads, then the block
-// writes the output row (w/2 pixels x 64 bytes) with coalesced 16-byte stores.
+// For a fixed (ch, dy) the eight bytes b = 0..3, dx = 0..1 are the input
+// columns 2j-4 .. 2j+3 of one row.  One block per (image, output row i): input
+// rows 2i and 2i+1 of every channel are staged in shared memory between
+// 16-byte zero margins (so columns outside the image read as 0), each thread
+// builds one output pixel's 64 bytes as whole words from one funnel-shifted
+// word pair per (ch, dy), and the row (w/2 pixels x 64 bytes) is staged with a
+// 16-byte-chunk swizzle (conflict-free 128-bit shared stores and loads) and
+// written with coalesced 16-byte stores.
+constexpr int kStemMargin = 16;
+
+__host__ __device__ constexpr int stem_row_stride(int w) {
+  return ((w + 2 * kStemMargin + 15) / 16) * 16;
+}
+
+template <int C>
 __global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restrict__ x,
-                                                        uint8_t* __restrict__ y, int32_t n,
-                                                        int32_t c, int32_t h, int32_t w,
-                                                        uint8_t xor_mask) {
-  extern __shared__ uint8_t rows[];  // [c][2][w]
+                                                        uint8_t* __restrict__ y, int32_t h,
+                                                        int32_t w, uint8_t xor_mask) {
+  extern __shared__ __align__(16) uint8_t stem_smem[];
   const int32_t ho = h / 2, wo = w / 2;
+  const int32_t rs = stem_row_stride(w);
+  uint8_t* rows = stem_smem;               // [C][2][rs]: margin | w columns | margin
+  uint8_t* tile = stem_smem + C * 2 * rs;  // [wo][64], 16-byte chunks swizzled
   const int32_t i = blockIdx.x % ho;
   const int64_t img = blockIdx.x / ho;
-  const uint8_t* xi = x + img * c * h * w;
-  const int32_t span = 2 * w;  // two consecutive input rows are contiguous in NCHW
-  for (int cc = 0; cc < c; ++cc) {
+  const uint8_t* xi = x + img * C * h * static_cast<int64_t>(w);
+  const uint32_t mask4 = 0x01010101u * xor_mask;
+
+  // zero margins
+  const int32_t right = rs - kStemMargin - w;
+  for (int t = threadIdx.x; t < C * 2 * (kStemMargin + right); t += blockDim.x) {
+    const int32_t r = t / (kStemMargin + right), k = t % (kStemMargin + right);
+    rows[r * rs + (k < kStemMargin ? k : kStemMargin + w + k - kStemMargin)] = 0;
+  }
+  // rows 2i, 2i+1 of every channel (contiguous 2w bytes per channel in NCHW)
+#pragma unroll
+  for (int cc = 0; cc < C; ++cc) {
     const uint8_t* src = xi + (static_cast<int64_t>(cc) * h + 2 * i) * w;
-    uint8_t* dst = rows + cc * span;
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (span & 15) == 0) {
-      for (int t = threadIdx.x; t < span / 16; t += blockDim.x) {
-        reinterpret_cast<uint4*>(dst)[t] = __ldg(reinterpret_cast<const uint4*>(src) + t);
+    uint8_t* dst = rows + cc * 2 * rs + kStemMargin;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (w & 15) == 0) {
+      for (int t = threadIdx.x; t < (2 * w) >> 4; t += blockDim.x) {
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + t);
+        v.x ^= mask4;
+        v.y ^= mask4;
+        v.z ^= mask4;
+        v.w ^= mask4;
+        const int32_t off = t << 4, dy = off >= w;
+        *reinterpret_cast<uint4*>(dst + dy * rs + off - dy * w) = v;
       }
     } else {
-      for (int t = threadIdx.x; t < span; t += blockDim.x) dst[t] = src[t];
+      for (int t = threadIdx.x; t < 2 * w; t += blockDim.x) {
+        const int32_t dy = t >= w;
+        dst[dy * rs + t - dy * w] = src[t] ^ xor_mask;
+      }
     }
   }
   __syncthreads();
-  uint4* out = reinterpret_cast<uint4*>(y + ((img * ho + i) * static_cast<int64_t>(wo)) * 64);
-  for (int t = threadIdx.x; t < wo * 4; t += blockDim.x) {
-    const int32_t j = t >> 2, g = t & 3;
-    uint32_t v[4] = {0, 0, 0, 0};
+
+  for (int j = threadIdx.x; j < wo; j += blockDim.x) {
+    // columns 2j-4 .. 2j+3 start at byte kStemMargin - 4 + 2j (even)
+    const int32_t base = kStemMargin - 4 + 2 * j;
+    const uint32_t sh = (base & 3) * 8;
+    uint32_t lo[C][2], hi[C][2];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int32_t chan = g * 16 + k;
-      if (chan < 16 * c) {
-        const int32_t cc = chan % c;
-        const int32_t rest = chan / c;  // (b*2 + dy)*2 + dx
-        const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
-        const int32_t jj = j + b - 2;
-        if (jj >= 0 && jj < wo) {
-          const uint32_t byte = rows[cc * span + dy * w + 2 * jj + dx] ^ xor_mask;
-          v[k >> 2] |= byte << (8 * (k & 3));
-        }
+    for (int cc = 0; cc < C; ++cc) {
+#pragma unroll
+      for (int dy = 0; dy < 2; ++dy) {
+        const uint32_t* r = reinterpret_cast<const uint32_t*>(rows + (cc * 2 + dy) * rs + (base & ~3));
+        const uint32_t w0 = r[0], w1 = r[1], w2 = r[2];
+        lo[cc][dy] = __funnelshift_r(w0, w1, sh);
+        hi[cc][dy] = __funnelshift_r(w1, w2, sh);
       }
     }
-    out[t] = make_uint4(v[0], v[1], v[2], v[3]);
+    uint32_t o[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      uint32_t v = 0;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int chan = 4 * q + kk;
+        if (chan < 16 * C) {
+          const int cc = chan % C, rest = chan / C;
+          const int dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
+          const int k = 2 * b + dx;
+          const uint32_t src = k < 4 ? lo[cc][dy] : hi[cc][dy];
+          v |= ((src >> (8 * (k & 3))) & 0xFFu) << (8 * kk);
+        }
+      }
+      o[q] = v;
+    }
+    const int32_t swz = (j >> 1) & 3;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      *reinterpret_cast<uint4*>(tile + j * 64 + 16 * (k ^ swz)) =
+          make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+    }
+  }
+  __syncthreads();
+
+  uint4* out = reinterpret_cast<uint4*>(y + ((img * ho + i) * static_cast<int64_t>(wo)) * 64);
+  for (int q = threadIdx.x; q < wo * 4; q += blockDim.x) {
+    const int32_t p = q >> 2, k = q & 3;
+    out[q] = *reinterpret_cast<const uint4*>(tile + p * 64 + 16 * (k ^ ((p >> 1) & 3)));
   }
 }
 
