@@ -48,7 +48,7 @@ class Q8Params(C.Structure):
 
 class ConvPlan(C.Structure):
     _fields_ = [(n, _i32) for n in ("bn", "bk_bytes", "m_sub", "stages", "resident_weights",
-                                    "out_bufs", "row_band", "grid")]
+                                    "out_bufs", "row_band", "grid", "a_tiled")]
 
 
 class CudaConvError(RuntimeError):

@@ -87,6 +87,10 @@ struct IgemmArgs {
   int32_t wp, rows_t, rows_box, tiles_img;
   int32_t stage_bytes;  // shared memory per stage (band + slack for the shifted reads)
   int32_t band_bytes;   // bytes one band load delivers
+  // 1x1, stride 1, no padding: the A operand is the activation tensor itself
+  // viewed as a [pixels, channels] matrix, loaded with 2D tiled TMA (rows past
+  // the last pixel read as zero) instead of im2col.
+  int32_t a_tiled;
 };
 
 __host__ __device__ constexpr uint32_t swizzle_layout_code(int row_bytes) {
@@ -197,7 +201,9 @@ struct EpiQ8 {
 // The 16x256b TMEM reads give this thread rows r and r + 8 of each 16-row half
 // (r = lane / 4) and the column pairs 8j + 2q, 8j + 2q + 1 (q = lane % 4):
 // 8 columns per 32-column chunk, whose constants are read from shared memory
-// once per chunk and serve all 4 of its rows.
+// once per chunk and serve all 4 of its rows.  The two 16-row halves of a
+// chunk are read one at a time so that one half's TMEM read is in flight
+// while the other half is requantized.
 template <int kMode, bool kS8, bool kClamp, int kCols, int kRows, int kPanelW>
 __device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int row0, int col0,
                                             const EpiQ8& e, uint64_t* acce) {
@@ -210,49 +216,45 @@ __device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int r
 #pragma unroll
   for (int j = 0; j < 4; ++j) lo_part[j] = (8 * j + 2 * q4) ^ (xr & 0x10u);
   uint8_t* const tb = s_tile + (row0 + r8) * kPanelW;
+  uint32_t acc[2][16];  // [16-row half]
+  tmem_ld_16x256b_x4(t_q, acc[0]);
+  tmem_ld_wait(acc[0]);
 #pragma unroll 1
   for (int cc = 0; cc < kCols; cc += 32) {
     const int col = col0 + cc;
     uint8_t* const cb = tb + (col / kPanelW) * (kRows * kPanelW) + ((col % kPanelW) ^ (xr & 0x60u));
-    uint32_t acc[2][16];
-    tmem_ld_16x256b_x4(t_q + cc, acc[0]);
     tmem_ld_16x256b_x4(t_q + (16u << 16) + cc, acc[1]);
-    tmem_ld_wait();
-    if (cc + 32 >= kCols) {
-      // Last read of this accumulator buffer by this warp: hand it back so
-      // the MMA warp can start the next tile while we finish the epilogue.
-      tc_fence_before();
-      __syncwarp();
-      if (e.lane == 0) mbar_arrive(acce);
-    }
+    // constants of this thread's column pairs 8j + 2q, 8j + 2q + 1
+    long long ka[4][2] = {};
+    int32_t kb[4][2] = {}, km[4][2] = {};
+    if constexpr (kMode != kReqExact) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      // constants of this thread's column pair 8j + 2q, 8j + 2q + 1
-      const int c = cc + 8 * j + 2 * q4;
-      long long ka[2] = {0, 0};
-      int32_t kb[2] = {0, 0}, km[2] = {0, 0};
-      if constexpr (kMode != kReqExact) {
+      for (int j = 0; j < 4; ++j) {
+        const int c = cc + 8 * j + 2 * q4;
         const int2 m2 = *reinterpret_cast<const int2*>(e.s_mant + c);
-        km[0] = m2.x;
-        km[1] = m2.y;
+        km[j][0] = m2.x;
+        km[j][1] = m2.y;
         if constexpr (kMode == kReqFold) {
           const longlong2 a2 = *reinterpret_cast<const longlong2*>(e.s_add + c);
-          ka[0] = a2.x;
-          ka[1] = a2.y;
+          ka[j][0] = a2.x;
+          ka[j][1] = a2.y;
         } else {
           const int2 b2 = *reinterpret_cast<const int2*>(e.s_bias + c);
-          kb[0] = b2.x;
-          kb[1] = b2.y;
+          kb[j][0] = b2.x;
+          kb[j][1] = b2.y;
         }
       }
+    }
+    auto half = [&](const uint32_t(&a16)[16], int h) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int j = 0; j < 4; ++j) {
+        const int c = cc + 8 * j + 2 * q4;
 #pragma unroll
         for (int rs = 0; rs < 2; ++rs) {
           int32_t r[2];
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            const uint32_t a = acc[h][4 * j + 2 * rs + x];
+            const uint32_t a = a16[4 * j + 2 * rs + x];
             if constexpr (kMode == kReqExact) {
               RequantConst k;
               k.mant = e.s_mant[c + x];
@@ -262,14 +264,14 @@ __device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int r
             } else {
               long long p;
               if constexpr (kMode == kReqFold) {
-                p = static_cast<long long>(static_cast<int32_t>(a)) * km[x] + ka[x];
+                p = static_cast<long long>(static_cast<int32_t>(a)) * km[j][x] + ka[j][x];
               } else {
-                const int32_t t = static_cast<int32_t>(a + static_cast<uint32_t>(kb[x]));
+                const int32_t t = static_cast<int32_t>(a + static_cast<uint32_t>(kb[j][x]));
                 const int32_t sg = t >> 31;
                 const long long cs = static_cast<long long>(
                     (static_cast<unsigned long long>(static_cast<uint32_t>(e.hi_c + sg)) << 32) |
                     static_cast<uint32_t>(sg));
-                p = static_cast<long long>(t) * km[x] + cs;
+                p = static_cast<long long>(t) * km[j][x] + cs;
               }
               r[x] = static_cast<int32_t>(p >> 32) >> e.shm;
               if constexpr (kClamp) r[x] = min(max(r[x], e.lo), e.hi);
@@ -279,7 +281,21 @@ __device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int r
               static_cast<uint16_t>(pack2_sat<kS8>(r[0], r[1]));
         }
       }
+    };
+    half(acc[0], 0);
+    tmem_ld_wait(acc[1]);
+    const bool more = cc + 32 < kCols;
+    if (more) {
+      tmem_ld_16x256b_x4(t_q + cc + 32, acc[0]);
+    } else {
+      // Last read of this accumulator buffer by this warp: hand it back so
+      // the MMA warp can start the next tile while we finish the epilogue.
+      tc_fence_before();
+      __syncwarp();
+      if (e.lane == 0) mbar_arrive(acce);
     }
+    half(acc[1], 1);
+    if (more) tmem_ld_wait(acc[0]);
   }
 }
 
@@ -565,13 +581,21 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
           }
           uint8_t* st = stage_base + s * stage_bytes;
           mbar_arrive_expect_tx(&full_bar[s], kStage);
-          const uint16_t offw = static_cast<uint16_t>(kx * args.dil_w);
-          const uint16_t offh = static_cast<uint16_t>(ky * args.dil_h);
-          tma_load_im2col_4d(st, &tmap_a, &full_bar[s], cb * kBkElems, wc, hc, img, offw, offh);
-          if constexpr (!KIND_I8) {
-            // lo plane: activation channels [c, 2c)
-            tma_load_im2col_4d(st + kA, &tmap_a, &full_bar[s], args.c + cb * kBkElems, wc, hc,
-                               img, offw, offh);
+          if (args.a_tiled) {
+            tma_load_2d(st, &tmap_a, &full_bar[s], cb * kBkElems, static_cast<int32_t>(p0));
+            if constexpr (!KIND_I8) {
+              tma_load_2d(st + kA, &tmap_a, &full_bar[s], args.c + cb * kBkElems,
+                          static_cast<int32_t>(p0));
+            }
+          } else {
+            const uint16_t offw = static_cast<uint16_t>(kx * args.dil_w);
+            const uint16_t offh = static_cast<uint16_t>(ky * args.dil_h);
+            tma_load_im2col_4d(st, &tmap_a, &full_bar[s], cb * kBkElems, wc, hc, img, offw, offh);
+            if constexpr (!KIND_I8) {
+              // lo plane: activation channels [c, 2c)
+              tma_load_im2col_4d(st + kA, &tmap_a, &full_bar[s], args.c + cb * kBkElems, wc, hc,
+                                 img, offw, offh);
+            }
           }
           if constexpr (!B_RES) {
             const int32_t kcoord = tap * args.k_per_tap * kParts + cb * kBkElems;

@@ -312,7 +312,14 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t a_chan = i8 ? x_c_store : 2 * x_c_store;
   int rc;
-  if (h_wp > 0) {
+  const bool a_tiled = h_wp == 0 && d->kh == 1 && d->kw == 1 && d->stride_h == 1 &&
+                       d->stride_w == 1 && s.pad_top == 0 && s.pad_left == 0 &&
+                       s.pad_bottom == 0 && s.pad_right == 0 && m_total < (int64_t{1} << 31);
+  if (a_tiled) {
+    // [n*h*w pixels, a_chan] matrix, box = bk elements x one tile of rows
+    rc = encode_2d(&out->ta, x, dt, elem_bytes, m_total, a_chan, static_cast<int>(bk_elems),
+                   128 * v.m_sub);
+  } else if (h_wp > 0) {
     // band box: bk channels x wp columns (from -pad_left) x rows_box rows
     rc = encode_nhwc_4d(&out->ta, x, dt, elem_bytes, d->n, d->h, d->w, a_chan,
                         static_cast<int>(bk_elems), static_cast<int>(h_wp),
@@ -369,6 +376,7 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   a.acc_bound = d->kh * d->kw * d->c * 255 * 128;
   a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128 * v.m_sub));
   a.n_tiles = static_cast<int32_t>(ceil_div(d->m, v.bn));
+  a.a_tiled = a_tiled ? 1 : 0;
   if (h_wp > 0) {
     a.halo = 1;
     a.wp = static_cast<int32_t>(h_wp);
@@ -425,6 +433,7 @@ int launch_setup(IgemmSetup& su, bool a_signed, cudaStream_t st) {
   g_last_plan.out_bufs = su.v.out_bufs;
   g_last_plan.row_band = su.args.halo;
   g_last_plan.grid = su.grid;
+  g_last_plan.a_tiled = su.args.a_tiled;
   LaunchFn fn = su.v.i8 ? (a_signed ? pick_launch<true, true>(su.v) : pick_launch<true, false>(su.v))
                         : pick_launch<false, false>(su.v);
   if (fn == nullptr) {

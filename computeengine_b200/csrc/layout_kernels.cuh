@@ -334,6 +334,39 @@ __global__ void maxpool_q8_nhwc(const uint8_t* __restrict__ x, uint8_t* __restri
   const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(ow) * oh));
   const uint32_t init = is_signed ? 0x80808080u : 0u;
   uint4 best = make_uint4(init, init, init, init);
+  if (k == 3) {
+    // All nine window loads in flight at once.  The first in-bounds pixel of
+    // the window (it always exists: pad < k) stands in for out-of-bounds
+    // taps, which leaves the maximum unchanged.
+    const int32_t y0 = oy * stride - pad, x0 = ox * stride - pad;
+    const int32_t fy = y0 < 0 ? 0 : y0, fx = x0 < 0 ? 0 : x0;
+    const uint8_t* base = x + static_cast<int64_t>(img) * h * w * c_store + g * 16;
+    uint4 v[9];
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        int32_t iy = y0 + ky, ix = x0 + kx;
+        const bool in = iy >= 0 && iy < h && ix >= 0 && ix < w;
+        iy = in ? iy : fy;
+        ix = in ? ix : fx;
+        v[ky * 3 + kx] = __ldg(reinterpret_cast<const uint4*>(
+            base + (static_cast<int64_t>(iy) * w + ix) * c_store));
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+      if (is_signed) {
+        best.x = __vmaxs4(best.x, v[t].x); best.y = __vmaxs4(best.y, v[t].y);
+        best.z = __vmaxs4(best.z, v[t].z); best.w = __vmaxs4(best.w, v[t].w);
+      } else {
+        best.x = __vmaxu4(best.x, v[t].x); best.y = __vmaxu4(best.y, v[t].y);
+        best.z = __vmaxu4(best.z, v[t].z); best.w = __vmaxu4(best.w, v[t].w);
+      }
+    }
+    reinterpret_cast<uint4*>(y)[pix * groups + g] = best;
+    return;
+  }
   for (int ky = 0; ky < k; ++ky) {
     const int32_t iy = oy * stride - pad + ky;
     if (iy < 0 || iy >= h) continue;

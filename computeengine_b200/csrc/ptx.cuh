@@ -268,6 +268,18 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The same wait, naming the registers a pending load writes: the compiler
+// then cannot move their uses above the wait (used when a load is left in
+// flight while other registers are processed).
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile (tcgen05 format,
 // version 1).  layout: 0 none, 2 128B swizzle, 4 64B swizzle, 6 32B swizzle.
 // sbo = byte distance between consecutive 8-row groups; lbo = byte distance

@@ -272,6 +272,7 @@ typedef struct {
   int32_t out_bufs;       /* staged output tiles (int8 requantized output) */
   int32_t row_band;
   int32_t grid;           /* CTAs launched */
+  int32_t a_tiled;        /* 1x1 stride-1 unpadded: A loaded as a 2D [pixels, channels] tile */
 } ie_conv_plan;
 int ie_cuda_last_plan(ie_conv_plan* out);
 
