@@ -7,12 +7,17 @@
 //                                    every tensor to <dir> (raw little-endian,
 //                                    with manifest.txt) for the Python side
 //                                    to check against the oracle
+//   ie_cuda_backend_test quant <dir> runs the int8 quantizer on seeded host
+//                                    tensors (no GPU) and writes its outputs
+//                                    for the Python side to check
 //
 // The cases follow the reference's Conv2DOp tests
 // (tests/unit/traditional_ops_test.cpp:82-340): attribute errors are
 // InvalidArgument, a non-F32 input is Unsupported.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -22,6 +27,7 @@
 #include <vector>
 
 #include "cuda_conv_ops.h"
+#include "int8_quant.h"
 
 using ie::Error;
 
@@ -141,6 +147,67 @@ int run_cpu() {
   expect(has_code(conv.forward({&x.t, &w.t}, outs, no_alloc), Error::Code::InvalidArgument),
          "missing allocator rejected");
 
+  // int8 quantizer: the reference plugin contract and its error codes
+  {
+    ie_b200::Int8QuantPlugin plug;
+    const ie::PluginMeta meta = plug.meta();
+    expect(meta.name == "int8_quant" && meta.api_version == "0.1", "quant plugin meta");
+    HostTensor wt({2, 3}, ie::DType::F32);
+    const float wv[6] = {1.0f, -0.5f, 0.25f, 0.0f, 0.0f, 0.0f};
+    std::memcpy(wt.data<float>(), wv, sizeof(wv));
+    ie::QuantConfig sym;  // int8, symmetric
+    auto q = plug.quantize(wt.t, sym);
+    expect(q.has_value() && q->dtype == ie::DType::I8 && q->shape.dims == wt.t.shape.dims,
+           "symmetric quantize gives I8 of the same shape");
+    if (q.has_value()) {
+      const int8_t* qv = q->data<int8_t>();
+      // channel 0: scale 1/127, -63.5 rounds to even (-64), 31.75 -> 32; channel 1 all zero
+      expect(qv[0] == 127 && qv[1] == -64 && qv[2] == 32 && qv[3] == 0 && qv[5] == 0,
+             "per-channel symmetric known answer");
+      const ie_b200::QuantParams* p = plug.params(*q);
+      expect(p != nullptr && p->per_channel && p->scales.size() == 2 && p->scales[1] == 1.0f,
+             "params kept with the result (all-zero channel has scale 1)");
+      auto back = plug.dequantize(*q, sym);
+      expect(back.has_value() && back->dtype == ie::DType::F32 &&
+                 back->data<float>()[0] == 127.0f * p->scales[0],
+             "dequantize with the kept parameters");
+    }
+    ie::QuantConfig four = sym;
+    four.bits = 4;
+    expect(!plug.quantize(wt.t, four).has_value() &&
+               plug.quantize(wt.t, four).error().code == Error::Code::Unsupported,
+           "4-bit quantization is Unsupported");
+    ie::QuantConfig gguf = sym;
+    gguf.format = "gguf";
+    expect(plug.quantize(wt.t, gguf).error().code == Error::Code::Unsupported,
+           "unknown format is Unsupported");
+    HostTensor wi({2, 3}, ie::DType::I8);
+    expect(plug.quantize(wi.t, sym).error().code == Error::Code::Unsupported,
+           "non-F32 input is Unsupported");
+    HostTensor nan_t({3}, ie::DType::F32);
+    nan_t.data<float>()[0] = 0.0f;
+    nan_t.data<float>()[1] = std::nanf("");
+    nan_t.data<float>()[2] = 1.0f;
+    expect(plug.quantize(nan_t.t, sym).error().code == Error::Code::InvalidArgument,
+           "non-finite value is InvalidArgument");
+    ie::Tensor empty;
+    empty.shape = ie::Shape{{0}};
+    expect(plug.quantize(empty, sym).error().code == Error::Code::InvalidArgument,
+           "empty tensor is InvalidArgument");
+    HostTensor foreign({3}, ie::DType::I8);
+    expect(plug.dequantize(foreign.t, sym).error().code == Error::Code::NotFound,
+           "dequantize of a foreign tensor is NotFound");
+    ie_b200::ActivationCalibrator cal;
+    expect(!cal.params().has_value(), "empty calibrator has no range");
+    ie_b200::QuantParams xp = ie_b200::u8_params_for_range(0.0f, 2.55f);
+    ie_b200::QuantParams bad_w = xp;  // U8 where int8 weights are expected
+    expect(ie_b200::make_qlinear_conv_attrs({}, xp, bad_w, xp, 1, nullptr,
+                                            ie_b200::FusedActivation::None)
+                   .error()
+                   .code == Error::Code::InvalidArgument,
+           "qlinear attrs reject uint8 weights");
+  }
+
   int count = 0;
   const bool has_gpu = cudaGetDeviceCount(&count) == cudaSuccess && count > 0;
   cudaGetLastError();
@@ -257,9 +324,172 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "q8_bias", bt.t);
     dump(dir, manifest, "q8_y", y);
   }
+  // int8 post-training quantization of an fp32 Conv2D + ReLU: calibrate the
+  // input and output ranges on the fp32 op, quantize, run the int8 op with
+  // the emitted attributes, dequantize
+  {
+    Lcg rng(4);
+    const int64_t n = 2, c = 32, h = 20, w = 20, m = 48;
+    HostTensor x({n, c, h, w}, ie::DType::F32), wt({m, c, 3, 3}, ie::DType::F32),
+        b({m}, ie::DType::F32);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    for (int64_t i = 0; i < wt.t.numel(); ++i) wt.data<float>()[i] = rng.uniform(-0.1f, 0.1f);
+    for (int64_t i = 0; i < m; ++i) b.data<float>()[i] = rng.uniform(-0.05f, 0.05f);
+    const ie::Attrs conv_attrs{{"pads", std::vector<int64_t>{1, 1, 1, 1}}};
+    ie_b200::CudaConv2DOp fp;
+    fp.configure(conv_attrs);
+    ie::Tensor yf;
+    std::vector<ie::Tensor*> outs{&yf};
+    ie::Status st = fp.forward({&x.t, &wt.t, &b.t}, outs, ctx);
+    expect(st.has_value(), "PTQ: fp32 forward");
+    if (!st.has_value()) return 4;
+    for (int64_t i = 0; i < yf.numel(); ++i) {
+      yf.data<float>()[i] = std::max(yf.data<float>()[i], 0.0f);  // the ReLU node
+    }
+    ie_b200::ActivationCalibrator cal_x, cal_y;
+    expect(cal_x.observe(x.t).has_value() && cal_y.observe(yf).has_value(), "PTQ: calibrate");
+    ie_b200::Int8QuantPlugin plug;
+    auto xp = cal_x.params(), yp = cal_y.params();
+    auto wq = plug.quantize(wt.t, ie::QuantConfig{});
+    auto xq = plug.quantize_with(x.t, *xp);
+    expect(xp.has_value() && yp.has_value() && wq.has_value() && xq.has_value(),
+           "PTQ: quantize weights and input");
+    if (!wq.has_value() || !xq.has_value()) return 4;
+    auto attrs = ie_b200::make_qlinear_conv_attrs(conv_attrs, *xp, *plug.params(*wq), *yp, m,
+                                                  b.data<float>(), ie_b200::FusedActivation::Relu);
+    expect(attrs.has_value(), "PTQ: qlinear attrs");
+    if (!attrs.has_value()) return 4;
+    ie_b200::CudaQLinearConv2DOp qop;
+    expect(qop.configure(*attrs).has_value(), "PTQ: QLinearConv2D configure");
+    ie::Tensor yq;
+    std::vector<ie::Tensor*> qouts{&yq};
+    st = qop.forward({&*xq, &*wq}, qouts, ctx);
+    expect(st.has_value(), "PTQ: QLinearConv2D forward");
+    if (!st.has_value()) return 4;
+    auto ydq = plug.dequantize_with(yq, *yp);
+    expect(ydq.has_value(), "PTQ: dequantize output");
+    if (!ydq.has_value()) return 4;
+    const auto& mult = std::get<std::vector<double>>(attrs->at("multiplier"));
+    const auto& bias = std::get<std::vector<int64_t>>(attrs->at("bias"));
+    HostTensor mt({m}, ie::DType::F32), bt({m}, ie::DType::F32), zp({3}, ie::DType::F32);
+    for (int64_t i = 0; i < m; ++i) {
+      mt.data<float>()[i] = static_cast<float>(mult[static_cast<size_t>(i)]);
+      bt.data<float>()[i] = static_cast<float>(bias[static_cast<size_t>(i)]);  // |bias| < 2^24
+    }
+    zp.data<float>()[0] = static_cast<float>(xp->zero_point);
+    zp.data<float>()[1] = static_cast<float>(yp->zero_point);
+    zp.data<float>()[2] = static_cast<float>(std::get<int64_t>(attrs->at("qmin")));
+    dump(dir, manifest, "ptq_yf", yf);
+    dump(dir, manifest, "ptq_ydq", *ydq);
+    dump(dir, manifest, "ptq_xq", *xq);
+    dump(dir, manifest, "ptq_wq", *wq);
+    dump(dir, manifest, "ptq_yq", yq);
+    dump(dir, manifest, "ptq_mult", mt.t);
+    dump(dir, manifest, "ptq_bias", bt.t);
+    dump(dir, manifest, "ptq_zp", zp.t);
+  }
   cudaStreamDestroy(stream);
   std::printf("%s (%d failures)\n", g_failures == 0 ? "PASSED" : "FAILED", g_failures);
   return g_failures == 0 ? 0 : 1;
+}
+
+// ------------------------------------------------------------ quantizer
+
+int run_quant(const std::string& dir) {
+  std::ofstream manifest(dir + "/manifest.txt");
+  ie_b200::Int8QuantPlugin plug;
+  Lcg rng(11);
+  // weights: per-channel symmetric, one channel all zero, one with a single value
+  HostTensor w({16, 8, 3, 3}, ie::DType::F32);
+  for (int64_t i = 0; i < w.t.numel(); ++i) w.data<float>()[i] = rng.uniform(-0.3f, 0.3f);
+  for (int64_t i = 0; i < 72; ++i) w.data<float>()[3 * 72 + i] = 0.0f;
+  for (int64_t i = 0; i < 72; ++i) w.data<float>()[5 * 72 + i] = (i == 7) ? -0.02f : 0.0f;
+  auto wq = plug.quantize(w.t, ie::QuantConfig{});
+  // activations: asymmetric uint8 over the tensor's own range
+  HostTensor x({3, 5, 7, 9}, ie::DType::F32);
+  for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-0.7f, 2.3f);
+  ie::QuantConfig asym;
+  asym.symmetric = false;
+  auto xq = plug.quantize(x.t, asym);
+  // per-tensor symmetric
+  ie::QuantConfig pt;
+  pt.format = "int8_per_tensor";
+  auto wt = plug.quantize(w.t, pt);
+  // percentile calibration over two batches
+  HostTensor a1({4096}, ie::DType::F32), a2({4096}, ie::DType::F32);
+  for (int64_t i = 0; i < 4096; ++i) {
+    a1.data<float>()[i] = rng.uniform(0.0f, 1.0f);
+    a2.data<float>()[i] = rng.uniform(-0.2f, 3.0f);
+  }
+  a2.data<float>()[17] = 40.0f;  // an outlier the percentile range drops
+  ie_b200::ActivationCalibrator cal(99.9), mm;
+  cal.observe(a1.t);
+  cal.observe(a2.t);
+  mm.observe(a1.t);
+  mm.observe(a2.t);
+  auto cp = cal.params(), mp = mm.params();
+  if (!wq.has_value() || !xq.has_value() || !wt.has_value() || !cp.has_value() || !mp.has_value()) {
+    std::printf("FAILED: quantize\n");
+    return 1;
+  }
+  // layer attributes from those parameters (bias small enough to be exact in fp32)
+  HostTensor bias({16}, ie::DType::F32);
+  for (int64_t i = 0; i < 16; ++i) bias.data<float>()[i] = rng.uniform(-0.02f, 0.02f);
+  const ie_b200::QuantParams yq = ie_b200::u8_params_for_range(0.0f, 4.0f);
+  auto attrs = ie_b200::make_qlinear_conv_attrs({}, *plug.params(*xq), *plug.params(*wq), yq, 16,
+                                                bias.data<float>(),
+                                                ie_b200::FusedActivation::Relu6);
+  if (!attrs.has_value()) {
+    std::printf("FAILED: attrs %s\n", attrs.error().message.c_str());
+    return 1;
+  }
+  HostTensor ws({16}, ie::DType::F32), xs({2}, ie::DType::F32), wts({1}, ie::DType::F32),
+      cal_t({6}, ie::DType::F32), mt({16}, ie::DType::F32), bt({16}, ie::DType::F32),
+      qclamp({3}, ie::DType::F32);
+  for (int i = 0; i < 16; ++i) ws.data<float>()[i] = plug.params(*wq)->scales[i];
+  xs.data<float>()[0] = plug.params(*xq)->scales[0];
+  xs.data<float>()[1] = static_cast<float>(plug.params(*xq)->zero_point);
+  wts.data<float>()[0] = plug.params(*wt)->scales[0];
+  cal_t.data<float>()[0] = cp->scales[0];
+  cal_t.data<float>()[1] = static_cast<float>(cp->zero_point);
+  cal_t.data<float>()[2] = mp->scales[0];
+  cal_t.data<float>()[3] = static_cast<float>(mp->zero_point);
+  cal_t.data<float>()[4] = mm.lo();
+  cal_t.data<float>()[5] = mm.hi();
+  const auto& mult = std::get<std::vector<double>>(attrs->at("multiplier"));
+  const auto& bq = std::get<std::vector<int64_t>>(attrs->at("bias"));
+  for (int i = 0; i < 16; ++i) {
+    mt.data<float>()[i] = static_cast<float>(mult[i]);
+    bt.data<float>()[i] = static_cast<float>(bq[i]);
+  }
+  qclamp.data<float>()[0] = static_cast<float>(std::get<int64_t>(attrs->at("qmin")));
+  qclamp.data<float>()[1] = static_cast<float>(std::get<int64_t>(attrs->at("qmax")));
+  qclamp.data<float>()[2] = static_cast<float>(std::get<int64_t>(attrs->at("y_zero_point")));
+  dump(dir, manifest, "w", w.t);
+  dump(dir, manifest, "wq", *wq);
+  dump(dir, manifest, "w_scales", ws.t);
+  dump(dir, manifest, "x", x.t);
+  dump(dir, manifest, "xq", *xq);
+  dump(dir, manifest, "x_params", xs.t);
+  dump(dir, manifest, "wt", *wt);
+  dump(dir, manifest, "wt_scale", wts.t);
+  dump(dir, manifest, "a1", a1.t);
+  dump(dir, manifest, "a2", a2.t);
+  dump(dir, manifest, "cal", cal_t.t);
+  dump(dir, manifest, "bias", bias.t);
+  dump(dir, manifest, "mult", mt.t);
+  dump(dir, manifest, "bias_q", bt.t);
+  dump(dir, manifest, "clamp", qclamp.t);
+  auto wdq = plug.dequantize(*wq, ie::QuantConfig{});
+  auto xdq = plug.dequantize(*xq, asym);
+  if (!wdq.has_value() || !xdq.has_value()) {
+    std::printf("FAILED: dequantize\n");
+    return 1;
+  }
+  dump(dir, manifest, "wdq", *wdq);
+  dump(dir, manifest, "xdq", *xdq);
+  std::printf("PASSED\n");
+  return 0;
 }
 
 }  // namespace
@@ -267,6 +497,7 @@ int run_gpu(const std::string& dir) {
 int main(int argc, char** argv) {
   if (argc >= 2 && std::strcmp(argv[1], "cpu") == 0) return run_cpu();
   if (argc >= 3 && std::strcmp(argv[1], "gpu") == 0) return run_gpu(argv[2]);
-  std::fprintf(stderr, "usage: %s cpu | gpu <outdir>\n", argv[0]);
+  if (argc >= 3 && std::strcmp(argv[1], "quant") == 0) return run_quant(argv[2]);
+  std::fprintf(stderr, "usage: %s cpu | gpu <outdir> | quant <outdir>\n", argv[0]);
   return 2;
 }

@@ -12,6 +12,8 @@
 //   Op                            src/core/ops/op.h:27-54
 //   OpType (the two conv kinds)   src/core/ir/op_type.h:25-26
 //   OpRegistry                    src/core/ops/op_registry.h:15-30, op_registry.cpp:23-50
+//   PluginMeta                    src/core/plugin/plugin_meta.h:8-14
+//   QuantConfig / QuantPlugin     src/core/plugin/quant_plugin.h:11-28
 // Built inside the reference tree with IE_B200_REFERENCE_HEADERS defined (and
 // the reference's src/ on the include path), it includes the reference's own
 // headers instead and the ops compile against the real types unchanged.
@@ -22,6 +24,7 @@
 #include "core/ir/op_type.h"
 #include "core/ops/op.h"
 #include "core/ops/op_registry.h"
+#include "core/plugin/quant_plugin.h"
 
 #else
 
@@ -228,6 +231,28 @@ class OpRegistry {
  private:
   mutable std::mutex mutex_;
   std::unordered_map<OpType, Creator> creators_;
+};
+
+struct PluginMeta {
+  std::string name;
+  std::string version;
+  std::string api_version;
+  std::vector<std::string> tags;
+  std::string description;
+};
+
+struct QuantConfig {
+  std::string format;
+  int bits{8};
+  bool symmetric{true};
+};
+
+class QuantPlugin {
+ public:
+  virtual ~QuantPlugin() = default;
+  virtual PluginMeta meta() const = 0;
+  virtual Result<Tensor> quantize(const Tensor& tensor, const QuantConfig& config) = 0;
+  virtual Result<Tensor> dequantize(const Tensor& tensor, const QuantConfig& config) = 0;
 };
 
 // Host allocator (malloc/free), the engine's default for CPU tensors.

@@ -1,6 +1,8 @@
 """The C++ ops (CudaConv2DOp, its depthwise form, CudaQLinearConv2DOp) driven
 through the reference-shaped Op / OpRegistry interface on host tensors, checked
-against the oracle: fp32 within max|err| <= 1e-3 * max|ref|, int8 bit-exact."""
+against the oracle: fp32 within max|err| <= 1e-3 * max|ref|, int8 bit-exact;
+and the int8 post-training quantization flow (calibrate, quantize, int8 op,
+dequantize) against the fp32 op."""
 import subprocess
 
 import numpy as np
@@ -34,3 +36,19 @@ def test_cpp_ops_match_oracle(oracle, tmp_path):
                             pads=(1, 1, 1, 1))
     np.testing.assert_array_equal(t["q8_y"], want)
     assert (want == 0).any() and (want > 0).mean() > 0.2
+
+    # int8 post-training quantization of a Conv2D + ReLU (calibrated on the
+    # fp32 op): the int8 step is bit-exact with the oracle on the quantized
+    # tensors and attributes the quantizer emitted, and the dequantized
+    # output stays within the quantization error of the fp32 result
+    # (max |err| <= 5% and mean |err| <= 0.5% of max |ref|: input, weight and
+    # output steps of 1/255 of their ranges over a 288-term sum)
+    zp_x, zp_y, qmin = (int(v) for v in t["ptq_zp"])
+    want = oracle.conv2d_q8(t["ptq_xq"], t["ptq_wq"], t["ptq_bias"].astype(np.int32),
+                            t["ptq_mult"], zp_x, zp_y, qmin, 255, pads=(1, 1, 1, 1))
+    np.testing.assert_array_equal(t["ptq_yq"], want)
+    ref = t["ptq_yf"]
+    err = np.abs(t["ptq_ydq"] - ref)
+    scale = float(np.abs(ref).max())
+    assert err.max() <= 0.05 * scale, (err.max(), scale)
+    assert err.mean() <= 0.005 * scale, (err.mean(), scale)
