@@ -161,15 +161,15 @@ using LaunchFn = int (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorM
 template <int BN, int BKB, bool I8, bool AS>
 LaunchFn pick_bn_bk(int m_sub, bool b_res) {
   if constexpr (I8) {
-    // The requantize epilogue is the limiter of the small-K layers.  Tiles
-    // up to 128 columns use 16 epilogue warps (2 sub-tiles x 2 column
-    // groups x 4 lane quarters); 256-column tiles use 8 warps of 128 columns
-    // each, which leaves ~135 registers per thread instead of 96 for
-    // interleaving the requantize chains (measured 2-7% faster than 16).
+    // The requantize epilogue is the limiter of the small-K layers.  It runs
+    // on 8 warps (4 lane quarters x 2 sub-tiles or x 2 column groups) rather
+    // than 16: ~125-135 registers per thread instead of 96 let each warp
+    // interleave more requantize chains, which measured 3-12% faster per
+    // layer than twice the warps.
     if constexpr (BN <= 128) {
       if (m_sub == 2) {
-        return b_res ? launch_variant<BN, BKB, 16, 2, true, I8, AS>
-                     : launch_variant<BN, BKB, 16, 2, false, I8, AS>;
+        return b_res ? launch_variant<BN, BKB, 8, 2, true, I8, AS>
+                     : launch_variant<BN, BKB, 8, 2, false, I8, AS>;
       }
       return nullptr;
     } else {
@@ -234,7 +234,7 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   if (v.bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
                               static_cast<long long>(x_c_store));
   v.m_sub = (i8 && v.bn <= 128) ? 2 : 1;
-  v.epi = i8 ? (v.bn >= 256 ? 8 : 16) : (v.bn >= 256 ? 8 : 4);
+  v.epi = i8 ? 8 : (v.bn >= 256 ? 8 : 4);
   const int64_t bk_elems = v.bkb / elem_bytes;
   const int64_t cblocks = ceil_div(x_c_store, bk_elems);
   const int64_t taps = d->kh * d->kw;
