@@ -11,8 +11,10 @@ in HBM.  ``value`` is whole-job int8 TOPS (2 ops per MAC, 8.174 GOP per image
 counted on the real 7x7 stem); ``e2e`` is the same metric through the C ABI
 with host buffers: every step's pinned H2D of its input and D2H of its output
 are inside the timed region, on a second stream and double-buffered so that
-they overlap the neighbouring steps' compute.  The working set (5.6 GB of activations per step) is far
-larger than L2, so no flush is needed between steps.
+they overlap the neighbouring steps' compute; with N > 1 each rank first binds
+to the CPUs of its GPU's NUMA node so that its pinned buffers live there.  The
+working set (5.6 GB of activations per step) is far larger than L2, so no
+flush is needed between steps.
 
 ``--impl reference`` times the reference engine's own CPU convolution
 (Conv2DOp compiled from its sources, fp32, run on the dequantized stack, one
@@ -350,10 +352,17 @@ def run_ours(args, world, rank, local):
     from computeengine_b200 import _lib as L
     from computeengine_b200.resnet import (ResNet50Q8, macs_per_image, make_input_u8,
                                            make_q8_params, resnet50_layers)
-    from computeengine_b200.shard import broadcast_from_rank0, input_seed, max_over_ranks, shard_batch
+    from computeengine_b200.shard import (bind_to_pci_local_cpus, broadcast_from_rank0,
+                                          input_seed, max_over_ranks, shard_batch)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    prev_affinity = None
+    if world > 1:
+        # every rank's pinned input and output buffers on its GPU's NUMA node
+        props = torch.cuda.get_device_properties(dev)
+        prev_affinity = bind_to_pci_local_cpus(props.pci_domain_id, props.pci_bus_id,
+                                               props.pci_device_id)
     layers = resnet50_layers(IMAGE)
     ops_img = 2 * macs_per_image(layers)
     b = args.batch
@@ -443,6 +452,9 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), dev)
     e2e_value = ops_img * total_images / (e2e_ms / 1e3) / 1e12
+
+    if prev_affinity is not None:
+        os.sched_setaffinity(0, prev_affinity)
 
     # ---- CPU baseline (rank 0, single GPU runs only)
     cpu = None

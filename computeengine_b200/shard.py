@@ -10,7 +10,9 @@ src/train/distributed/distributed.h:29-34).
 """
 from __future__ import annotations
 
-from typing import Iterable, Tuple
+import os
+from pathlib import Path
+from typing import Iterable, List, Optional, Set, Tuple
 
 
 def shard_batch(global_batch: int, world: int, rank: int) -> Tuple[int, int]:
@@ -50,3 +52,51 @@ def max_over_ranks(value: float, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def parse_cpulist(text: str) -> List[int]:
+    """CPU ids of a sysfs cpulist such as "0-3,8,10-11"."""
+    cpus: List[int] = []
+    for part in text.strip().split(","):
+        part = part.strip()
+        if not part:
+            continue
+        if "-" in part:
+            lo, hi = part.split("-", 1)
+            cpus.extend(range(int(lo), int(hi) + 1))
+        else:
+            cpus.append(int(part))
+    return cpus
+
+
+def pci_local_cpus(domain: int, bus: int, device: int,
+                   sysfs: str = "/sys/bus/pci/devices") -> Optional[List[int]]:
+    """CPUs attached to the same NUMA node as a PCI device (function 0), or
+    None when sysfs does not say."""
+    path = Path(sysfs) / f"{domain:04x}:{bus:02x}:{device:02x}.0" / "local_cpulist"
+    try:
+        cpus = parse_cpulist(path.read_text())
+    except (OSError, ValueError):
+        return None
+    return cpus or None
+
+
+def bind_to_pci_local_cpus(domain: int, bus: int, device: int,
+                           sysfs: str = "/sys/bus/pci/devices") -> Optional[Set[int]]:
+    """Restricts this process to the CPUs local to a GPU's PCI address
+    (intersected with its current affinity), so that pinned host buffers it
+    allocates afterwards are placed on the GPU's own NUMA node by first touch
+    and its copies do not cross the socket link.  Returns the previous
+    affinity (for os.sched_setaffinity to restore), or None when nothing was
+    changed (no sysfs entry, no overlap, or no affinity support)."""
+    if not hasattr(os, "sched_getaffinity"):
+        return None
+    local = pci_local_cpus(domain, bus, device, sysfs)
+    if local is None:
+        return None
+    prev = set(os.sched_getaffinity(0))
+    want = prev & set(local)
+    if not want or want == prev:
+        return None
+    os.sched_setaffinity(0, want)
+    return prev

@@ -52,3 +52,44 @@ def test_two_gloo_ranks_broadcast_and_max():
         assert ok
         assert sent == 64 * 4 + 10 * 4
         assert m == 4.5
+
+
+def test_parse_cpulist():
+    from computeengine_b200.shard import parse_cpulist
+    assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    assert parse_cpulist("5") == [5]
+    assert parse_cpulist("") == []
+
+
+def test_pci_local_cpus_reads_sysfs(tmp_path):
+    from computeengine_b200.shard import pci_local_cpus
+    dev = tmp_path / "0000:1b:00.0"
+    dev.mkdir()
+    (dev / "local_cpulist").write_text("0-1,4\n")
+    assert pci_local_cpus(0, 0x1B, 0, sysfs=str(tmp_path)) == [0, 1, 4]
+    assert pci_local_cpus(0, 0x2B, 0, sysfs=str(tmp_path)) is None  # no such device
+
+
+def test_bind_to_pci_local_cpus_intersects_and_restores(tmp_path):
+    import os
+    from computeengine_b200.shard import bind_to_pci_local_cpus
+    if not hasattr(os, "sched_getaffinity"):
+        pytest.skip("no CPU affinity on this platform")
+    before = set(os.sched_getaffinity(0))
+    one = min(before)
+    dev = tmp_path / "0000:00:05.0"
+    dev.mkdir()
+    # a local set that overlaps the current affinity in one CPU, plus CPUs it lacks
+    (dev / "local_cpulist").write_text(f"{one},{max(before) + 1}-{max(before) + 4}\n")
+    prev = bind_to_pci_local_cpus(0, 0, 5, sysfs=str(tmp_path))
+    try:
+        if len(before) == 1:
+            assert prev is None  # already bound to that CPU: nothing to change
+        else:
+            assert prev == before and set(os.sched_getaffinity(0)) == {one}
+    finally:
+        os.sched_setaffinity(0, before)
+    # no overlap at all: affinity left alone
+    (dev / "local_cpulist").write_text(f"{max(before) + 10}\n")
+    assert bind_to_pci_local_cpus(0, 0, 5, sysfs=str(tmp_path)) is None
+    assert set(os.sched_getaffinity(0)) == before
