@@ -42,6 +42,12 @@ class ConvShape(C.Structure):
                                     "out_h", "out_w")]
 
 
+class PoolDesc(C.Structure):
+    _fields_ = [(n, _i64) for n in ("n", "c", "h", "w", "kh", "kw", "stride_h", "stride_w",
+                                    "pad_top", "pad_left", "pad_bottom", "pad_right")] + \
+               [("auto_pad", _i32), ("ceil_mode", _i32), ("count_include_pad", _i32)]
+
+
 class Q8Params(C.Structure):
     _fields_ = [(n, _i32) for n in ("x_signed", "zp_x", "y_signed", "zp_y", "qmin", "qmax")]
 
@@ -92,6 +98,12 @@ def _load() -> C.CDLL:
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
         "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
+        "ie_pool2d_resolve": (C.c_int, [P(PoolDesc), P(ConvShape)]),
+        "ie_cuda_pool2d_f32": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
+        "ie_cuda_global_avg_pool_f32": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _p]),
+        "ie_cuda_gemm_f32_workspace_bytes": (C.c_size_t, [_i64, _i64, _i64, _i32, _i32]),
+        "ie_cuda_gemm_f32": (C.c_int, [_i64, _i64, _i64, _i32, _i32, C.c_float, C.c_float, _p,
+                                       _p, _p, _i32, _p, _p, C.c_size_t, _p]),
         "ie_cuda_f32x2_maxpool2d": (C.c_int, [_p, _p] + [_i64] * 7 + [_p]),
     }
     for name, (res, args) in sig.items():

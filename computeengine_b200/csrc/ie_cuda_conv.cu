@@ -15,6 +15,7 @@
 #include "direct_kernels.cuh"
 #include "host_util.h"
 #include "layout_kernels.cuh"
+#include "pool_gemm_kernels.cuh"
 #include "ptx.cuh"
 
 using namespace ie_cuda;
@@ -958,6 +959,181 @@ int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x, 
   }
   if ((rc = ie_cuda_f32_pack_weights(desc, w, packed, stream)) != IE_OK) return rc;
   return ie_cuda_conv2d_bf16x3(desc, act, x_split, packed, bias, y, IE_Y_F32_NCHW, stream);
+}
+
+// ------------------------------------------------------------ head ops
+
+int ie_pool2d_resolve(const ie_pool2d_desc* d, ie_conv2d_shape* out) {
+  if (d == nullptr || out == nullptr) return fail(IE_INVALID_ARGUMENT, "null descriptor");
+  if (d->n <= 0 || d->c <= 0 || d->h <= 0 || d->w <= 0) {
+    return fail(IE_INVALID_ARGUMENT, "Pooling expects positive dimensions");
+  }
+  if (d->kh <= 0 || d->kw <= 0) return fail(IE_INVALID_ARGUMENT, "kernel_shape values must be positive");
+  if (d->stride_h <= 0 || d->stride_w <= 0) return fail(IE_INVALID_ARGUMENT, "strides must be positive");
+  int64_t pt = d->pad_top, pl = d->pad_left, pb = d->pad_bottom, pr = d->pad_right;
+  if (pt < 0 || pl < 0 || pb < 0 || pr < 0) return fail(IE_INVALID_ARGUMENT, "pads must be non-negative");
+  auto same = [](int64_t in, int64_t k, int64_t s, bool lower, int64_t* b, int64_t* a) {
+    const int64_t o = (in + s - 1) / s;
+    const int64_t total = std::max<int64_t>(0, (o - 1) * s + k - in);
+    int64_t before = total / 2, after = total - before;
+    if (lower) std::swap(before, after);
+    *b = before;
+    *a = after;
+  };
+  if (d->auto_pad == IE_PAD_VALID) {
+    pt = pl = pb = pr = 0;
+  } else if (d->auto_pad == IE_PAD_SAME_UPPER || d->auto_pad == IE_PAD_SAME_LOWER) {
+    const bool lower = d->auto_pad == IE_PAD_SAME_LOWER;
+    same(d->h, d->kh, d->stride_h, lower, &pt, &pb);
+    same(d->w, d->kw, d->stride_w, lower, &pl, &pr);
+  } else if (d->auto_pad != IE_PAD_NOTSET) {
+    return fail(IE_INVALID_ARGUMENT, "unsupported auto_pad");
+  }
+  const int64_t span_h = d->h + pt + pb, span_w = d->w + pl + pr;
+  if (span_h < d->kh || span_w < d->kw) return fail(IE_INVALID_ARGUMENT, "Pool kernel exceeds padded input");
+  int64_t oh, ow;
+  if (d->ceil_mode) {
+    oh = ceil_div(span_h - d->kh, d->stride_h) + 1;
+    ow = ceil_div(span_w - d->kw, d->stride_w) + 1;
+    if ((oh - 1) * d->stride_h >= d->h + pt) --oh;  // a last window starting in the padding
+    if ((ow - 1) * d->stride_w >= d->w + pl) --ow;
+  } else {
+    oh = (span_h - d->kh) / d->stride_h + 1;
+    ow = (span_w - d->kw) / d->stride_w + 1;
+  }
+  if (oh <= 0 || ow <= 0) return fail(IE_INVALID_ARGUMENT, "Pool produces an empty output");
+  out->pad_top = pt;
+  out->pad_left = pl;
+  out->pad_bottom = pb;
+  out->pad_right = pr;
+  out->out_h = oh;
+  out->out_w = ow;
+  return IE_OK;
+}
+
+int ie_cuda_pool2d_f32(const ie_pool2d_desc* d, int32_t max_pool, const float* x, float* y,
+                       void* stream) {
+  ie_conv2d_shape s;
+  int rc = ie_pool2d_resolve(d, &s);
+  if (rc != IE_OK) return rc;
+  if (x == nullptr || y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  if (d->h > INT32_MAX || d->w > INT32_MAX || d->kh > INT32_MAX || d->kw > INT32_MAX ||
+      d->stride_h > INT32_MAX || d->stride_w > INT32_MAX || s.out_h * s.out_w > INT32_MAX ||
+      s.pad_top + s.pad_bottom + d->h > INT32_MAX || s.pad_left + s.pad_right + d->w > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "pooling extent too large");
+  }
+  Pool2dArgs a;
+  a.planes = d->n * d->c;
+  a.h = static_cast<int32_t>(d->h);
+  a.w = static_cast<int32_t>(d->w);
+  a.out_h = static_cast<int32_t>(s.out_h);
+  a.out_w = static_cast<int32_t>(s.out_w);
+  a.kh = static_cast<int32_t>(d->kh);
+  a.kw = static_cast<int32_t>(d->kw);
+  a.stride_h = static_cast<int32_t>(d->stride_h);
+  a.stride_w = static_cast<int32_t>(d->stride_w);
+  a.pad_t = static_cast<int32_t>(s.pad_top);
+  a.pad_l = static_cast<int32_t>(s.pad_left);
+  a.pad_b = static_cast<int32_t>(s.pad_bottom);
+  a.pad_r = static_cast<int32_t>(s.pad_right);
+  a.max_pool = max_pool ? 1 : 0;
+  a.count_include_pad = d->count_include_pad ? 1 : 0;
+  const int64_t total = a.planes * s.out_h * s.out_w;
+  pool2d_f32_nchw<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(x, y, a);
+  return check_launch("pool2d_f32_nchw");
+}
+
+int ie_cuda_global_avg_pool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h,
+                                int64_t w, void* stream) {
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) {
+    return fail(IE_INVALID_ARGUMENT, "GlobalAvgPool expects positive dimensions");
+  }
+  if (x == nullptr || y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  const int64_t planes = n * c;
+  global_avg_pool_f32<<<grid_1d(planes, 128), 128, 0, as_stream(stream)>>>(x, y, planes, h * w);
+  return check_launch("global_avg_pool_f32");
+}
+
+namespace {
+
+// 1x1 convolution view of a Gemm: M "pixels" of K channels against N filters.
+ie_conv2d_desc gemm_as_conv(int64_t m, int64_t n, int64_t k) {
+  ie_conv2d_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.n = m;
+  d.c = k;
+  d.h = d.w = 1;
+  d.m = n;
+  d.kh = d.kw = 1;
+  d.stride_h = d.stride_w = d.dil_h = d.dil_w = 1;
+  d.group = 1;
+  return d;
+}
+
+int transpose(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st) {
+  if (ceil_div(rows, 32) > 65535) return fail(IE_UNSUPPORTED, "transpose: too many rows");
+  const dim3 grid(static_cast<unsigned>(ceil_div(cols, 32)), static_cast<unsigned>(ceil_div(rows, 32)));
+  transpose_f32<<<grid, dim3(32, 8), 0, st>>>(in, out, rows, cols);
+  return check_launch("transpose_f32");
+}
+
+}  // namespace
+
+size_t ie_cuda_gemm_f32_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t trans_a,
+                                        int32_t trans_b) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const ie_conv2d_desc d = gemm_as_conv(m, n, k);
+  size_t bytes = ie_cuda_conv2d_f32_workspace_bytes(&d);
+  if (trans_a) bytes += static_cast<size_t>(round_up(m * k * 4, 256));
+  if (!trans_b) bytes += static_cast<size_t>(round_up(n * k * 4, 256));
+  bytes += static_cast<size_t>(round_up(m * n * 4, 256));  // product before the epilogue
+  return bytes;
+}
+
+int ie_cuda_gemm_f32(int64_t m, int64_t n, int64_t k, int32_t trans_a, int32_t trans_b,
+                     float alpha, float beta, const float* a, const float* b, const float* c,
+                     int32_t c_mode, float* y, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (m <= 0 || n <= 0 || k <= 0) return fail(IE_INVALID_ARGUMENT, "Gemm expects positive dimensions");
+  if (a == nullptr || b == nullptr || y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  if (c_mode < IE_GEMM_C_NONE || c_mode > IE_GEMM_C_FULL) return fail(IE_INVALID_ARGUMENT, "bad C mode");
+  if (c_mode != IE_GEMM_C_NONE && c == nullptr) return fail(IE_INVALID_ARGUMENT, "C is null");
+  const size_t need = ie_cuda_gemm_f32_workspace_bytes(m, n, k, trans_a, trans_b);
+  if (workspace == nullptr || workspace_bytes < need) {
+    return fail(IE_INVALID_ARGUMENT, "Gemm workspace too small (%zu < %zu)", workspace_bytes, need);
+  }
+  const cudaStream_t st = as_stream(stream);
+  const ie_conv2d_desc d = gemm_as_conv(m, n, k);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* conv_ws = ws;
+  ws += round_up(static_cast<int64_t>(ie_cuda_conv2d_f32_workspace_bytes(&d)), 256);
+  int rc;
+  const float* a_rows = a;  // [M, K]
+  if (trans_a) {
+    float* t = reinterpret_cast<float*>(ws);
+    ws += round_up(m * k * 4, 256);
+    if ((rc = transpose(a, t, k, m, st)) != IE_OK) return rc;
+    a_rows = t;
+  }
+  const float* b_rows = b;  // [N, K]
+  if (!trans_b) {
+    float* t = reinterpret_cast<float*>(ws);
+    ws += round_up(n * k * 4, 256);
+    if ((rc = transpose(b, t, k, n, st)) != IE_OK) return rc;
+    b_rows = t;
+  }
+  const bool fused = c_mode == IE_GEMM_C_COLUMN && alpha == 1.0f && beta == 1.0f;
+  if (fused || (c_mode == IE_GEMM_C_NONE && alpha == 1.0f)) {
+    return ie_cuda_conv2d_f32(&d, IE_ACT_NONE, a_rows, b_rows, fused ? c : nullptr, y, conv_ws,
+                              ie_cuda_conv2d_f32_workspace_bytes(&d), stream);
+  }
+  float* p = reinterpret_cast<float*>(ws);
+  if ((rc = ie_cuda_conv2d_f32(&d, IE_ACT_NONE, a_rows, b_rows, nullptr, p, conv_ws,
+                               ie_cuda_conv2d_f32_workspace_bytes(&d), stream)) != IE_OK) {
+    return rc;
+  }
+  gemm_epilogue_f32<<<grid_1d(m * n, 256), 256, 0, st>>>(p, y, m, n, alpha, beta, c, c_mode);
+  return check_launch("gemm_epilogue_f32");
 }
 
 size_t ie_cuda_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }

@@ -259,6 +259,64 @@ int ie_cuda_take_device_error(uint32_t* code);
  * since the last reset (for the benchmark's launch count). */
 uint64_t ie_cuda_launch_count(int reset);
 
+/* ---------------------------------------------------------------- head ops
+ * The rest of a ResNet graph's head on the GPU, so no node falls back to the
+ * host: 2D pooling, global average pooling and Gemm over fp32 tensors. */
+
+/* Pooling attributes and shape, the union of PoolConfig (pool_ops.h:13-21)
+ * and the NCHW input shape pool2d_forward reads (pool_ops.cpp:131-136). */
+typedef struct ie_pool2d_desc {
+  int64_t n, c, h, w;
+  int64_t kh, kw;                                    /* kernel_shape */
+  int64_t stride_h, stride_w;
+  int64_t pad_top, pad_left, pad_bottom, pad_right;  /* the "pads" attribute */
+  int32_t auto_pad;                                  /* IE_PAD_* */
+  int32_t ceil_mode;
+  int32_t count_include_pad;
+} ie_pool2d_desc;
+
+/* Effective pads and output extent (resolve_pool_geometry, pool_ops.cpp:24-61):
+ * SAME pads split like convolution, ceil_mode drops a last window that would
+ * start in the padding; IE_INVALID_ARGUMENT for a window larger than the
+ * padded input or an empty output. */
+int ie_pool2d_resolve(const ie_pool2d_desc* desc, ie_conv2d_shape* out);
+
+/* Max (max_pool = 1) or average pooling, NCHW fp32 -> [n, c, out_h, out_w]
+ * (pool2d_forward, pool_ops.cpp:111-215, behind MaxPool2DOp / AvgPool2DOp,
+ * pool_ops.h:37-68).  Same window order and arithmetic as the reference:
+ * results equal it bit for bit. */
+int ie_cuda_pool2d_f32(const ie_pool2d_desc* desc, int32_t max_pool, const float* x, float* y,
+                       void* stream);
+
+/* [n, c, h, w] -> [n, c, 1, 1] mean over each plane (global_avg_pool_forward,
+ * pool_ops.cpp:217-270, behind GlobalAvgPoolOp): one sequential fp32 sum per
+ * plane, bit-exact with the reference. */
+int ie_cuda_global_avg_pool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h,
+                                int64_t w, void* stream);
+
+/* C broadcast of Gemm (gemm_op.cpp:103-139). */
+enum {
+  IE_GEMM_C_NONE = 0,   /* no C */
+  IE_GEMM_C_SCALAR = 1, /* one value */
+  IE_GEMM_C_ROW = 2,    /* [M] or [M, 1]: C(i, j) = c[i] */
+  IE_GEMM_C_COLUMN = 3, /* [N] or [1, N]: C(i, j) = c[j] */
+  IE_GEMM_C_FULL = 4    /* [M, N] */
+};
+
+/* Y[M, N] = alpha * A' * B' + beta * C, A' = A [M, K] or A^T (trans_a, A is
+ * [K, M]), B' = B [K, N] or B^T (trans_b, B is [N, K]) — the drop-in for
+ * GemmOp::forward (gemm_op.cpp:76-221).  The product runs on the tensor cores
+ * as bf16x3 (a 1x1 convolution over M "pixels" of K channels), accurate to
+ * about 1e-5 relative; a column C with alpha = beta = 1 is fused as the
+ * convolution's bias, anything else goes through a separate epilogue.
+ * workspace must hold ie_cuda_gemm_f32_workspace_bytes(...) bytes. */
+size_t ie_cuda_gemm_f32_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t trans_a,
+                                        int32_t trans_b);
+int ie_cuda_gemm_f32(int64_t m, int64_t n, int64_t k, int32_t trans_a, int32_t trans_b,
+                     float alpha, float beta, const float* a, const float* b, const float* c,
+                     int32_t c_mode, float* y, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
 /* Tile plan of the last implicit-GEMM launch issued on the calling host thread
  * (performance introspection; no counterpart in the reference).  row_band is 1
  * when the stride-1 row-band mode ran: tiles of whole output rows, one input

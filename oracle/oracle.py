@@ -205,6 +205,52 @@ class RefConv:
         return rc, (y if rc == OK else None)
 
 
+    def pool2d(self, x, kernel=(1, 1), strides=(1, 1), pads=(0, 0, 0, 0), auto_pad="NOTSET",
+               ceil_mode=0, count_include_pad=0, kind="max"):
+        """The reference MaxPool2DOp / AvgPool2DOp / GlobalAvgPoolOp (kind "max",
+        "avg", "global").  Returns (status, y)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        k = np.array(kernel, np.int64)
+        s = np.array(strides, np.int64)
+        p = np.array(pads, np.int64)
+        dims = np.zeros(4, np.int64)
+        mode = {"max": 1, "avg": 0, "global": 2}[kind]
+        f = self.lib.ref_pool2d_f32
+        f.restype = C.c_int
+        args = [_ptr(x), *[C.c_int64(v) for v in x.shape], C.c_int(mode), _ptr(k), _ptr(s),
+                _ptr(p), C.c_int(AUTO_PAD[auto_pad]), C.c_int(ceil_mode),
+                C.c_int(count_include_pad)]
+        rc = f(*args, None, C.c_int64(0), _ptr(dims))
+        if rc != OK:
+            return rc, None
+        y = np.empty(tuple(int(v) for v in dims), np.float32)
+        rc = f(*args, _ptr(y), C.c_int64(y.size), _ptr(dims))
+        return rc, (y if rc == OK else None)
+
+    def gemm(self, a, b, c=None, alpha=1.0, beta=1.0, trans_a=0, trans_b=0):
+        """The reference GemmOp.  Returns (status, y)."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        m = a.shape[1] if trans_a else a.shape[0]
+        n = b.shape[0] if trans_b else b.shape[1]
+        cd = np.zeros(2, np.int64)
+        cp, nd = None, 0
+        if c is not None:
+            c = np.ascontiguousarray(c, dtype=np.float32)
+            nd = c.ndim
+            cd[:nd] = c.shape
+            cp = _ptr(c)
+        y = np.empty((max(m, 1), max(n, 1)), np.float32)
+        dims = np.zeros(2, np.int64)
+        f = self.lib.ref_gemm_f32
+        f.restype = C.c_int
+        rc = f(_ptr(a), C.c_int64(a.shape[0]), C.c_int64(a.shape[1]), _ptr(b),
+               C.c_int64(b.shape[0]), C.c_int64(b.shape[1]), cp, C.c_int(nd), _ptr(cd),
+               C.c_double(alpha), C.c_double(beta), C.c_int(trans_a), C.c_int(trans_b), _ptr(y),
+               C.c_int64(y.size), _ptr(dims))
+        return rc, (y if rc == OK else None)
+
+
 def host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))

@@ -21,6 +21,8 @@
 #include "core/memory/malloc_allocator.h"
 #include "core/ops/kernel_fns.h"
 #include "ops/traditional/conv2d_op.h"
+#include "ops/traditional/gemm_op.h"
+#include "ops/traditional/pool_ops.h"
 
 namespace {
 
@@ -189,6 +191,89 @@ int ref_conv2d_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w,
         if (v != 0) return v;
     }
     if (out_dims != nullptr) out_dims[0] = n;
+    return 0;
+}
+
+// Runs the reference MaxPool2DOp (max_pool = 1), AvgPool2DOp (0) or
+// GlobalAvgPoolOp (2) on a host fp32 NCHW buffer.  pads = {top, left,
+// bottom, right}; kernel / strides ignored for the global pool.  out_dims
+// receives the output shape; y (may be NULL for a shape query) must hold
+// y_capacity floats.  Returns 0 or 1 + the reference Error::Code, or
+// kShapeMismatch when y is too small.
+int ref_pool2d_f32(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int max_pool,
+                   const int64_t* kernel, const int64_t* strides, const int64_t* pads,
+                   int auto_pad, int ceil_mode, int count_include_pad, float* y,
+                   int64_t y_capacity, int64_t* out_dims) {
+    ie::Attrs attrs;
+    if (max_pool != 2) {
+        attrs["kernel_shape"] = std::vector<int64_t>{kernel[0], kernel[1]};
+        attrs["strides"] = std::vector<int64_t>{strides[0], strides[1]};
+        attrs["pads"] = std::vector<int64_t>{pads[0], pads[1], pads[2], pads[3]};
+        static const char* kAuto[] = {"NOTSET", "VALID", "SAME_UPPER", "SAME_LOWER"};
+        if (auto_pad > 0 && auto_pad < 4) attrs["auto_pad"] = std::string(kAuto[auto_pad]);
+        attrs["ceil_mode"] = static_cast<int64_t>(ceil_mode);
+        attrs["count_include_pad"] = static_cast<int64_t>(count_include_pad);
+    }
+    std::unique_ptr<ie::Op> op;
+    if (max_pool == 1) {
+        op = std::make_unique<ie::MaxPool2DOp>();
+    } else if (max_pool == 0) {
+        op = std::make_unique<ie::AvgPool2DOp>();
+    } else {
+        op = std::make_unique<ie::GlobalAvgPoolOp>();
+    }
+    if (auto st = op->configure(attrs); !st.has_value()) return code_of(st.error());
+    auto alloc = std::make_shared<ie::MallocAllocator>();
+    ie::Tensor xt = host_tensor({n, c, h, w}, x, alloc);
+    std::vector<ie::Tensor> out(1);
+    std::vector<ie::Tensor*> outputs{&out[0]};
+    ie::ExecutionContext ctx;
+    ctx.allocator = alloc;
+    if (auto st = op->forward({&xt}, outputs, ctx); !st.has_value()) return code_of(st.error());
+    const auto& d = out[0].shape.dims;
+    for (int i = 0; i < 4; ++i) out_dims[i] = d[i];
+    if (y != nullptr) {
+        if (out[0].numel() > y_capacity) return kShapeMismatch;
+        std::memcpy(y, out[0].data<float>(), static_cast<size_t>(out[0].numel()) * sizeof(float));
+    }
+    return 0;
+}
+
+// Runs the reference GemmOp: a [a0, a1], b [b0, b1], optional c with
+// c_ndim (0..2) dims c_dims; y must hold y_capacity floats; out_dims gets
+// [M, N].
+int ref_gemm_f32(const float* a, int64_t a0, int64_t a1, const float* b, int64_t b0, int64_t b1,
+                 const float* c, int c_ndim, const int64_t* c_dims, double alpha, double beta,
+                 int trans_a, int trans_b, float* y, int64_t y_capacity, int64_t* out_dims) {
+    ie::Attrs attrs;
+    attrs["alpha"] = alpha;
+    attrs["beta"] = beta;
+    attrs["transA"] = static_cast<int64_t>(trans_a);
+    attrs["transB"] = static_cast<int64_t>(trans_b);
+    ie::GemmOp op;
+    if (auto st = op.configure(attrs); !st.has_value()) return code_of(st.error());
+    auto alloc = std::make_shared<ie::MallocAllocator>();
+    ie::Tensor at = host_tensor({a0, a1}, a, alloc);
+    ie::Tensor bt = host_tensor({b0, b1}, b, alloc);
+    ie::Tensor ct;
+    std::vector<ie::Tensor*> inputs{&at, &bt};
+    if (c != nullptr) {
+        std::vector<int64_t> dims(c_dims, c_dims + c_ndim);
+        ct = host_tensor(dims, c, alloc);
+        inputs.push_back(&ct);
+    }
+    int which = 0;
+    ie::KernelFns fns = select_kernels(&which);
+    std::vector<ie::Tensor> out(1);
+    std::vector<ie::Tensor*> outputs{&out[0]};
+    ie::ExecutionContext ctx;
+    ctx.allocator = alloc;
+    ctx.kernels = &fns;
+    if (auto st = op.forward(inputs, outputs, ctx); !st.has_value()) return code_of(st.error());
+    out_dims[0] = out[0].shape.dims[0];
+    out_dims[1] = out[0].shape.dims[1];
+    if (out[0].numel() > y_capacity) return kShapeMismatch;
+    std::memcpy(y, out[0].data<float>(), static_cast<size_t>(out[0].numel()) * sizeof(float));
     return 0;
 }
 
