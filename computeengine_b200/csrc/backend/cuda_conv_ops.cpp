@@ -50,6 +50,23 @@ ie::Status read_int(const ie::Attrs& attrs, const char* key, bool* found, int64_
   return ie::Error::invalid_argument(std::string("attribute '") + key + "' must be an int");
 }
 
+ie::Status read_double(const ie::Attrs& attrs, const char* key, bool* found, double* value) {
+  *found = false;
+  const auto it = attrs.find(key);
+  if (it == attrs.end()) return {};
+  if (const auto* v = std::get_if<double>(&it->second)) {
+    *found = true;
+    *value = *v;
+    return {};
+  }
+  if (const auto* v = std::get_if<int64_t>(&it->second)) {
+    *found = true;
+    *value = static_cast<double>(*v);
+    return {};
+  }
+  return ie::Error::invalid_argument(std::string("attribute '") + key + "' must be numeric");
+}
+
 ie::Status read_double_list(const ie::Attrs& attrs, const char* key, bool* found,
                             std::vector<double>* out) {
   *found = false;
@@ -594,14 +611,271 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   return {};
 }
 
-ie::Status register_cuda_ops(ie::OpRegistry& registry) {
-  if (auto st = registry.register_op(ie::OpType::Conv2D,
-                                     [] { return std::make_unique<CudaConv2DOp>(false); });
-      !st.has_value()) {
-    return st;
+// ------------------------------------------------ pooling and Gemm
+
+namespace {
+
+// Host NCHW F32 out of a device buffer: allocate outputs[0] and copy back.
+ie::Status download_f32(const void* ydev, ie::Shape shape, ie::ExecutionContext& context,
+                        std::vector<ie::Tensor*>& outputs, cudaStream_t st) {
+  auto out = ie::Tensor::allocate(shape, ie::DType::F32, context.allocator);
+  if (!out.has_value()) return out.error();
+  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, ydev, out->bytes(), cudaMemcpyDeviceToHost, st),
+                           "cudaMemcpyAsync D2H");
+      !e.has_value()) {
+    return e;
   }
-  return registry.register_op(ie::OpType::DepthwiseConv2D,
-                              [] { return std::make_unique<CudaConv2DOp>(true); });
+  if (auto e = finish(st); !e.has_value()) return e;
+  *outputs[0] = std::move(*out);
+  return {};
+}
+
+// Device copy of a constant input (weights, bias), uploaded once per host buffer.
+ie::Result<const void*> cached_const(DeviceBuffers& dev, const ie::Tensor& t, int kind,
+                                     cudaStream_t st) {
+  if (t.device == ie::Device::CUDA) return static_cast<const void*>(t.buffer);
+  bool fresh = false;
+  auto slot = dev.cached(t.buffer, t.bytes(), kind, &fresh);
+  if (!slot.has_value()) return slot.error();
+  if (fresh) {
+    if (auto e = cuda_status(cudaMemcpyAsync(*slot, t.buffer, t.bytes(), cudaMemcpyHostToDevice, st),
+                             "cudaMemcpyAsync H2D");
+        !e.has_value()) {
+      return e.error();
+    }
+  }
+  return static_cast<const void*>(*slot);
+}
+
+ie::Status validate_unary(const std::vector<ie::Tensor*>& inputs,
+                          std::vector<ie::Tensor*>& outputs, const ie::ExecutionContext& context,
+                          const char* name) {
+  if (inputs.size() != 1 || outputs.size() != 1 || outputs[0] == nullptr) {
+    return ie::Error::invalid_argument(std::string(name) + " expects one input and one output");
+  }
+  if (context.allocator == nullptr) {
+    return ie::Error::invalid_argument(std::string(name) + " requires an allocator");
+  }
+  if (inputs[0] == nullptr || inputs[0]->buffer == nullptr) {
+    return ie::Error::invalid_argument("null tensor or buffer");
+  }
+  if (inputs[0]->dtype != ie::DType::F32) return ie::Error::unsupported("P0 kernels support F32 only");
+  const auto& dims = inputs[0]->shape.dims;
+  if (dims.size() != 4) return ie::Error::invalid_argument(std::string(name) + " expects 4D NCHW tensors");
+  for (int64_t v : dims) {
+    if (v <= 0) return ie::Error::invalid_argument(std::string(name) + " expects positive dimensions");
+  }
+  return {};
+}
+
+}  // namespace
+
+ie::Status parse_pool_config(const ie::Attrs& attrs, PoolConfig& config) {
+  config = PoolConfig{};
+  IntListAttr kernel;
+  if (auto st = read_int_list(attrs, "kernel_shape", kernel); !st.has_value()) return st;
+  if (!kernel.found || kernel.values.empty()) return ie::Error::invalid_argument("kernel_shape is required");
+  if (kernel.values.size() != 2) return ie::Error::invalid_argument("kernel_shape must contain 2 values");
+  if (kernel.values[0] <= 0 || kernel.values[1] <= 0) {
+    return ie::Error::invalid_argument("kernel_shape values must be positive");
+  }
+  config.has_kernel_shape = true;
+  config.kernel_shape = {kernel.values[0], kernel.values[1]};
+  if (auto st = read_pair(attrs, "strides", config.strides); !st.has_value()) return st;
+  if (auto st = read_pads(attrs, config.pads); !st.has_value()) return st;
+  if (auto st = read_auto_pad(attrs, config.auto_pad); !st.has_value()) return st;
+  bool found = false;
+  int64_t v = 0;
+  if (auto st = read_int(attrs, "ceil_mode", &found, &v); !st.has_value()) return st;
+  config.ceil_mode = found && v != 0;
+  if (auto st = read_int(attrs, "count_include_pad", &found, &v); !st.has_value()) return st;
+  config.count_include_pad = found && v != 0;
+  return {};
+}
+
+ie::Status CudaPool2DOp::configure(const ie::Attrs& attrs) { return parse_pool_config(attrs, config_); }
+
+ie::Status CudaPool2DOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                 std::vector<ie::Tensor*>& outputs,
+                                 ie::ExecutionContext& context) {
+  if (auto st = validate_unary(inputs, outputs, context, "Pooling"); !st.has_value()) return st;
+  if (!config_.has_kernel_shape) return ie::Error::invalid_argument("kernel_shape is required");
+  const ie::Tensor& x = *inputs[0];
+  ie_pool2d_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.n = x.shape.dims[0];
+  d.c = x.shape.dims[1];
+  d.h = x.shape.dims[2];
+  d.w = x.shape.dims[3];
+  d.kh = config_.kernel_shape[0];
+  d.kw = config_.kernel_shape[1];
+  d.stride_h = config_.strides[0];
+  d.stride_w = config_.strides[1];
+  d.pad_top = config_.pads[0];
+  d.pad_left = config_.pads[1];
+  d.pad_bottom = config_.pads[2];
+  d.pad_right = config_.pads[3];
+  d.auto_pad = config_.auto_pad == AutoPad::Valid       ? IE_PAD_VALID
+               : config_.auto_pad == AutoPad::SameUpper ? IE_PAD_SAME_UPPER
+               : config_.auto_pad == AutoPad::SameLower ? IE_PAD_SAME_LOWER
+                                                        : IE_PAD_NOTSET;
+  d.ceil_mode = config_.ceil_mode ? 1 : 0;
+  d.count_include_pad = config_.count_include_pad ? 1 : 0;
+  ie_conv2d_shape s;
+  if (auto st = to_status(ie_pool2d_resolve(&d, &s)); !st.has_value()) return st;
+  if (auto st = require_device(); !st.has_value()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(d.n * d.c * s.out_h * s.out_w) * sizeof(float));
+  if (!ydev.has_value()) return ydev.error();
+  if (auto e = to_status(ie_cuda_pool2d_f32(&d, max_pool_ ? 1 : 0, static_cast<const float*>(*xd),
+                                            static_cast<float*>(*ydev), st));
+      !e.has_value()) {
+    return e;
+  }
+  return download_f32(*ydev, ie::Shape{{d.n, d.c, s.out_h, s.out_w}}, context, outputs, st);
+}
+
+ie::Status CudaGlobalAvgPoolOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                        std::vector<ie::Tensor*>& outputs,
+                                        ie::ExecutionContext& context) {
+  if (auto st = validate_unary(inputs, outputs, context, "GlobalAvgPool"); !st.has_value()) return st;
+  if (auto st = require_device(); !st.has_value()) return st;
+  const ie::Tensor& x = *inputs[0];
+  const auto& dm = x.shape.dims;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(dm[0] * dm[1]) * sizeof(float));
+  if (!ydev.has_value()) return ydev.error();
+  if (auto e = to_status(ie_cuda_global_avg_pool_f32(static_cast<const float*>(*xd),
+                                                     static_cast<float*>(*ydev), dm[0], dm[1],
+                                                     dm[2], dm[3], st));
+      !e.has_value()) {
+    return e;
+  }
+  return download_f32(*ydev, ie::Shape{{dm[0], dm[1], 1, 1}}, context, outputs, st);
+}
+
+ie::Status CudaGemmOp::configure(const ie::Attrs& attrs) {
+  alpha_ = beta_ = 1.0;
+  trans_a_ = trans_b_ = 0;
+  bool found = false;
+  double d = 0.0;
+  if (auto st = read_double(attrs, "alpha", &found, &d); !st.has_value()) return st;
+  if (found) alpha_ = d;
+  if (auto st = read_double(attrs, "beta", &found, &d); !st.has_value()) return st;
+  if (found) beta_ = d;
+  int64_t v = 0;
+  if (auto st = read_int(attrs, "transA", &found, &v); !st.has_value()) return st;
+  if (found) {
+    if (v != 0 && v != 1) return ie::Error::invalid_argument("Gemm transA must be 0 or 1");
+    trans_a_ = v;
+  }
+  if (auto st = read_int(attrs, "transB", &found, &v); !st.has_value()) return st;
+  if (found) {
+    if (v != 0 && v != 1) return ie::Error::invalid_argument("Gemm transB must be 0 or 1");
+    trans_b_ = v;
+  }
+  return {};
+}
+
+ie::Status CudaGemmOp::forward(const std::vector<ie::Tensor*>& inputs,
+                               std::vector<ie::Tensor*>& outputs, ie::ExecutionContext& context) {
+  if ((inputs.size() != 2 && inputs.size() != 3) || outputs.size() != 1 || outputs[0] == nullptr) {
+    return ie::Error::invalid_argument("Gemm expects two or three inputs and one output");
+  }
+  if (context.allocator == nullptr) return ie::Error::invalid_argument("Gemm requires an allocator");
+  for (const ie::Tensor* t : inputs) {
+    if (t == nullptr || t->buffer == nullptr) return ie::Error::invalid_argument("null tensor or buffer");
+    if (t->dtype != ie::DType::F32) return ie::Error::unsupported("P0 kernels support F32 only");
+  }
+  const ie::Tensor& a = *inputs[0];
+  const ie::Tensor& b = *inputs[1];
+  if (a.shape.dims.size() != 2 || b.shape.dims.size() != 2) {
+    return ie::Error::invalid_argument("Gemm expects 2D A and B tensors");
+  }
+  const int64_t m = trans_a_ ? a.shape.dims[1] : a.shape.dims[0];
+  const int64_t k_a = trans_a_ ? a.shape.dims[0] : a.shape.dims[1];
+  const int64_t k_b = trans_b_ ? b.shape.dims[1] : b.shape.dims[0];
+  const int64_t n = trans_b_ ? b.shape.dims[0] : b.shape.dims[1];
+  if (m <= 0 || k_a <= 0 || n <= 0 || k_b <= 0) {
+    return ie::Error::invalid_argument("Gemm expects positive dimensions");
+  }
+  if (k_a != k_b) return ie::Error::invalid_argument("Gemm inner dimensions mismatch");
+  // C broadcast, the reference's rules (gemm_op.cpp:103-139)
+  int32_t c_mode = IE_GEMM_C_NONE;
+  const ie::Tensor* c = inputs.size() == 3 ? inputs[2] : nullptr;
+  if (c != nullptr) {
+    const auto& dims = c->shape.dims;
+    if (dims.empty() || c->numel() == 1) {
+      c_mode = IE_GEMM_C_SCALAR;
+    } else if (dims.size() == 1) {
+      if (dims[0] == n) {
+        c_mode = IE_GEMM_C_COLUMN;
+      } else if (dims[0] == m) {
+        c_mode = IE_GEMM_C_ROW;
+      } else {
+        return ie::Error::invalid_argument("Gemm bias must broadcast to [M,N]");
+      }
+    } else if (dims.size() == 2) {
+      if (dims[0] == m && dims[1] == n) {
+        c_mode = IE_GEMM_C_FULL;
+      } else if (dims[0] == m && dims[1] == 1) {
+        c_mode = IE_GEMM_C_ROW;
+      } else if (dims[0] == 1 && dims[1] == n) {
+        c_mode = IE_GEMM_C_COLUMN;
+      } else {
+        return ie::Error::invalid_argument("Gemm bias must broadcast to [M,N]");
+      }
+    } else {
+      return ie::Error::invalid_argument("Gemm bias must broadcast to [M,N]");
+    }
+  }
+  if (auto st = require_device(); !st.has_value()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto ad = to_device(dev_, kSlotX, a, st);
+  if (!ad.has_value()) return ad.error();
+  auto bd = cached_const(dev_, b, kCacheW, st);
+  if (!bd.has_value()) return bd.error();
+  const void* cd = nullptr;
+  if (c != nullptr) {
+    auto r = cached_const(dev_, *c, kCacheBias, st);
+    if (!r.has_value()) return r.error();
+    cd = *r;
+  }
+  const size_t ws_bytes = ie_cuda_gemm_f32_workspace_bytes(m, n, m > 0 ? k_a : 0,
+                                                           static_cast<int32_t>(trans_a_),
+                                                           static_cast<int32_t>(trans_b_));
+  auto ws = dev_.scratch(kSlotWork, ws_bytes);
+  if (!ws.has_value()) return ws.error();
+  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(m * n) * sizeof(float));
+  if (!ydev.has_value()) return ydev.error();
+  if (auto e = to_status(ie_cuda_gemm_f32(
+          m, n, k_a, static_cast<int32_t>(trans_a_), static_cast<int32_t>(trans_b_),
+          static_cast<float>(alpha_), static_cast<float>(beta_), static_cast<const float*>(*ad),
+          static_cast<const float*>(*bd), static_cast<const float*>(cd), c_mode,
+          static_cast<float*>(*ydev), *ws, ws_bytes, st));
+      !e.has_value()) {
+    return e;
+  }
+  return download_f32(*ydev, ie::Shape{{m, n}}, context, outputs, st);
+}
+
+ie::Status register_cuda_ops(ie::OpRegistry& registry) {
+  const std::pair<ie::OpType, ie::OpRegistry::Creator> ops[] = {
+      {ie::OpType::Conv2D, [] { return std::make_unique<CudaConv2DOp>(false); }},
+      {ie::OpType::DepthwiseConv2D, [] { return std::make_unique<CudaConv2DOp>(true); }},
+      {ie::OpType::MaxPool2D, [] { return std::make_unique<CudaPool2DOp>(true); }},
+      {ie::OpType::AvgPool2D, [] { return std::make_unique<CudaPool2DOp>(false); }},
+      {ie::OpType::GlobalAvgPool, [] { return std::make_unique<CudaGlobalAvgPoolOp>(); }},
+      {ie::OpType::Gemm, [] { return std::make_unique<CudaGemmOp>(); }},
+  };
+  for (const auto& [type, creator] : ops) {
+    if (auto st = registry.register_op(type, creator); !st.has_value()) return st;
+  }
+  return {};
 }
 
 }  // namespace ie_b200

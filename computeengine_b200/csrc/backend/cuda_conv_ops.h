@@ -124,7 +124,68 @@ class CudaQLinearConv2DOp final : public ie::Op {
   DeviceBuffers dev_;
 };
 
-// Registers CudaConv2DOp for OpType::Conv2D and OpType::DepthwiseConv2D.  Like
+// Fields and defaults of the reference PoolConfig (pool_ops.h:13-21).
+struct PoolConfig {
+  bool has_kernel_shape{false};
+  std::array<int64_t, 2> kernel_shape{0, 0};
+  std::array<int64_t, 2> strides{1, 1};
+  std::array<int64_t, 4> pads{0, 0, 0, 0};
+  AutoPad auto_pad{AutoPad::NotSet};
+  bool ceil_mode{false};
+  bool count_include_pad{false};
+};
+
+// The reference's parse_pool_config (pool_ops.cpp:66-109): "kernel_shape"
+// (required, two positive values), "strides", "pads", "auto_pad",
+// "ceil_mode", "count_include_pad".
+ie::Status parse_pool_config(const ie::Attrs& attrs, PoolConfig& config);
+
+// CudaPool2DOp(true)  replaces MaxPool2DOp (pool_ops.h:37-51)
+// CudaPool2DOp(false) replaces AvgPool2DOp (pool_ops.h:54-68)
+// NCHW F32 host (or device) tensor in, host NCHW F32 out; bit-exact with the
+// reference (same window order and arithmetic).
+class CudaPool2DOp final : public ie::Op {
+ public:
+  explicit CudaPool2DOp(bool max_pool) : max_pool_(max_pool) {}
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  PoolConfig config_{};
+  bool max_pool_;
+  DeviceBuffers dev_;
+};
+
+// Replaces GlobalAvgPoolOp (pool_ops.h:71-79): [N, C, H, W] -> [N, C, 1, 1].
+class CudaGlobalAvgPoolOp final : public ie::Op {
+ public:
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  DeviceBuffers dev_;
+};
+
+// Replaces GemmOp (gemm_op.h:14-31): Y = alpha * A' * B' + beta * C with the
+// reference's attributes ("alpha", "beta", "transA", "transB") and C
+// broadcasts (scalar, [N], [M], [M,1], [1,N], [M,N]).  B and C stay on the
+// device keyed by their host buffers (the model's weights); the product runs
+// as bf16x3 on the tensor cores.
+class CudaGemmOp final : public ie::Op {
+ public:
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  double alpha_{1.0}, beta_{1.0};
+  int64_t trans_a_{0}, trans_b_{0};
+  DeviceBuffers dev_;
+};
+
+// Registers CudaConv2DOp for OpType::Conv2D and OpType::DepthwiseConv2D, and
+// the pooling and Gemm ops for MaxPool2D, AvgPool2D, GlobalAvgPool and Gemm.  Like
 // the reference registry it fails with AlreadyExists when a type is taken, so
 // call it on a fresh (backend-private) registry or before
 // register_builtin_ops, which skips types already present

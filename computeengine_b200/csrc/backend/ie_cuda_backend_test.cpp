@@ -147,6 +147,47 @@ int run_cpu() {
   expect(has_code(conv.forward({&x.t, &w.t}, outs, no_alloc), Error::Code::InvalidArgument),
          "missing allocator rejected");
 
+  // pooling and Gemm ops: attribute and shape errors as the reference reports them
+  {
+    ie_b200::PoolConfig pc;
+    expect(has_code(ie_b200::parse_pool_config({}, pc), Error::Code::InvalidArgument),
+           "pool without kernel_shape rejected");
+    expect(has_code(ie_b200::parse_pool_config({{"kernel_shape", std::vector<int64_t>{3, 3, 3}}}, pc),
+                    Error::Code::InvalidArgument),
+           "three-value kernel_shape rejected");
+    expect(ie_b200::parse_pool_config({{"kernel_shape", std::vector<int64_t>{3, 3}},
+                                       {"ceil_mode", int64_t{1}}},
+                                      pc)
+                   .has_value() &&
+               pc.ceil_mode && pc.kernel_shape[0] == 3,
+           "pool config parsed");
+    auto mp = reg.create(ie::OpType::MaxPool2D);
+    auto gp = reg.create(ie::OpType::GlobalAvgPool);
+    auto gm = reg.create(ie::OpType::Gemm);
+    expect(mp.has_value() && gp.has_value() && gm.has_value(), "create pool / GAP / Gemm ops");
+    ie_b200::CudaPool2DOp pool(true);
+    pool.configure({{"kernel_shape", std::vector<int64_t>{7, 7}}});
+    expect(has_code(pool.forward({&x.t}, outs, ctx), Error::Code::InvalidArgument),
+           "pool window larger than the input rejected");
+    ie_b200::CudaGlobalAvgPoolOp gap;
+    HostTensor x3({4, 5, 5}, ie::DType::F32);
+    expect(has_code(gap.forward({&x3.t}, outs, ctx), Error::Code::InvalidArgument),
+           "GAP on a 3D tensor rejected");
+    ie_b200::CudaGemmOp gemm;
+    expect(has_code(gemm.configure({{"transA", int64_t{2}}}), Error::Code::InvalidArgument),
+           "Gemm transA = 2 rejected");
+    gemm.configure({});
+    HostTensor ga({4, 5}, ie::DType::F32), gb({6, 3}, ie::DType::F32), gc({7}, ie::DType::F32),
+        gb2({5, 3}, ie::DType::F32);
+    expect(has_code(gemm.forward({&ga.t, &gb.t}, outs, ctx), Error::Code::InvalidArgument),
+           "Gemm inner dimension mismatch rejected");
+    expect(has_code(gemm.forward({&ga.t, &gb2.t, &gc.t}, outs, ctx), Error::Code::InvalidArgument),
+           "Gemm bias that does not broadcast rejected");
+    HostTensor gi({4, 5}, ie::DType::I8);
+    expect(has_code(gemm.forward({&gi.t, &gb2.t}, outs, ctx), Error::Code::Unsupported),
+           "Gemm on int8 is Unsupported");
+  }
+
   // int8 quantizer: the reference plugin contract and its error codes
   {
     ie_b200::Int8QuantPlugin plug;
@@ -323,6 +364,49 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "q8_mult", mt.t);
     dump(dir, manifest, "q8_bias", bt.t);
     dump(dir, manifest, "q8_y", y);
+  }
+  // the head of a ResNet through the registry: max pool, average pool,
+  // global average pool, Gemm (FC with bias)
+  {
+    Lcg rng(5);
+    HostTensor x({2, 16, 15, 13}, ie::DType::F32);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-2.f, 2.f);
+    auto mp = reg.create(ie::OpType::MaxPool2D);
+    auto ap = reg.create(ie::OpType::AvgPool2D);
+    auto gp = reg.create(ie::OpType::GlobalAvgPool);
+    auto gm = reg.create(ie::OpType::Gemm);
+    if (!mp.has_value() || !ap.has_value() || !gp.has_value() || !gm.has_value()) return 3;
+    (*mp)->configure({{"kernel_shape", std::vector<int64_t>{3, 3}},
+                      {"strides", std::vector<int64_t>{2, 2}},
+                      {"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+    (*ap)->configure({{"kernel_shape", std::vector<int64_t>{3, 3}},
+                      {"strides", std::vector<int64_t>{2, 2}},
+                      {"pads", std::vector<int64_t>{1, 1, 1, 1}},
+                      {"ceil_mode", int64_t{1}},
+                      {"count_include_pad", int64_t{1}}});
+    (*gm)->configure({{"transB", int64_t{1}}});
+    ie::Tensor ym, ya, yg, yf;
+    std::vector<ie::Tensor*> om{&ym}, oa{&ya}, og{&yg}, of{&yf};
+    expect((*mp)->forward({&x.t}, om, ctx).has_value(), "MaxPool2D forward");
+    expect((*ap)->forward({&x.t}, oa, ctx).has_value(), "AvgPool2D forward");
+    expect((*gp)->forward({&x.t}, og, ctx).has_value(), "GlobalAvgPool forward");
+    HostTensor feat({2, 16}, ie::DType::F32), wfc({10, 16}, ie::DType::F32), bfc({10}, ie::DType::F32);
+    if (yg.buffer != nullptr) std::memcpy(feat.storage.data(), yg.buffer, feat.t.bytes());
+    for (int64_t i = 0; i < wfc.t.numel(); ++i) wfc.data<float>()[i] = rng.uniform(-0.5f, 0.5f);
+    for (int64_t i = 0; i < 10; ++i) bfc.data<float>()[i] = rng.uniform(-0.1f, 0.1f);
+    const ie::Status gst = (*gm)->forward({&feat.t, &wfc.t, &bfc.t}, of, ctx);
+    expect(gst.has_value(), "Gemm forward");
+    if (!gst.has_value()) std::printf("  %s\n", gst.error().message.c_str());
+    if (ym.buffer == nullptr || ya.buffer == nullptr || yg.buffer == nullptr || yf.buffer == nullptr) {
+      return 4;
+    }
+    dump(dir, manifest, "head_x", x.t);
+    dump(dir, manifest, "head_max", ym);
+    dump(dir, manifest, "head_avg", ya);
+    dump(dir, manifest, "head_gap", yg);
+    dump(dir, manifest, "head_wfc", wfc.t);
+    dump(dir, manifest, "head_bfc", bfc.t);
+    dump(dir, manifest, "head_fc", yf);
   }
   // int8 post-training quantization of an fp32 Conv2D + ReLU: calibrate the
   // input and output ranges on the fp32 op, quantize, run the int8 op with

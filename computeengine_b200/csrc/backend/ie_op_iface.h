@@ -10,7 +10,7 @@
 //   AttrValue / Attrs             src/core/ir/attr.h:12-15
 //   ExecutionContext              src/core/runtime/execution_context.h:17-27
 //   Op                            src/core/ops/op.h:27-54
-//   OpType (the two conv kinds)   src/core/ir/op_type.h:25-26
+//   OpType (the kinds used here)  src/core/ir/op_type.h:25-30 and Gemm
 //   OpRegistry                    src/core/ops/op_registry.h:15-30, op_registry.cpp:23-50
 //   PluginMeta                    src/core/plugin/plugin_meta.h:8-14
 //   QuantConfig / QuantPlugin     src/core/plugin/quant_plugin.h:11-28
@@ -195,7 +195,7 @@ class Op {
                          ExecutionContext& context) = 0;
 };
 
-enum class OpType { Conv2D, DepthwiseConv2D };
+enum class OpType { Conv2D, DepthwiseConv2D, MaxPool2D, AvgPool2D, GlobalAvgPool, Gemm };
 
 // The reference registry is a process singleton with a private constructor;
 // here instances can also be made directly, which is what a backend-private

@@ -2,7 +2,8 @@
 through the reference-shaped Op / OpRegistry interface on host tensors, checked
 against the oracle: fp32 within max|err| <= 1e-3 * max|ref|, int8 bit-exact;
 and the int8 post-training quantization flow (calibrate, quantize, int8 op,
-dequantize) against the fp32 op."""
+dequantize) against the fp32 op; the pooling and Gemm ops through the registry
+against the reference's own ops."""
 import subprocess
 
 import numpy as np
@@ -52,3 +53,28 @@ def test_cpp_ops_match_oracle(oracle, tmp_path):
     scale = float(np.abs(ref).max())
     assert err.max() <= 0.05 * scale, (err.max(), scale)
     assert err.mean() <= 0.005 * scale, (err.mean(), scale)
+
+
+def test_cpp_head_ops_match_reference(refconv, tmp_path):
+    """MaxPool2D, AvgPool2D (ceil_mode, count_include_pad), GlobalAvgPool and
+    Gemm (transB, bias) through the registry against the reference's own ops:
+    pooling bit-exact, Gemm within 1e-3 * max |ref|."""
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    x = t["head_x"]
+    rc, want = refconv.pool2d(x, (3, 3), (2, 2), (1, 1, 1, 1), kind="max")
+    assert rc == 0
+    np.testing.assert_array_equal(t["head_max"], want)
+    rc, want = refconv.pool2d(x, (3, 3), (2, 2), (1, 1, 1, 1), ceil_mode=1, count_include_pad=1,
+                              kind="avg")
+    assert rc == 0
+    np.testing.assert_array_equal(t["head_avg"], want)
+    rc, want = refconv.pool2d(x, kind="global")
+    assert rc == 0
+    np.testing.assert_array_equal(t["head_gap"], want)
+    rc, want = refconv.gemm(want.reshape(2, 16), t["head_wfc"], t["head_bfc"], trans_b=1)
+    assert rc == 0
+    err = float(np.abs(t["head_fc"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
