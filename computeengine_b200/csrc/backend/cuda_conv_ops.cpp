@@ -331,7 +331,22 @@ ie::Result<void*> DeviceBuffers::cached(const void* host_key, size_t bytes, int 
 // ------------------------------------------------ fp32 Conv2D / DepthwiseConv2D
 
 ie::Status CudaConv2DOp::configure(const ie::Attrs& attrs) {
-  return parse_conv_config(attrs, config_);
+  if (auto st = parse_conv_config(attrs, config_); !st.has_value()) return st;
+  // "activation": a Relu / Clip(0, 6) node fused by ConvBnReluFusionPass
+  act_ = IE_ACT_NONE;
+  auto it = attrs.find("activation");
+  if (it != attrs.end()) {
+    const auto* v = std::get_if<std::string>(&it->second);
+    if (v == nullptr) return ie::Error::invalid_argument("attribute 'activation' must be a string");
+    if (*v == "Relu") {
+      act_ = IE_ACT_RELU;
+    } else if (*v == "Relu6") {
+      act_ = IE_ACT_RELU6;
+    } else if (!v->empty()) {
+      return ie::Error::invalid_argument("attribute 'activation' must be Relu or Relu6");
+    }
+  }
+  return {};
 }
 
 ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
@@ -426,10 +441,10 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     if (!xs.has_value()) return xs.error();
     rc = ie_cuda_f32_pack_input(static_cast<const float*>(*xd), *xs, d.n, d.c, d.h, d.w, c_store, st);
     if (rc == IE_OK) {
-      rc = ie_cuda_conv2d_bf16x3(&d, IE_ACT_NONE, *xs, wdev, bdev, *ydev, IE_Y_F32_NCHW, st);
+      rc = ie_cuda_conv2d_bf16x3(&d, act_, *xs, wdev, bdev, *ydev, IE_Y_F32_NCHW, st);
     }
   } else {
-    rc = ie_cuda_conv2d_f32(&d, IE_ACT_NONE, static_cast<const float*>(*xd),
+    rc = ie_cuda_conv2d_f32(&d, act_, static_cast<const float*>(*xd),
                             static_cast<const float*>(wdev), bdev, static_cast<float*>(*ydev),
                             nullptr, 0, st);
   }

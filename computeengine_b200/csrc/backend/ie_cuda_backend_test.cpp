@@ -23,10 +23,12 @@
 #include <cstring>
 #include <fstream>
 #include <memory>
+#include <optional>
 #include <string>
 #include <vector>
 
 #include "cuda_conv_ops.h"
+#include "graph_passes.h"
 #include "int8_quant.h"
 
 using ie::Error;
@@ -71,6 +73,70 @@ ie::ExecutionContext host_context() {
   ie::ExecutionContext ctx;
   ctx.allocator = std::make_shared<ie::MallocAllocator>();
   return ctx;
+}
+
+// x -> Conv2D(w, b) -> BatchNorm(scale, bias, mean, var) -> act -> y, with
+// seeded constants (act: Relu node, or Clip(0, 6) when clip is set).
+struct BnGraph {
+  ie::Graph g;
+  std::vector<std::unique_ptr<HostTensor>> keep;
+};
+
+std::unique_ptr<BnGraph> make_bn_graph(bool clip, int64_t c = 8, int64_t m = 12) {
+  auto bg = std::make_unique<BnGraph>();
+  ie::Graph& g = bg->g;
+  Lcg rng(21);
+  auto value = [&](ie::ValueId id, const char* name, bool in, bool out) {
+    ie::Value v;
+    v.id = id;
+    v.name = name;
+    v.is_input = in;
+    v.is_output = out;
+    g.values.push_back(v);
+  };
+  auto constant = [&](const char* name, std::vector<int64_t> dims, float lo, float hi) {
+    bg->keep.push_back(std::make_unique<HostTensor>(dims, ie::DType::F32));
+    HostTensor& t = *bg->keep.back();
+    for (int64_t i = 0; i < t.t.numel(); ++i) t.data<float>()[i] = rng.uniform(lo, hi);
+    g.weights.emplace(name, t.t);
+  };
+  value(0, "x", true, false);
+  value(1, "w", false, false);
+  value(2, "b", false, false);
+  value(3, "conv_out", false, false);
+  value(4, "bn_scale", false, false);
+  value(5, "bn_bias", false, false);
+  value(6, "bn_mean", false, false);
+  value(7, "bn_var", false, false);
+  value(8, "bn_out", false, false);
+  value(9, "y", false, true);
+  constant("w", {m, c, 3, 3}, -0.3f, 0.3f);
+  constant("b", {m}, -0.1f, 0.1f);
+  constant("bn_scale", {m}, 0.5f, 1.5f);
+  constant("bn_bias", {m}, -0.2f, 0.2f);
+  constant("bn_mean", {m}, -0.3f, 0.3f);
+  constant("bn_var", {m}, 0.2f, 1.2f);
+  ie::Node conv;
+  conv.id = 0;
+  conv.op = ie::OpType::Conv2D;
+  conv.inputs = {0, 1, 2};
+  conv.outputs = {3};
+  conv.attrs = {{"pads", std::vector<int64_t>{1, 1, 1, 1}}};
+  ie::Node bn;
+  bn.id = 1;
+  bn.op = ie::OpType::BatchNorm;
+  bn.inputs = {3, 4, 5, 6, 7};
+  bn.outputs = {8};
+  bn.attrs = {{"epsilon", 1e-3}};
+  ie::Node act;
+  act.id = 2;
+  act.op = clip ? ie::OpType::Clip : ie::OpType::Relu;
+  act.inputs = {8};
+  act.outputs = {9};
+  if (clip) act.attrs = {{"min", 0.0}, {"max", 6.0}};
+  g.nodes = {conv, bn, act};
+  g.edges = {{3, 0u, 1u}, {8, 1u, 2u}, {9, 2u, std::nullopt}};
+  return bg;
 }
 
 // ------------------------------------------------------------ cpu checks
@@ -146,6 +212,59 @@ int run_cpu() {
   ie::ExecutionContext no_alloc;
   expect(has_code(conv.forward({&x.t, &w.t}, outs, no_alloc), Error::Code::InvalidArgument),
          "missing allocator rejected");
+
+  // Conv + BatchNorm + Relu fusion pass on the graph
+  {
+    auto bg = make_bn_graph(false);
+    ie_b200::ConvBnReluFusionPass pass;
+    ie::PassContext pctx;
+    const ie::Status st = pass.run(bg->g, pctx);
+    const ie::Graph& g = bg->g;
+    expect(st.has_value() && pass.folded_batch_norms() == 1 && pass.fused_activations() == 1 &&
+               g.nodes.size() == 1,
+           "conv + BN + Relu fused into one node");
+    if (g.nodes.size() == 1) {
+      const ie::Node& n = g.nodes[0];
+      const auto* act = std::get_if<std::string>(&n.attrs.at("activation"));
+      expect(act != nullptr && *act == "Relu" && n.outputs == std::vector<ie::ValueId>{9} &&
+                 n.inputs.size() == 3 && n.inputs[0] == 0,
+             "fused node writes y with activation Relu");
+      const ie::Value* wv = g.find_value(n.inputs[1]);
+      expect(wv != nullptr && wv->name == "w.bn_folded" && g.weights.count("w.bn_folded") == 1 &&
+                 g.weights.count("w") == 1,
+             "folded weights added beside the originals");
+      expect(g.edges.size() == 1 && g.edges[0].value == 9 && g.edges[0].from.has_value() &&
+                 *g.edges[0].from == 0u,
+             "edges rewired to the fused node");
+    }
+    auto bc = make_bn_graph(true);
+    ie_b200::ConvBnReluFusionPass pass2;
+    expect(pass2.run(bc->g, pctx).has_value() && bc->g.nodes.size() == 1 &&
+               *std::get_if<std::string>(&bc->g.nodes[0].attrs.at("activation")) == "Relu6",
+           "Clip(0, 6) fused as Relu6");
+    auto bo = make_bn_graph(false);
+    for (ie::Value& v : bo->g.values) {
+      if (v.name == "conv_out") v.is_output = true;
+    }
+    ie_b200::ConvBnReluFusionPass pass3;
+    expect(pass3.run(bo->g, pctx).has_value() && bo->g.nodes.size() == 3 &&
+               pass3.folded_batch_norms() == 0,
+           "no fold when the conv output is a graph output");
+    auto bt = make_bn_graph(false);
+    bt->g.nodes[2].inputs = {3};  // a second consumer of the conv output
+    ie_b200::ConvBnReluFusionPass pass4;
+    expect(pass4.run(bt->g, pctx).has_value() && pass4.folded_batch_norms() == 0,
+           "no fold when the conv output has two consumers");
+    auto bv = make_bn_graph(false);
+    bv->keep[5]->data<float>()[3] = -1.0f;  // var + eps < 0
+    ie_b200::ConvBnReluFusionPass pass5;
+    expect(has_code(pass5.run(bv->g, pctx), Error::Code::InvalidArgument),
+           "negative variance rejected");
+    ie_b200::CudaConv2DOp act_op;
+    expect(has_code(act_op.configure({{"activation", std::string("Tanh")}}),
+                    Error::Code::InvalidArgument),
+           "unknown activation rejected");
+  }
 
   // pooling and Gemm ops: attribute and shape errors as the reference reports them
   {
@@ -364,6 +483,38 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "q8_mult", mt.t);
     dump(dir, manifest, "q8_bias", bt.t);
     dump(dir, manifest, "q8_y", y);
+  }
+  // a fused Conv + BatchNorm + Relu node from the fusion pass, run by the
+  // CUDA op with the folded constants and the activation attribute
+  {
+    auto bg = make_bn_graph(false);
+    HostTensor x({2, 8, 11, 9}, ie::DType::F32);
+    Lcg rng(22);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    std::vector<ie::Tensor> orig;
+    for (const char* k : {"w", "b", "bn_scale", "bn_bias", "bn_mean", "bn_var"}) {
+      orig.push_back(bg->g.weights.at(k));
+    }
+    ie_b200::ConvBnReluFusionPass pass;
+    ie::PassContext pctx;
+    expect(pass.run(bg->g, pctx).has_value() && bg->g.nodes.size() == 1, "PASS: fuse");
+    const ie::Node& n = bg->g.nodes[0];
+    auto op = reg.create(n.op);
+    if (!op.has_value()) return 3;
+    expect((*op)->configure(n.attrs).has_value(), "PASS: configure fused conv");
+    ie::Tensor* wf = &bg->g.weights.at(bg->g.find_value(n.inputs[1])->name);
+    ie::Tensor* bf = &bg->g.weights.at(bg->g.find_value(n.inputs[2])->name);
+    ie::Tensor y;
+    std::vector<ie::Tensor*> outs{&y};
+    const ie::Status st = (*op)->forward({&x.t, wf, bf}, outs, ctx);
+    expect(st.has_value(), "PASS: fused conv forward");
+    if (!st.has_value()) return 4;
+    dump(dir, manifest, "bn_x", x.t);
+    const char* names[] = {"bn_w", "bn_b", "bn_scale", "bn_bias", "bn_mean", "bn_var"};
+    for (size_t i = 0; i < orig.size(); ++i) dump(dir, manifest, names[i], orig[i]);
+    dump(dir, manifest, "bn_wf", *wf);
+    dump(dir, manifest, "bn_bf", *bf);
+    dump(dir, manifest, "bn_y", y);
   }
   // the head of a ResNet through the registry: max pool, average pool,
   // global average pool, Gemm (FC with bias)

@@ -10,8 +10,11 @@
 //   AttrValue / Attrs             src/core/ir/attr.h:12-15
 //   ExecutionContext              src/core/runtime/execution_context.h:17-27
 //   Op                            src/core/ops/op.h:27-54
-//   OpType (the kinds used here)  src/core/ir/op_type.h:25-30 and Gemm
+//   OpType (the kinds used here)  src/core/ir/op_type.h
 //   OpRegistry                    src/core/ops/op_registry.h:15-30, op_registry.cpp:23-50
+//   NodeId / ValueId, Value, Node, Edge, Graph (nodes, values, edges,
+//     weights, find_value)        src/core/ir/ids.h, graph.h:27-101
+//   ModelKind, PassContext, Pass  src/core/ir/model_kind.h, pass.h:14-25
 //   PluginMeta                    src/core/plugin/plugin_meta.h:8-14
 //   QuantConfig / QuantPlugin     src/core/plugin/quant_plugin.h:11-28
 // Built inside the reference tree with IE_B200_REFERENCE_HEADERS defined (and
@@ -24,6 +27,7 @@
 #include "core/ir/op_type.h"
 #include "core/ops/op.h"
 #include "core/ops/op_registry.h"
+#include "core/ir/pass.h"
 #include "core/plugin/quant_plugin.h"
 
 #else
@@ -195,7 +199,79 @@ class Op {
                          ExecutionContext& context) = 0;
 };
 
-enum class OpType { Conv2D, DepthwiseConv2D, MaxPool2D, AvgPool2D, GlobalAvgPool, Gemm };
+enum class OpType {
+  Add, Relu, Conv2D, DepthwiseConv2D, MaxPool2D, AvgPool2D, GlobalAvgPool, BatchNorm, Clip, Gemm
+};
+
+using NodeId = uint32_t;
+using ValueId = uint32_t;
+inline constexpr ValueId kInvalidValue = 0xFFFFFFFFu;
+inline constexpr NodeId kInvalidNode = 0xFFFFFFFFu;
+
+enum class ModelKind { TRADITIONAL, TRANSFORMER, HYBRID, RULE, UNKNOWN };
+
+struct Value {
+  ValueId id{kInvalidValue};
+  std::string name;
+  Shape shape;
+  DType dtype{DType::F32};
+  bool is_input{false};
+  bool is_output{false};
+};
+
+struct Node {
+  NodeId id{kInvalidNode};
+  OpType op{OpType::Add};
+  std::vector<ValueId> inputs;
+  std::vector<ValueId> outputs;
+  Attrs attrs;
+  std::optional<Device> placed_device;
+  ModelKind kind{ModelKind::UNKNOWN};
+};
+
+struct Edge {
+  ValueId value{kInvalidValue};
+  std::optional<NodeId> from;
+  std::optional<NodeId> to;
+};
+
+// The slice of the reference Graph a compiler pass over traditional nodes
+// uses: nodes in execution order, values, edges and the constant tensors
+// keyed by value name.
+class Graph {
+ public:
+  std::vector<Node> nodes;
+  std::vector<Value> values;
+  std::vector<Edge> edges;
+  std::unordered_map<std::string, Tensor> weights;
+
+  const Value* find_value(ValueId id) const {
+    for (const Value& v : values) {
+      if (v.id == id) return &v;
+    }
+    return nullptr;
+  }
+  const Value* find_value(const std::string& name) const {
+    for (const Value& v : values) {
+      if (v.name == name) return &v;
+    }
+    return nullptr;
+  }
+};
+
+struct HardwareProfile {};
+
+struct PassContext {
+  HardwareProfile hardware;
+  ModelKind model_kind{ModelKind::UNKNOWN};
+};
+
+class Pass {
+ public:
+  virtual ~Pass() = default;
+  virtual std::string name() const = 0;
+  virtual Status run(Graph& graph, PassContext& context) = 0;
+};
 
 // The reference registry is a process singleton with a private constructor;
 // here instances can also be made directly, which is what a backend-private

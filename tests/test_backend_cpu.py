@@ -3,7 +3,8 @@ attribute parsing and error codes as the reference's Conv2DOp tests assert
 them (tests/unit/traditional_ops_test.cpp:195-222), registry semantics
 (op_registry.cpp:23-50), and forward() failing with Runtime when no CUDA
 device exists (no CPU fallback); the int8 quantizer's plugin contract and
-error codes.  Also compiles the op and quantizer sources against the
+error codes; the Conv + BatchNorm + Relu fusion pass on small graphs.  Also
+compiles the op, quantizer and pass sources against the
 reference's own headers when the reference tree is present, which shows they
 drop into the reference engine unchanged."""
 import os
@@ -30,6 +31,6 @@ def test_cpp_ops_compile_against_reference_headers():
     cmd = ["g++", "-std=c++20", "-fsyntax-only", "-DIE_B200_REFERENCE_HEADERS",
            f"-I{REFERENCE_SRC}", f"-I{ROOT / 'include'}", f"-I{backend}",
            "-I/usr/local/cuda/include", str(backend / "cuda_conv_ops.cpp"),
-           str(backend / "int8_quant.cpp")]
+           str(backend / "int8_quant.cpp"), str(backend / "graph_passes.cpp")]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr

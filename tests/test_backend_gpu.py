@@ -78,3 +78,26 @@ def test_cpp_head_ops_match_reference(refconv, tmp_path):
     assert rc == 0
     err = float(np.abs(t["head_fc"] - want).max())
     assert err <= REL_TOL * float(np.abs(want).max()), err
+
+
+def test_conv_bn_relu_fusion_pass(oracle, tmp_path):
+    """ConvBnReluFusionPass: the folded constants equal the reference's
+    BatchNorm arithmetic applied to the weights (batch_norm_op.cpp:79-86,
+    bit for bit), and the fused Conv2D + Relu run by CudaConv2DOp matches
+    conv -> BatchNorm -> Relu (oracle conv, the reference's BatchNorm formula)
+    within 1e-3 * max |ref|."""
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    f32 = np.float32
+    inv = (1.0 / np.sqrt(t["bn_var"].astype(np.float64) + 1e-3)).astype(f32)
+    gain = t["bn_scale"] * inv
+    shift = t["bn_bias"] - t["bn_mean"] * gain
+    np.testing.assert_array_equal(t["bn_wf"], t["bn_w"] * gain[:, None, None, None])
+    np.testing.assert_array_equal(t["bn_bf"], t["bn_b"] * gain + shift)
+    conv = oracle.conv2d_f32(t["bn_x"], t["bn_w"], t["bn_b"], pads=(1, 1, 1, 1))
+    want = np.maximum(conv * gain[None, :, None, None] + shift[None, :, None, None], f32(0))
+    err = float(np.abs(t["bn_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
+    assert (want == 0).any() and (want > 0).mean() > 0.2
