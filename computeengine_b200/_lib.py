@@ -98,6 +98,10 @@ def _load() -> C.CDLL:
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
         "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
+        "ie_cuda_conv2d_f32_residual": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p, _p,
+                                                  C.c_size_t, _p]),
+        "ie_cuda_conv2d_bf16x3_residual": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p, _i32,
+                                                     _p]),
         "ie_pool2d_resolve": (C.c_int, [P(PoolDesc), P(ConvShape)]),
         "ie_cuda_pool2d_f32": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
         "ie_cuda_global_avg_pool_f32": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _p]),

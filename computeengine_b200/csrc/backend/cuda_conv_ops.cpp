@@ -244,7 +244,7 @@ ie::Status finish(cudaStream_t st) {
   return {};
 }
 
-enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork };
+enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork, kSlotResidual };
 enum CacheKind { kCacheW = 0, kCacheWPacked, kCacheBias, kCacheMult, kCacheBiasI32 };
 
 }  // namespace
@@ -332,6 +332,12 @@ ie::Result<void*> DeviceBuffers::cached(const void* host_key, size_t bytes, int 
 
 ie::Status CudaConv2DOp::configure(const ie::Attrs& attrs) {
   if (auto st = parse_conv_config(attrs, config_); !st.has_value()) return st;
+  // "fused_add": an Add node fused by ConvBnReluFusionPass; the residual is
+  // the fourth input
+  bool found = false;
+  int64_t fa = 0;
+  if (auto st = read_int(attrs, "fused_add", &found, &fa); !st.has_value()) return st;
+  fused_add_ = found && fa != 0;
   // "activation": a Relu / Clip(0, 6) node fused by ConvBnReluFusionPass
   act_ = IE_ACT_NONE;
   auto it = attrs.find("activation");
@@ -353,13 +359,27 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
                                  std::vector<ie::Tensor*>& outputs,
                                  ie::ExecutionContext& context) {
   const char* name = depthwise_ ? "DepthwiseConv2D" : "Conv2D";
-  if (auto st = validate(inputs, outputs, context, 2, 3, "Conv2D"); !st.has_value()) return st;
+  if (fused_add_) {
+    if (inputs.size() != 4) {
+      return ie::Error::invalid_argument("Conv2D with a fused add expects x, w, b and the residual");
+    }
+  } else if (auto st = validate(inputs, outputs, context, 2, 3, "Conv2D"); !st.has_value()) {
+    return st;
+  }
+  if (fused_add_) {
+    std::vector<ie::Tensor*> three(inputs.begin(), inputs.begin() + 3);
+    if (auto st = validate(three, outputs, context, 2, 3, "Conv2D"); !st.has_value()) return st;
+    if (inputs[3] == nullptr || inputs[3]->buffer == nullptr) {
+      return ie::Error::invalid_argument("null tensor or buffer");
+    }
+  }
   for (const ie::Tensor* t : inputs) {
     if (t->dtype != ie::DType::F32) return ie::Error::unsupported("P0 kernels support F32 only");
   }
   const ie::Tensor& x = *inputs[0];
   const ie::Tensor& w = *inputs[1];
-  const ie::Tensor* b = inputs.size() == 3 ? inputs[2] : nullptr;
+  const ie::Tensor* b = inputs.size() >= 3 ? inputs[2] : nullptr;
+  const ie::Tensor* res = fused_add_ ? inputs[3] : nullptr;
   if (auto st = check_ranks(x, w, config_, "Conv2D"); !st.has_value()) return st;
   ie_conv2d_desc d = make_desc(config_, x, w, depthwise_);
   if (d.group > 0 && d.c % d.group == 0 && w.shape.dims[1] != d.c / d.group) {
@@ -373,6 +393,13 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   ie_conv2d_shape s;
   if (auto st = to_status(ie_conv2d_resolve(&d, bias_len, &s)); !st.has_value()) return st;
   (void)name;
+  if (res != nullptr) {
+    if (d.group != 1) return ie::Error::unsupported("a fused add needs a dense convolution");
+    const std::vector<int64_t> want{d.n, d.m, s.out_h, s.out_w};
+    if (res->shape.dims != want) {
+      return ie::Error::invalid_argument("the fused add's residual must have the output's shape");
+    }
+  }
   if (auto st = require_device(); !st.has_value()) return st;
 
   cudaStream_t st = static_cast<cudaStream_t>(context.stream);
@@ -441,7 +468,13 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     if (!xs.has_value()) return xs.error();
     rc = ie_cuda_f32_pack_input(static_cast<const float*>(*xd), *xs, d.n, d.c, d.h, d.w, c_store, st);
     if (rc == IE_OK) {
-      rc = ie_cuda_conv2d_bf16x3(&d, act_, *xs, wdev, bdev, *ydev, IE_Y_F32_NCHW, st);
+      const float* rdev = nullptr;
+      if (res != nullptr) {
+        auto r = to_device(dev_, kSlotResidual, *res, st);
+        if (!r.has_value()) return r.error();
+        rdev = static_cast<const float*>(*r);
+      }
+      rc = ie_cuda_conv2d_bf16x3_residual(&d, act_, *xs, wdev, bdev, rdev, *ydev, IE_Y_F32_NCHW, st);
     }
   } else {
     rc = ie_cuda_conv2d_f32(&d, act_, static_cast<const float*>(*xd),

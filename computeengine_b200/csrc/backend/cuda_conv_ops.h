@@ -2,9 +2,10 @@
 // interface (src/core/ops/op.h:27-54, op_registry.h:15-30).
 //
 //   CudaConv2DOp(false)  replaces Conv2DOp            (conv2d_op.h:36-51); also
-//                        reads "activation" ("Relu" / "Relu6"), the
-//                        attribute ConvBnReluFusionPass sets when it fuses a
-//                        following Relu / Clip node into the epilogue
+//                        reads "activation" ("Relu" / "Relu6") and
+//                        "fused_add" (a residual as fourth input), the
+//                        attributes ConvBnReluFusionPass sets when it fuses a
+//                        following Add / Relu / Clip node into the epilogue
 //   CudaConv2DOp(true)   replaces DepthwiseConv2DOp   (conv2d_op.h:53-67)
 //   CudaQLinearConv2DOp  int8 convolution the reference plans but does not
 //                        implement (src/converter/quantization/quant_plugins.h:7-22)
@@ -101,6 +102,7 @@ class CudaConv2DOp final : public ie::Op {
   ConvConfig config_{};
   bool depthwise_;
   int32_t act_ = IE_ACT_NONE;  // fused activation ("activation" attribute)
+  bool fused_add_ = false;     // fourth input added in the epilogue ("fused_add")
   DeviceBuffers dev_;
 };
 

@@ -83,16 +83,18 @@ ie::ValueId add_constant(ie::Graph& g, const std::string& name, ie::Tensor t) {
   return v.id;
 }
 
-// Node `removed` disappears; the value it produced now comes straight from
-// node `kept`, and the edge between them goes.
+// Node `removed` disappears: the value it produced now comes straight from
+// node `kept`, the edge carrying kept's output into it goes, and its other
+// inputs (an Add's residual) now flow into `kept`.
 void splice_out(ie::Graph& g, size_t kept, size_t removed) {
   const ie::NodeId kept_id = g.nodes[kept].id, removed_id = g.nodes[removed].id;
-  const ie::ValueId middle = g.nodes[removed].inputs[0];
+  const ie::ValueId middle = g.nodes[kept].outputs[0];
   g.nodes[kept].outputs = g.nodes[removed].outputs;
   std::vector<ie::Edge> edges;
   for (ie::Edge e : g.edges) {
     if (e.value == middle && e.to.has_value() && *e.to == removed_id) continue;
     if (e.from.has_value() && *e.from == removed_id) e.from = kept_id;
+    if (e.to.has_value() && *e.to == removed_id) e.to = kept_id;
     edges.push_back(e);
   }
   g.edges = std::move(edges);
@@ -181,10 +183,50 @@ bool is_conv(const ie::Node& n) {
   return n.op == ie::OpType::Conv2D || n.op == ie::OpType::DepthwiseConv2D;
 }
 
+// A value the node at `pos` may read: a graph input, a constant, or the
+// output of an earlier node.
+bool available_at(const ie::Graph& g, ie::ValueId id, size_t pos) {
+  for (const ie::Value& v : g.values) {
+    if (v.id == id && (v.is_input || g.weights.count(v.name) != 0)) return true;
+  }
+  for (size_t i = 0; i < pos && i < g.nodes.size(); ++i) {
+    for (ie::ValueId o : g.nodes[i].outputs) {
+      if (o == id) return true;
+    }
+  }
+  return false;
+}
+
+// Conv -> Add(conv, r): r becomes the convolution's fourth input, added in
+// its epilogue ("fused_add"); a convolution without a bias gets a zero one.
+ie::Result<bool> fuse_add(ie::Graph& g, size_t c, size_t a) {
+  const ie::Node& add = g.nodes[a];
+  const ie::ValueId out = g.nodes[c].outputs[0];
+  if (add.inputs.size() != 2 || add.outputs.size() != 1) return false;
+  if (add.inputs[0] == out && add.inputs[1] == out) return false;
+  const ie::ValueId r = add.inputs[0] == out ? add.inputs[1] : add.inputs[0];
+  if (!available_at(g, r, c)) return false;
+  ie::Tensor* w = constant_of(g, g.nodes[c].inputs[1]);
+  if (w == nullptr || w->shape.dims.size() != 4) return false;
+  if (g.nodes[c].inputs.size() < 3) {
+    auto alloc = std::make_shared<ie::MallocAllocator>();
+    auto zero = ie::Tensor::allocate(ie::Shape{{w->shape.dims[0]}}, ie::DType::F32, alloc);
+    if (!zero.has_value()) return zero.error();
+    std::fill(zero->data<float>(), zero->data<float>() + zero->numel(), 0.0f);
+    const std::string name = unique_name(g, value_by_id(g, g.nodes[c].inputs[1])->name + ".bias");
+    const ie::ValueId bid = add_constant(g, name, std::move(*zero));
+    g.nodes[c].inputs.push_back(bid);
+  }
+  g.nodes[c].inputs.push_back(r);
+  g.nodes[c].attrs["fused_add"] = int64_t{1};
+  splice_out(g, c, a);
+  return true;
+}
+
 }  // namespace
 
 ie::Status ConvBnReluFusionPass::run(ie::Graph& graph, ie::PassContext& /*context*/) {
-  folded_ = fused_ = 0;
+  folded_ = fused_ = fused_adds_ = 0;
   for (size_t i = 0; i < graph.nodes.size(); ++i) {
     if (!is_conv(graph.nodes[i]) || graph.nodes[i].outputs.size() != 1 ||
         graph.nodes[i].inputs.size() < 2) {
@@ -200,6 +242,19 @@ ie::Status ConvBnReluFusionPass::run(ie::Graph& graph, ie::PassContext& /*contex
         auto r = fold(graph, i, cons[0]);
         if (!r.has_value()) return r.error();
         if (*r) ++folded_;
+      }
+    }
+    // conv -> Add(conv, residual): a dense convolution run by this backend
+    if (fuse_activation_ && graph.nodes[i].op == ie::OpType::Conv2D &&
+        graph.nodes[i].attrs.count("fused_add") == 0 &&
+        graph.nodes[i].attrs.count("activation") == 0) {
+      out = graph.nodes[i].outputs[0];
+      cons = consumers(graph, out);
+      if (cons.size() == 1 && cons[0] > i && !is_graph_output(graph, out) &&
+          graph.nodes[cons[0]].op == ie::OpType::Add) {
+        auto r = fuse_add(graph, i, cons[0]);
+        if (!r.has_value()) return r.error();
+        if (*r) ++fused_adds_;
       }
     }
     // conv -> Relu / Clip(0, 6), into a convolution without an activation yet

@@ -18,9 +18,15 @@
 // (b = 0 without a conv bias), each operation rounded once.  The folded
 // convolution differs from conv-then-BN only by that rounding.
 //
-// The "activation" attribute is this backend's extension: only
-// CudaConv2DOp reads it, so run the pass with fuse_activation = true only on
-// graphs executed with the CUDA registry (register_cuda_ops).
+//   With fuse_activation it also moves an Add that takes a dense Conv2D's
+//   output and a residual (graph input, constant or earlier node's output)
+//   into the convolution: the residual becomes its fourth input and
+//   "fused_add" = 1, and CudaConv2DOp computes act((conv + b) + r) in its
+//   epilogue (the ResNet bottleneck's shortcut add, fused before its Relu).
+//
+// The "activation" and "fused_add" attributes are this backend's extension:
+// only CudaConv2DOp reads them, so run the pass with fuse_activation = true
+// only on graphs executed with the CUDA registry (register_cuda_ops).
 #pragma once
 
 #include <string>
@@ -33,7 +39,7 @@ class ConvBnReluFusionPass final : public ie::Pass {
  public:
   explicit ConvBnReluFusionPass(bool fuse_activation = true) : fuse_activation_(fuse_activation) {}
   std::string name() const override { return "conv_bn_relu_fusion"; }
-  // Rewrites every Conv2D / DepthwiseConv2D -> BatchNorm [-> Relu | Clip(0,6)]
+  // Rewrites every Conv2D / DepthwiseConv2D -> BatchNorm [-> Add] [-> Relu | Clip(0,6)]
   // chain whose intermediate values have no other consumer and are not graph
   // outputs, and whose weights, bias and BatchNorm parameters are F32
   // constants in graph.weights.  Folded weights are added as new constants
@@ -43,11 +49,13 @@ class ConvBnReluFusionPass final : public ie::Pass {
   ie::Status run(ie::Graph& graph, ie::PassContext& context) override;
   int folded_batch_norms() const { return folded_; }
   int fused_activations() const { return fused_; }
+  int fused_adds() const { return fused_adds_; }
 
  private:
   bool fuse_activation_;
   int folded_ = 0;
   int fused_ = 0;
+  int fused_adds_ = 0;
 };
 
 }  // namespace ie_b200

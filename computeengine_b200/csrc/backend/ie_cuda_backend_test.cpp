@@ -82,7 +82,9 @@ struct BnGraph {
   std::vector<std::unique_ptr<HostTensor>> keep;
 };
 
-std::unique_ptr<BnGraph> make_bn_graph(bool clip, int64_t c = 8, int64_t m = 12) {
+// With with_add: ... -> BatchNorm -> Add(., r) -> act, r a graph input [2, m, 11, 9].
+std::unique_ptr<BnGraph> make_bn_graph(bool clip, bool with_add = false, int64_t c = 8,
+                                       int64_t m = 12) {
   auto bg = std::make_unique<BnGraph>();
   ie::Graph& g = bg->g;
   Lcg rng(21);
@@ -110,6 +112,10 @@ std::unique_ptr<BnGraph> make_bn_graph(bool clip, int64_t c = 8, int64_t m = 12)
   value(7, "bn_var", false, false);
   value(8, "bn_out", false, false);
   value(9, "y", false, true);
+  if (with_add) {
+    value(10, "r", true, false);
+    value(11, "add_out", false, false);
+  }
   constant("w", {m, c, 3, 3}, -0.3f, 0.3f);
   constant("b", {m}, -0.1f, 0.1f);
   constant("bn_scale", {m}, 0.5f, 1.5f);
@@ -134,8 +140,20 @@ std::unique_ptr<BnGraph> make_bn_graph(bool clip, int64_t c = 8, int64_t m = 12)
   act.inputs = {8};
   act.outputs = {9};
   if (clip) act.attrs = {{"min", 0.0}, {"max", 6.0}};
-  g.nodes = {conv, bn, act};
-  g.edges = {{3, 0u, 1u}, {8, 1u, 2u}, {9, 2u, std::nullopt}};
+  if (with_add) {
+    ie::Node add;
+    add.id = 3;
+    add.op = ie::OpType::Add;
+    add.inputs = {10, 8};  // residual first: either order is an Add of the conv output
+    add.outputs = {11};
+    act.inputs = {11};
+    g.nodes = {conv, bn, add, act};
+    g.edges = {{3, 0u, 1u}, {8, 1u, 3u}, {10, std::nullopt, 3u}, {11, 3u, 2u},
+               {9, 2u, std::nullopt}};
+  } else {
+    g.nodes = {conv, bn, act};
+    g.edges = {{3, 0u, 1u}, {8, 1u, 2u}, {9, 2u, std::nullopt}};
+  }
   return bg;
 }
 
@@ -264,6 +282,35 @@ int run_cpu() {
     expect(has_code(act_op.configure({{"activation", std::string("Tanh")}}),
                     Error::Code::InvalidArgument),
            "unknown activation rejected");
+    auto ba = make_bn_graph(false, true);
+    ie_b200::ConvBnReluFusionPass pass6;
+    expect(pass6.run(ba->g, pctx).has_value() && ba->g.nodes.size() == 1 &&
+               pass6.folded_batch_norms() == 1 && pass6.fused_adds() == 1 &&
+               pass6.fused_activations() == 1,
+           "conv + BN + Add + Relu fused into one node");
+    if (ba->g.nodes.size() == 1) {
+      const ie::Node& n = ba->g.nodes[0];
+      const auto* fa = std::get_if<int64_t>(&n.attrs.at("fused_add"));
+      expect(fa != nullptr && *fa == 1 && n.inputs.size() == 4 && n.inputs[3] == 10 &&
+                 n.outputs == std::vector<ie::ValueId>{9},
+             "residual is the fused node's fourth input");
+      bool edge_ok = false;
+      for (const ie::Edge& e : ba->g.edges) {
+        if (e.value == 10 && e.to.has_value() && *e.to == 0u) edge_ok = true;
+      }
+      expect(edge_ok && ba->g.edges.size() == 2, "residual edge now feeds the fused node");
+    }
+    auto bl = make_bn_graph(false, true);
+    for (ie::Value& v : bl->g.values) {
+      if (v.id == 10) v.is_input = false;  // the residual is produced by nothing before the conv
+    }
+    ie_b200::ConvBnReluFusionPass pass7;
+    expect(pass7.run(bl->g, pctx).has_value() && pass7.fused_adds() == 0,
+           "no add fusion when the residual is not available at the conv");
+    ie_b200::CudaConv2DOp fa_op;
+    fa_op.configure({{"fused_add", int64_t{1}}});
+    expect(has_code(fa_op.forward({&x.t, &w.t, &bias.t}, outs, ctx), Error::Code::InvalidArgument),
+           "fused add without the residual input rejected");
   }
 
   // pooling and Gemm ops: attribute and shape errors as the reference reports them
@@ -515,6 +562,40 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "bn_wf", *wf);
     dump(dir, manifest, "bn_bf", *bf);
     dump(dir, manifest, "bn_y", y);
+  }
+  // conv + BN + shortcut add + Relu fused, run with a residual input
+  {
+    auto bg = make_bn_graph(false, true);
+    HostTensor x({2, 8, 11, 9}, ie::DType::F32), r({2, 12, 11, 9}, ie::DType::F32);
+    Lcg rng(23);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    for (int64_t i = 0; i < r.t.numel(); ++i) r.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    std::vector<ie::Tensor> orig;
+    for (const char* k : {"w", "b", "bn_scale", "bn_bias", "bn_mean", "bn_var"}) {
+      orig.push_back(bg->g.weights.at(k));
+    }
+    ie_b200::ConvBnReluFusionPass pass;
+    ie::PassContext pctx;
+    expect(pass.run(bg->g, pctx).has_value() && bg->g.nodes.size() == 1, "ADD: fuse");
+    const ie::Node& n = bg->g.nodes[0];
+    auto op = reg.create(n.op);
+    if (!op.has_value()) return 3;
+    expect((*op)->configure(n.attrs).has_value(), "ADD: configure fused conv");
+    ie::Tensor* wf = &bg->g.weights.at(bg->g.find_value(n.inputs[1])->name);
+    ie::Tensor* bf = &bg->g.weights.at(bg->g.find_value(n.inputs[2])->name);
+    ie::Tensor y;
+    std::vector<ie::Tensor*> outs{&y};
+    const ie::Status st = (*op)->forward({&x.t, wf, bf, &r.t}, outs, ctx);
+    expect(st.has_value(), "ADD: fused conv forward");
+    if (!st.has_value()) {
+      std::printf("  %s\n", st.error().message.c_str());
+      return 4;
+    }
+    dump(dir, manifest, "add_x", x.t);
+    dump(dir, manifest, "add_r", r.t);
+    const char* names[] = {"add_w", "add_b", "add_scale", "add_bias", "add_mean", "add_var"};
+    for (size_t i = 0; i < orig.size(); ++i) dump(dir, manifest, names[i], orig[i]);
+    dump(dir, manifest, "add_y", y);
   }
   // the head of a ResNet through the registry: max pool, average pool,
   // global average pool, Gemm (FC with bias)

@@ -71,6 +71,8 @@ struct IgemmArgs {
   const float* mult;         // int8 path: per-channel requantize multiplier
   int32_t zp_y, qmin, qmax;  // int8 path: output zero point and clamp range
   float act_lo, act_hi;      // fp32 path: clamp range after bias
+  const float* residual;     // fp32 path, may be null: added after the bias, before the
+                             // clamp (same layout as y: NCHW, or NHWC with y_ld)
   int32_t act;               // fp32 path: 0 = no clamp (NaN propagates)
   int32_t out_mode;
   void* y;
@@ -325,30 +327,49 @@ __device__ __forceinline__ void store_chunk_direct(const IgemmArgs& a, const uin
     }
     return;
   }
-  auto finish = [&](int j) {
-    float f = __uint_as_float(acc[j]) + sbf[j];
+  // (acc + bias) [+ residual], then the clamp: one rounding per operation,
+  // the order of the reference's Conv2D, Add and Relu nodes
+  auto finish = [&](int j, const float* r) {
+    float f = __fadd_rn(__uint_as_float(acc[j]), sbf[j]);
+    if (r != nullptr) f = __fadd_rn(f, __ldg(r));
     if (a.act) f = fminf(fmaxf(f, a.act_lo), a.act_hi);
     return f;
   };
+  auto finish0 = [&](int j) { return finish(j, nullptr); };
   if (a.out_mode == kOutF32) {
-    float* dst = static_cast<float*>(a.y) + pixel * a.y_ld + col0;
+    const int64_t off = pixel * a.y_ld + col0;
+    float* dst = static_cast<float*>(a.y) + off;
     const int n16 = valid >= 32 ? 8 : (valid + 3) / 4;
+    if (a.residual != nullptr) {
+      const float* res = a.residual + off;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q < n16) {
+          reinterpret_cast<float4*>(dst)[q] =
+              make_float4(finish(4 * q, res + 4 * q), finish(4 * q + 1, res + 4 * q + 1),
+                          finish(4 * q + 2, res + 4 * q + 2), finish(4 * q + 3, res + 4 * q + 3));
+        }
+      }
+      return;
+    }
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (q < n16) {
         reinterpret_cast<float4*>(dst)[q] =
-            make_float4(finish(4 * q), finish(4 * q + 1), finish(4 * q + 2), finish(4 * q + 3));
+            make_float4(finish0(4 * q), finish0(4 * q + 1), finish0(4 * q + 2), finish0(4 * q + 3));
       }
     }
   } else if (a.out_mode == kOutF32Nchw) {
     // Lanes hold consecutive pixels, so each channel's store is coalesced.
     const int64_t hw = static_cast<int64_t>(a.out_h) * a.out_w;
     const int64_t img = pixel / hw;
-    float* dst = static_cast<float*>(a.y) + (img * a.m + col0) * hw + (pixel - img * hw);
+    const int64_t off = (img * a.m + col0) * hw + (pixel - img * hw);
+    float* dst = static_cast<float*>(a.y) + off;
     const int n = valid >= 32 ? 32 : valid;
+    const float* res = a.residual != nullptr ? a.residual + off : nullptr;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      if (j < n) dst[j * hw] = finish(j);
+      if (j < n) dst[j * hw] = finish(j, res != nullptr ? res + j * hw : nullptr);
     }
   } else {  // kOutBF16x2: [hi plane (y_ld/2) | lo plane (y_ld/2)]
     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.y) + pixel * a.y_ld + col0;
@@ -361,7 +382,7 @@ __device__ __forceinline__ void store_chunk_direct(const IgemmArgs& a, const uin
         uint32_t* pl = reinterpret_cast<uint32_t*>(&vl);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float f0 = finish(8 * q + 2 * j), f1 = finish(8 * q + 2 * j + 1);
+          const float f0 = finish0(8 * q + 2 * j), f1 = finish0(8 * q + 2 * j + 1);
           const __nv_bfloat16 h0 = __float2bfloat16_rn(f0), h1 = __float2bfloat16_rn(f1);
           const __nv_bfloat16 l0 = __float2bfloat16_rn(f0 - __bfloat162float(h0));
           const __nv_bfloat16 l1 = __float2bfloat16_rn(f1 - __bfloat162float(h1));

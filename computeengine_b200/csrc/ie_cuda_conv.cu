@@ -865,6 +865,13 @@ int ie_cuda_f32_pack_input(const float* x_nchw, void* x_split, int64_t n, int64_
 int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x_split,
                           const void* packed, const float* bias, void* y, int32_t y_format,
                           void* stream) {
+  return ie_cuda_conv2d_bf16x3_residual(desc, act, x_split, packed, bias, nullptr, y, y_format,
+                                        stream);
+}
+
+int ie_cuda_conv2d_bf16x3_residual(const ie_conv2d_desc* desc, int32_t act, const void* x_split,
+                                   const void* packed, const float* bias, const float* residual,
+                                   void* y, int32_t y_format, void* stream) {
   ie_conv2d_shape s;
   int rc = resolve(desc, -1, &s);
   if (rc != IE_OK) return rc;
@@ -876,8 +883,12 @@ int ie_cuda_conv2d_bf16x3(const ie_conv2d_desc* desc, int32_t act, const void* x
   const int64_t c_store = round_up(desc->c, 16);
   IgemmSetup su;
   if ((rc = setup_igemm(desc, s, 2, c_store, x_split, packed, &su)) != IE_OK) return rc;
+  if (residual != nullptr && y_format == IE_Y_BF16X2_NHWC) {
+    return fail(IE_UNSUPPORTED, "a residual needs an fp32 output format");
+  }
   IgemmArgs& a = su.args;
   a.bias_f32 = bias;
+  a.residual = residual;
   a.act = act != IE_ACT_NONE;
   a.act_lo = 0.0f;
   a.act_hi = act == IE_ACT_RELU6 ? 6.0f : INFINITY;
@@ -1134,6 +1145,34 @@ int ie_cuda_gemm_f32(int64_t m, int64_t n, int64_t k, int32_t trans_a, int32_t t
   }
   gemm_epilogue_f32<<<grid_1d(m * n, 256), 256, 0, st>>>(p, y, m, n, alpha, beta, c, c_mode);
   return check_launch("gemm_epilogue_f32");
+}
+
+int ie_cuda_conv2d_f32_residual(const ie_conv2d_desc* desc, int32_t act, const float* x,
+                                const float* w, const float* bias, const float* residual,
+                                float* y, void* workspace, size_t workspace_bytes, void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if (x == nullptr || w == nullptr || y == nullptr || residual == nullptr) {
+    return fail(IE_INVALID_ARGUMENT, "null tensor");
+  }
+  if (desc->group != 1) return fail(IE_UNSUPPORTED, "residual fusion runs dense convolutions only");
+  if (act < IE_ACT_NONE || act > IE_ACT_RELU6) return fail(IE_INVALID_ARGUMENT, "bad activation");
+  const size_t need = ie_cuda_conv2d_f32_workspace_bytes(desc);
+  if (workspace == nullptr || workspace_bytes < need) {
+    return fail(IE_INVALID_ARGUMENT, "workspace too small (%zu < %zu)", workspace_bytes, need);
+  }
+  const int64_t c_store = round_up(desc->c, 16);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* x_split = ws;
+  void* packed = ws + round_up(desc->n * desc->h * desc->w * c_store * 4, 256);
+  if ((rc = ie_cuda_f32_pack_input(x, x_split, desc->n, desc->c, desc->h, desc->w, c_store,
+                                   stream)) != IE_OK) {
+    return rc;
+  }
+  if ((rc = ie_cuda_f32_pack_weights(desc, w, packed, stream)) != IE_OK) return rc;
+  return ie_cuda_conv2d_bf16x3_residual(desc, act, x_split, packed, bias, residual, y,
+                                        IE_Y_F32_NCHW, stream);
 }
 
 size_t ie_cuda_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }

@@ -221,6 +221,24 @@ int ie_cuda_conv2d_f32(const ie_conv2d_desc* desc, int32_t act, const float* x,
                        const float* w, const float* bias, float* y, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* Residual-add fusion: the dense fp32 convolution with an extra tensor of the
+ * output's shape and layout added after the bias and before the activation,
+ *   y = act((conv(x, w) + bias) + residual)
+ * one rounding per operation, the order of the reference's Conv2D, Add
+ * (core/ops) and Relu nodes.  This is the ResNet bottleneck's projection /
+ * identity add run in the last 1x1 convolution's epilogue instead of as a
+ * separate pass over the activation.  residual may equal y (each element is
+ * read before it is written, by the same thread).  Dense (group == 1) only:
+ * IE_UNSUPPORTED otherwise.  The bf16x3 form takes split inputs and packed
+ * weights like ie_cuda_conv2d_bf16x3 and an fp32 output format; the f32 form
+ * is the NCHW drop-in with ie_cuda_conv2d_f32's workspace. */
+int ie_cuda_conv2d_bf16x3_residual(const ie_conv2d_desc* desc, int32_t act, const void* x_split,
+                                   const void* packed, const float* bias, const float* residual,
+                                   void* y, int32_t y_format, void* stream);
+int ie_cuda_conv2d_f32_residual(const ie_conv2d_desc* desc, int32_t act, const float* x,
+                                const float* w, const float* bias, const float* residual,
+                                float* y, void* workspace, size_t workspace_bytes, void* stream);
+
 /* No-allocation variant of ie_cuda_conv2d_f32.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory or hand
  * this library a workspace: an Op::forward that only receives the engine's

@@ -101,3 +101,22 @@ def test_conv_bn_relu_fusion_pass(oracle, tmp_path):
     err = float(np.abs(t["bn_y"] - want).max())
     assert err <= REL_TOL * float(np.abs(want).max()), err
     assert (want == 0).any() and (want > 0).mean() > 0.2
+
+
+def test_conv_bn_add_relu_fusion(oracle, tmp_path):
+    """The pass also fuses the bottleneck's shortcut Add: the fused Conv2D
+    (folded BatchNorm, residual as fourth input, Relu) run by CudaConv2DOp
+    matches conv -> BatchNorm -> Add -> Relu within 1e-3 * max |ref|."""
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    f32 = np.float32
+    inv = (1.0 / np.sqrt(t["add_var"].astype(np.float64) + 1e-3)).astype(f32)
+    gain = t["add_scale"] * inv
+    shift = t["add_bias"] - t["add_mean"] * gain
+    conv = oracle.conv2d_f32(t["add_x"], t["add_w"], t["add_b"], pads=(1, 1, 1, 1))
+    bn = conv * gain[None, :, None, None] + shift[None, :, None, None]
+    want = np.maximum(bn + t["add_r"], f32(0))
+    err = float(np.abs(t["add_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
