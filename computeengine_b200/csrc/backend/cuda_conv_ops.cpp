@@ -6,6 +6,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <optional>
 #include <string>
 #include <utility>
 
@@ -244,6 +245,37 @@ ie::Status finish(cudaStream_t st) {
   return {};
 }
 
+// True when the caller keeps values in device memory (CudaExecutor): the
+// context's allocator hands out device memory, outputs stay there and the
+// op returns without synchronizing (the executor does, once per run).
+bool device_mode(const ie::ExecutionContext& context) {
+  return context.device == ie::Device::CUDA;
+}
+
+// outputs[0] from a device result: copied to a host tensor (and the stream
+// synchronized) normally, or to a device tensor from the context's allocator
+// in device mode.
+ie::Status deliver(const void* ydev, ie::Shape shape, ie::DType dtype,
+                   ie::ExecutionContext& context, std::vector<ie::Tensor*>& outputs,
+                   cudaStream_t st) {
+  auto out = ie::Tensor::allocate(shape, dtype, context.allocator);
+  if (!out.has_value()) return out.error();
+  const bool dev = device_mode(context);
+  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, ydev, out->bytes(),
+                                           dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st),
+                           "cudaMemcpyAsync");
+      !e.has_value()) {
+    return e;
+  }
+  if (dev) {
+    out->device = ie::Device::CUDA;
+  } else if (auto e = finish(st); !e.has_value()) {
+    return e;
+  }
+  *outputs[0] = std::move(*out);
+  return {};
+}
+
 enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork, kSlotResidual };
 enum CacheKind { kCacheW = 0, kCacheWPacked, kCacheBias, kCacheMult, kCacheBiasI32 };
 
@@ -457,7 +489,15 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     }
   }
   const size_t y_bytes = static_cast<size_t>(d.n * d.m * s.out_h * s.out_w) * sizeof(float);
-  auto ydev = dev_.scratch(kSlotY, y_bytes);
+  const ie::Shape y_shape{{d.n, d.m, s.out_h, s.out_w}};
+  std::optional<ie::Tensor> dev_out;  // device mode: the result is written in place
+  if (device_mode(context)) {
+    auto t = ie::Tensor::allocate(y_shape, ie::DType::F32, context.allocator);
+    if (!t.has_value()) return t.error();
+    t->device = ie::Device::CUDA;
+    dev_out = std::move(*t);
+  }
+  auto ydev = dev_out ? ie::Result<void*>(dev_out->buffer) : dev_.scratch(kSlotY, y_bytes);
   if (!ydev.has_value()) return ydev.error();
   int rc;
   if (dense) {
@@ -483,17 +523,11 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   }
   if (auto e = to_status(rc); !e.has_value()) return e;
 
-  auto out = ie::Tensor::allocate(ie::Shape{{d.n, d.m, s.out_h, s.out_w}}, ie::DType::F32,
-                                  context.allocator);
-  if (!out.has_value()) return out.error();
-  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, *ydev, y_bytes, cudaMemcpyDeviceToHost, st),
-                           "cudaMemcpyAsync D2H");
-      !e.has_value()) {
-    return e;
+  if (dev_out) {
+    *outputs[0] = std::move(*dev_out);
+    return {};
   }
-  if (auto e = finish(st); !e.has_value()) return e;
-  *outputs[0] = std::move(*out);
-  return {};
+  return deliver(*ydev, y_shape, ie::DType::F32, context, outputs, st);
 }
 
 // ------------------------------------------------ int8 QLinearConv2D
@@ -666,16 +700,7 @@ namespace {
 // Host NCHW F32 out of a device buffer: allocate outputs[0] and copy back.
 ie::Status download_f32(const void* ydev, ie::Shape shape, ie::ExecutionContext& context,
                         std::vector<ie::Tensor*>& outputs, cudaStream_t st) {
-  auto out = ie::Tensor::allocate(shape, ie::DType::F32, context.allocator);
-  if (!out.has_value()) return out.error();
-  if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, ydev, out->bytes(), cudaMemcpyDeviceToHost, st),
-                           "cudaMemcpyAsync D2H");
-      !e.has_value()) {
-    return e;
-  }
-  if (auto e = finish(st); !e.has_value()) return e;
-  *outputs[0] = std::move(*out);
-  return {};
+  return deliver(ydev, std::move(shape), ie::DType::F32, context, outputs, st);
 }
 
 // Device copy of a constant input (weights, bias), uploaded once per host buffer.

@@ -25,9 +25,11 @@
 #include <memory>
 #include <optional>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "cuda_conv_ops.h"
+#include "cuda_executor.h"
 #include "graph_passes.h"
 #include "int8_quant.h"
 
@@ -155,6 +157,78 @@ std::unique_ptr<BnGraph> make_bn_graph(bool clip, bool with_add = false, int64_t
     g.edges = {{3, 0u, 1u}, {8, 1u, 2u}, {9, 2u, std::nullopt}};
   }
   return bg;
+}
+
+// A ResNet-shaped graph: conv3x3+BN+Relu -> MaxPool -> conv1x1+BN -> Add
+// (pool shortcut) -> Relu -> GlobalAvgPool -> Flatten -> Gemm (FC + bias).
+struct NetGraph {
+  ie::Graph g;
+  std::vector<std::unique_ptr<HostTensor>> keep;
+  std::vector<std::string> names;  // constants in creation order
+};
+
+std::unique_ptr<NetGraph> make_net_graph() {
+  auto ng = std::make_unique<NetGraph>();
+  ie::Graph& g = ng->g;
+  Lcg rng(31);
+  ie::ValueId next = 0;
+  auto value = [&](const std::string& name, bool in = false, bool out = false) {
+    ie::Value v;
+    v.id = next++;
+    v.name = name;
+    v.is_input = in;
+    v.is_output = out;
+    g.values.push_back(v);
+    return v.id;
+  };
+  auto constant = [&](const std::string& name, std::vector<int64_t> dims, float lo, float hi) {
+    ng->keep.push_back(std::make_unique<HostTensor>(dims, ie::DType::F32));
+    HostTensor& t = *ng->keep.back();
+    for (int64_t i = 0; i < t.t.numel(); ++i) t.data<float>()[i] = rng.uniform(lo, hi);
+    g.weights.emplace(name, t.t);
+    ng->names.push_back(name);
+    return value(name);
+  };
+  auto node = [&](ie::OpType op, std::vector<ie::ValueId> in, ie::ValueId out, ie::Attrs attrs = {}) {
+    ie::Node n;
+    n.id = static_cast<ie::NodeId>(g.nodes.size());
+    n.op = op;
+    n.inputs = std::move(in);
+    n.outputs = {out};
+    n.attrs = std::move(attrs);
+    g.nodes.push_back(n);
+  };
+  const ie::ValueId x = value("x", true);
+  const ie::ValueId w1 = constant("w1", {16, 3, 3, 3}, -0.4f, 0.4f);
+  const ie::ValueId b1 = constant("b1", {16}, -0.1f, 0.1f);
+  const ie::ValueId bn1[4] = {constant("bn1_scale", {16}, 0.5f, 1.5f),
+                              constant("bn1_bias", {16}, -0.2f, 0.2f),
+                              constant("bn1_mean", {16}, -0.2f, 0.2f),
+                              constant("bn1_var", {16}, 0.3f, 1.3f)};
+  const ie::ValueId w2 = constant("w2", {16, 16, 1, 1}, -0.4f, 0.4f);
+  const ie::ValueId bn2[4] = {constant("bn2_scale", {16}, 0.5f, 1.5f),
+                              constant("bn2_bias", {16}, -0.2f, 0.2f),
+                              constant("bn2_mean", {16}, -0.2f, 0.2f),
+                              constant("bn2_var", {16}, 0.3f, 1.3f)};
+  const ie::ValueId wfc = constant("wfc", {10, 16}, -0.5f, 0.5f);
+  const ie::ValueId bfc = constant("bfc", {10}, -0.1f, 0.1f);
+  const ie::ValueId c1 = value("c1"), n1 = value("n1"), r1 = value("r1"), pl = value("pool");
+  const ie::ValueId c2 = value("c2"), n2 = value("n2"), ad = value("add"), r2 = value("r2");
+  const ie::ValueId gp = value("gap"), fl = value("flat"), y = value("y", false, true);
+  node(ie::OpType::Conv2D, {x, w1, b1}, c1, {{"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+  node(ie::OpType::BatchNorm, {c1, bn1[0], bn1[1], bn1[2], bn1[3]}, n1);
+  node(ie::OpType::Relu, {n1}, r1);
+  node(ie::OpType::MaxPool2D, {r1}, pl,
+       {{"kernel_shape", std::vector<int64_t>{3, 3}}, {"strides", std::vector<int64_t>{2, 2}},
+        {"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+  node(ie::OpType::Conv2D, {pl, w2}, c2);
+  node(ie::OpType::BatchNorm, {c2, bn2[0], bn2[1], bn2[2], bn2[3]}, n2);
+  node(ie::OpType::Add, {n2, pl}, ad);
+  node(ie::OpType::Relu, {ad}, r2);
+  node(ie::OpType::GlobalAvgPool, {r2}, gp);
+  node(ie::OpType::Flatten, {gp}, fl);
+  node(ie::OpType::Gemm, {fl, wfc, bfc}, y, {{"transB", int64_t{1}}});
+  return ng;
 }
 
 // ------------------------------------------------------------ cpu checks
@@ -562,6 +636,42 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "bn_wf", *wf);
     dump(dir, manifest, "bn_bf", *bf);
     dump(dir, manifest, "bn_y", y);
+  }
+  // the ResNet-shaped graph: fusion pass, then the device-resident executor
+  {
+    auto ng = make_net_graph();
+    ie::Graph& g = ng->g;
+    ie_b200::ConvBnReluFusionPass pass;
+    ie::PassContext pctx;
+    expect(pass.run(g, pctx).has_value() && pass.folded_batch_norms() == 2 &&
+               pass.fused_adds() == 1 && pass.fused_activations() == 2 && g.nodes.size() == 6,
+           "EXEC: graph fused to 6 nodes");
+    HostTensor x({2, 3, 32, 32}, ie::DType::F32);
+    Lcg rng(32);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    ie_b200::CudaExecutor exec(reg);
+    std::unordered_map<std::string, ie::Tensor> in{{"x", x.t}};
+    auto r1 = exec.run(g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r1.has_value() && r1->size() == 1, "EXEC: run");
+    if (!r1.has_value()) {
+      std::printf("  %s\n", r1.error().message.c_str());
+      return 4;
+    }
+    auto r2 = exec.run(g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r2.has_value() && std::memcmp((*r1)[0].buffer, (*r2)[0].buffer, (*r1)[0].bytes()) == 0,
+           "EXEC: second run (cached weights) identical");
+    expect((*r1)[0].shape.dims == std::vector<int64_t>{2, 10} && (*r1)[0].device == ie::Device::CPU,
+           "EXEC: host output [2, 10]");
+    dump(dir, manifest, "net_x", x.t);
+    for (size_t i = 0; i < ng->names.size(); ++i) {
+      dump(dir, manifest, ("net_" + ng->names[i]).c_str(), ng->keep[i]->t);
+    }
+    dump(dir, manifest, "net_y", (*r1)[0]);
+    auto raw = make_net_graph();  // unfused: BatchNorm has no CUDA op
+    ie_b200::CudaExecutor exec2(reg);
+    auto bad = exec2.run(raw->g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(!bad.has_value() && bad.error().code == Error::Code::Unsupported,
+           "EXEC: unfused graph is Unsupported");
   }
   // conv + BN + shortcut add + Relu fused, run with a residual input
   {

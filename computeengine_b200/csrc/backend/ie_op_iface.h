@@ -200,7 +200,8 @@ class Op {
 };
 
 enum class OpType {
-  Add, Relu, Conv2D, DepthwiseConv2D, MaxPool2D, AvgPool2D, GlobalAvgPool, BatchNorm, Clip, Gemm
+  Add, Relu, Reshape, Conv2D, DepthwiseConv2D, MaxPool2D, AvgPool2D, GlobalAvgPool, BatchNorm,
+  Clip, Gemm, Flatten
 };
 
 using NodeId = uint32_t;

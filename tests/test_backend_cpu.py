@@ -31,6 +31,7 @@ def test_cpp_ops_compile_against_reference_headers():
     cmd = ["g++", "-std=c++20", "-fsyntax-only", "-DIE_B200_REFERENCE_HEADERS",
            f"-I{REFERENCE_SRC}", f"-I{ROOT / 'include'}", f"-I{backend}",
            "-I/usr/local/cuda/include", str(backend / "cuda_conv_ops.cpp"),
-           str(backend / "int8_quant.cpp"), str(backend / "graph_passes.cpp")]
+           str(backend / "int8_quant.cpp"), str(backend / "graph_passes.cpp"),
+           str(backend / "cuda_executor.cpp")]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr

@@ -120,3 +120,33 @@ def test_conv_bn_add_relu_fusion(oracle, tmp_path):
     want = np.maximum(bn + t["add_r"], f32(0))
     err = float(np.abs(t["add_y"] - want).max())
     assert err <= REL_TOL * float(np.abs(want).max()), err
+
+
+def test_cuda_executor_runs_fused_graph(oracle, tmp_path):
+    """A ResNet-shaped graph (conv3x3+BN+Relu, max pool, conv1x1+BN, shortcut
+    Add, Relu, global average pool, Flatten, Gemm) after the fusion pass, run
+    by CudaExecutor with every intermediate value in device memory, against
+    the same unfused network computed from the oracle convolution and numpy:
+    max |err| <= 1e-3 * max |ref|; a second run reproduces the first."""
+    from oracle.oracle import maxpool2d_nchw
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    f32 = np.float32
+
+    def bn(v, p):
+        inv = (1.0 / np.sqrt(t[p + "_var"].astype(np.float64) + 1e-5)).astype(f32)
+        gain = t[p + "_scale"] * inv
+        shift = t[p + "_bias"] - t[p + "_mean"] * gain
+        return v * gain[None, :, None, None] + shift[None, :, None, None]
+
+    c1 = oracle.conv2d_f32(t["net_x"], t["net_w1"], t["net_b1"], pads=(1, 1, 1, 1))
+    r1 = np.maximum(bn(c1, "net_bn1"), f32(0))
+    pool = maxpool2d_nchw(r1, 3, 2, 1).astype(f32)
+    c2 = oracle.conv2d_f32(pool, t["net_w2"], None)
+    r2 = np.maximum(bn(c2, "net_bn2") + pool, f32(0))
+    gap = r2.mean(axis=(2, 3), dtype=np.float64).astype(f32)
+    want = gap @ t["net_wfc"].T + t["net_bfc"]
+    err = float(np.abs(t["net_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
