@@ -8,7 +8,8 @@ import numpy as np
 
 def make_q8_problem(rng, n, c, h, w, m, kh, kw, *, x_zp=128, x_signed=False, x_std=30.0,
                     s_x=0.02, s_y=0.05, zp_y=0, bias_std=500.0, with_bias=True, group=1):
-    """Seeded int8 conv problem in the BASELINE int8 scheme (NCHW host arrays)."""
+    """Seeded int8 conv problem in the benchmark's int8 scheme: uint8 activations with a zero
+    point, per-channel int8 weights, int32 bias, fp32 multipliers (NCHW host arrays)."""
     if x_signed:
         x = np.clip(np.rint(rng.normal(0, x_std, (n, c, h, w))), -128, 127).astype(np.int8)
     else:
