@@ -51,79 +51,125 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH_PER_GPU)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the single-conv, fp32-stack and MobileNetV2 workloads")
     return ap.parse_args()
 
 
 # ----------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while running."""
+    """Samples the GPU's SM clock, board power and clock-event (throttle)
+    reasons while the timed region runs.  Read-only NVML queries every 5 ms,
+    so even a timed region of a few tens of milliseconds gets several samples;
+    nvidia-smi every 100 ms when NVML is unavailable.  mark_start() /
+    mark_stop() bracket the timed region on the host clock: only samples taken
+    between them are summarised."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
-        self.skip = 0
+    def __init__(self, gpu_index: int, pci_bus_id: str = None, period_s: float = 0.005):
+        self.gpu, self.pci, self.period = gpu_index, pci_bus_id, period_s
+        self.samples = []  # (host time, sm MHz, power W, [reason names])
+        self.max_mhz = None
+        self.source = None
+        self.t0 = self.t1 = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
 
-    def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-            # nvidia-smi takes a few hundred ms to print its first line: wait for
-            # it so that the samples fall inside the timed region that follows.
-            t0 = time.time()
-            while not self.lines and time.time() - t0 < 3.0:
-                time.sleep(0.01)
-            self.skip = len(self.lines)
-        except FileNotFoundError:
-            self.proc = None
-        return self
+    def mark_start(self):
+        self.t0 = time.perf_counter()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark_stop(self):
+        self.t1 = time.perf_counter()
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+    def _nvml_loop(self, nv, h):
+        masks = [(name, getattr(nv, attr, 0)) for name, attr in self.REASONS]
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((time.perf_counter(), float(sm), pw,
+                                     [n for n, m in masks if m and bits & m]))
+            except Exception:  # pragma: no cover - a transient NVML error skips a sample
+                pass
+            self._stop.wait(self.period)
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        lines = self.lines[self.skip:]
-        note = None
-        if not lines and self.lines:
-            # the timed region ended before the next sample: report the one
-            # taken as it started (the warm-up had the GPU busy then)
-            lines, note = self.lines[-1:], "timed region shorter than the sampling period"
-        for ln in lines:
-            parts = [p.strip() for p in ln.split(",")]
+    def _smi_loop(self):
+        for line in self._proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                sm, self.max_mhz = float(parts[1]), float(parts[2])
+                pw = float(parts[3])
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        out = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-               "samples": len(sm)}
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            self.samples.append((time.perf_counter(), sm, pw,
+                                 [n for n, v in zip(names, parts[5:9]) if v.lower() == "active"]))
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = (nv.nvmlDeviceGetHandleByPciBusId(self.pci) if self.pci
+                 else nv.nvmlDeviceGetHandleByIndex(self.gpu))
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.source = "nvml (5 ms)"
+        except Exception:
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.SMI_FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._thread = threading.Thread(target=self._smi_loop, daemon=True)
+                self.source = "nvidia-smi (100 ms)"
+            except FileNotFoundError:
+                return self
+        self._thread.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 3.0:  # first sample before timing
+            time.sleep(0.002)
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        inside = [s for s in self.samples
+                  if (self.t0 is None or s[0] >= self.t0) and (self.t1 is None or s[0] <= self.t1)]
+        note = None
+        if not inside and self.samples:
+            before = [s for s in self.samples if self.t0 is None or s[0] < self.t0]
+            inside = before[-1:] or self.samples[:1]
+            note = "timed region shorter than the sampling period: the last sample before it"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": self.source}
+        reasons = sorted({r for s in inside for r in s[3]})
+        out = {"sm_mhz": float(np.median([s[1] for s in inside])),
+               "sm_mhz_min": float(min(s[1] for s in inside)), "sm_max_mhz": self.max_mhz,
+               "power_w_max": float(max(s[2] for s in inside)), "reasons": reasons,
+               "samples": len(inside), "source": self.source}
         if note:
             out["note"] = note
         return out
@@ -131,11 +177,15 @@ class ClockSampler:
 
 # ------------------------------------------------------------ distributed
 
-def dist_setup(want_gpus: int):
+def dist_setup(want_gpus: int, impl: str = "ours"):
+    """Rank, world size and local rank from torchrun's environment.  Our arm
+    joins an NCCL process group (weights broadcast, barriers, max over ranks);
+    the reference arm runs on rank 0's host cores only and touches no GPU, so
+    it joins none."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and impl == "ours":
         import datetime
 
         import torch
@@ -344,6 +394,116 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- the other workloads
+
+def _ref_seconds(fn, min_s=1.0, max_reps=50):
+    """Host seconds per call of fn (one untimed call, then repeats for about
+    min_s seconds)."""
+    fn()
+    reps, t0 = 0, time.perf_counter()
+    while reps < max_reps and (reps == 0 or time.perf_counter() - t0 < min_s):
+        fn()
+        reps += 1
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_workloads(threads: int, stack_tops: float = None) -> dict:
+    """The reference's fp32 Conv2DOp (oracle/_ref) on the host cores for the
+    single-convolution, fp32-stack and MobileNetV2 workloads; int8 workloads run
+    on their dequantized tensors (the reference has no int8 convolution).
+    Returns per config {"value", "unit", "cores", "sample"}."""
+    from oracle.oracle import RefConv
+    if not RefConv.available():
+        return {}
+    from computeengine_b200.mobilenet import mobilenetv2_layers
+    ref = RefConv()
+    rng = np.random.default_rng(0)
+    out = {}
+    # config 1: one fp32 conv + ReLU, one call on one core (the op is single-threaded)
+    x = rng.uniform(-1, 1, (1, 64, 56, 56)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2 / 576), (64, 64, 3, 3)).astype(np.float32)
+    b = rng.normal(0, 0.01, 64).astype(np.float32)
+
+    def c1():
+        rc, y = ref.conv2d(x, w, b, pads=(1, 1, 1, 1))
+        np.maximum(y, 0.0, out=y)
+    t = _ref_seconds(c1)
+    out["1"] = {"value": 2 * 64 * 64 * 9 * 56 * 56 / t / 1e12, "unit": "TFLOP/s", "cores": 1,
+                "sample": "reference Conv2DOp + Relu on [1,64,56,56], repeated ~1 s"}
+    # config 2: the int8 conv dequantized, one image per thread
+    n2 = min(8, threads)
+    x2 = rng.normal(0, 0.6, (n2, 128, 28, 28)).astype(np.float32)
+    w2 = rng.normal(0, 0.3, (128, 128, 3, 3)).astype(np.float32)
+    t = _ref_seconds(lambda: ref.conv2d(x2, w2, None, pads=(1, 1, 1, 1), nthreads=n2))
+    out["2"] = {"value": n2 * 2 * 128 * 128 * 9 * 28 * 28 / t / 1e12, "unit": "TOPS",
+                "cores": n2, "sample": f"reference Conv2DOp (fp32) on the dequantized "
+                                       f"[{n2},128,28,28] conv, one image per thread"}
+    # config 3: the fp32 stack's ops per image equal the int8 stack's; the
+    # reference stack measured for the headline's cpu_baseline is this one
+    if stack_tops is not None:
+        out["3"] = {"value": stack_tops, "unit": "TFLOP/s", "cores": threads,
+                    "sample": "the reference fp32 Conv2DOp ResNet-50 stack timed for the headline "
+                              "cpu_baseline (same convolutions, same FLOPs per image)"}
+    # config 4: the MobileNetV2 sweep, fp32 on dequantized tensors, one image per thread
+    layers = mobilenetv2_layers()
+    xs = {}
+    for l in layers:
+        key = (l.cin, l.h)
+        if key not in xs:
+            xs[key] = rng.uniform(0, 2, (threads, l.cin, l.h, l.h)).astype(np.float32)
+    ws = [rng.normal(0, 0.1, (l.cout, 1 if l.kind == "dw" else l.cin, l.k, l.k)).astype(np.float32)
+          for l in layers]
+
+    def c4():
+        for l, wl in zip(layers, ws):
+            g = l.cin if l.kind == "dw" else 1
+            ref.conv2d(xs[(l.cin, l.h)], wl, None, strides=(l.stride, l.stride),
+                       pads=(l.k // 2,) * 4, group=g, depthwise=l.kind == "dw", nthreads=threads)
+    t = _ref_seconds(c4, min_s=2.0, max_reps=5)
+    macs = sum(l.macs_per_image for l in layers)
+    out["4"] = {"value": threads * 2 * macs / t / 1e12, "unit": "TOPS", "cores": threads,
+                "images_per_s": threads / t,
+                "sample": f"reference Conv2DOp / DepthwiseConv2DOp (fp32) over the 17-block "
+                          f"sweep's 52 convolutions, {threads} images, one per thread"}
+    return out
+
+
+def gpu_workloads(peaks: dict) -> dict:
+    """Configs 1-4 on this GPU (CUDA events on the launching stream, after
+    warm-up), each with its roofline fraction and the denominator it uses."""
+    from computeengine_b200 import conv_bench, mobilenet, resnet
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    src = "MEASURED_PEAKS.json" if "bf16_tflops" in peaks else "fallback"
+    c12 = {r["config"]: r for r in conv_bench.bench_configs(iters=200)}
+    r1, r2 = c12[1], c12[2]
+    f3 = resnet.bench_f32(32, iters=20)
+    m4 = mobilenet.benchmark(64, 50)
+    return {
+        "1": {"workload": r1["workload"], "value": r1["gflops"] / 1e3, "unit": "TFLOP/s",
+              "us_per_call": r1["us"], "dtype": "f32 (bf16x3)",
+              "roofline": {"bound": "latency (0.23 GFLOP, three launches)",
+                           "frac": r1["frac_of_bf16_peak_over_3"],
+                           "denominator": f"bf16 burst / 3 = {bf16 / 3:.0f} TFLOP/s ({src})"}},
+        "2": {"workload": r2["workload"], "value": r2["kernel_tops"], "unit": "TOPS",
+              "kernel_us": r2["kernel_us"], "drop_in_us": r2["drop_in_us"],
+              "drop_in_tops": r2["drop_in_tops"], "dtype": "int8",
+              "roofline": {"bound": "tensor", "frac": r2["frac_of_2x_bf16_peak"],
+                           "denominator": f"2 x bf16 burst = {2 * bf16:.0f} TOPS ({src})"}},
+        "3": {"workload": f3["workload"], "value": f3["tflops"], "unit": "TFLOP/s",
+              "ms_per_step": f3["ms_per_step"], "batch": f3["batch"],
+              "images_per_s": f3["images_per_s"], "dtype": "f32 (bf16x3)",
+              "roofline": {"bound": "tensor", "frac": f3["tflops"] / (bf16 / 3),
+                           "denominator": f"bf16 burst / 3 = {bf16 / 3:.0f} TFLOP/s ({src})"}},
+        "4": {"workload": m4["workload"], "value": m4["tops"], "unit": "TOPS",
+              "ms_per_step": m4["ms_per_step"], "batch": m4["batch"],
+              "images_per_s": m4["images_per_s"], "dtype": "int8",
+              "algorithmic_gbs": m4["algorithmic_gbs"],
+              "roofline": {"bound": "hbm", "frac": m4["algorithmic_gbs"] / hbm,
+                           "denominator": f"HBM copy {hbm:.0f} GB/s ({src})"}},
+    }
+
+
 # ------------------------------------------------------------------ ours
 
 def run_ours(args, world, rank, local):
@@ -389,14 +549,18 @@ def run_ours(args, world, rank, local):
     L.launch_count(reset=True)
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    props = torch.cuda.get_device_properties(dev)
+    pci = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    with ClockSampler(local, pci) as clocks:
         barrier(world)
         torch.cuda.synchronize(dev)
+        clocks.mark_start()
         start.record(stream)
         for _ in range(args.steps):
             net.replay()
         stop.record(stream)
         torch.cuda.synchronize(dev)
+        clocks.mark_stop()
         barrier(world)
     ms = start.elapsed_time(stop)
     ms_max = max_over_ranks(ms, dev)
@@ -404,8 +568,8 @@ def run_ours(args, world, rank, local):
     total_images = b * world * args.steps
     value = ops_img * total_images / (ms_max / 1e3) / 1e12
 
-    # ---- per-kernel durations of the convolutions (roofline of the dominant kernel)
-    conv_ms, conv_ops = per_layer_times(net, layers, x_dev, args.steps, ops_img // 2, b)
+    # ---- per-launch durations of the convolutions (roofline of the dominant kernel)
+    conv_ms, conv_ops = per_layer_times(net, layers, ops_img // 2, b)
 
     # ---- end to end through the C ABI with host buffers: every step copies its
     # input from pinned host memory and reads its output back; the copies run
@@ -416,7 +580,7 @@ def run_ours(args, world, rank, local):
     out_stage = [torch.empty_like(net.output) for _ in range(2)]
     out_pin = [torch.empty(net.output.shape, dtype=torch.uint8).pin_memory() for _ in range(2)]
 
-    def e2e_steps(nsteps):
+    def e2e_steps(nsteps, compute=True):
         d2h_done = [None, None]
         with torch.cuda.stream(copy):
             x_next.copy_(x_pin, non_blocking=True)
@@ -430,7 +594,8 @@ def run_ours(args, world, rank, local):
                 with torch.cuda.stream(copy):
                     x_next.copy_(x_pin, non_blocking=True)
                 h2d_done = copy.record_event()
-            net.replay()
+            if compute:
+                net.replay()
             j = i % 2
             if d2h_done[j] is not None:
                 stream.wait_event(d2h_done[j])
@@ -452,6 +617,17 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), dev)
     e2e_value = ops_img * total_images / (e2e_ms / 1e3) / 1e12
+    # the same loop with the stack left out: the pinned-copy ceiling of e2e on
+    # this box (all ranks copy at once, as in the e2e run)
+    e2e_steps(2, compute=False)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0.record(stream)
+    e2e_steps(args.steps, compute=False)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    copy_ms = max_over_ranks(e0.elapsed_time(e1), dev)
+    copy_value = ops_img * total_images / (copy_ms / 1e3) / 1e12
 
     if prev_affinity is not None:
         os.sched_setaffinity(0, prev_affinity)
@@ -476,12 +652,19 @@ def run_ours(args, world, rank, local):
         return
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    workloads = None
+    if world == 1 and not args.no_workloads:
+        workloads = gpu_workloads(peaks)
+        if cpu is not None:
+            for k, v in cpu_workloads(cpu_threads(), cpu["value"]).items():
+                workloads[k]["cpu_baseline"] = v
     bf16 = peaks.get("bf16_tflops")
     peak_src = "2x measured cuBLAS bf16 burst (MEASURED_PEAKS.json)"
     if bf16 is None:
         bf16, peak_src = 1590.0, "2x fallback bf16 1.59 PFLOP/s"
     peak = 2.0 * bf16
     achieved = conv_ops * 2 / (conv_ms / 1e3) / 1e12  # TOPS over the conv launches
+    step_ms = ms_max / args.steps
     traffic = None
     if PROFILE_JSON.exists():
         prof = json.loads(PROFILE_JSON.read_text())
@@ -505,79 +688,83 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_value, "unit": "TOPS",
                 "h2d_bytes_per_step": int(x_pin.numel()),
                 "d2h_bytes_per_step": int(out_pin[0].numel()),
-                "copies": "pinned H2D / D2H on a second stream, double-buffered"},
+                "copies": "pinned H2D / D2H on a second stream, double-buffered",
+                "copy_only_ms_per_step": copy_ms / args.steps,
+                "copy_only_ceiling": copy_value,
+                "frac_of_copy_ceiling": e2e_value / copy_value,
+                "host_copy_gbs": (int(x_pin.numel()) + int(out_pin[0].numel())) * world
+                                 * args.steps / (copy_ms / 1e3) / 1e9},
         "roofline": {"bound": "tensor", "kernel": "conv_igemm_kernel (int8, all 53 layers)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src,
                      "traffic": traffic,
-                     "conv_ms_per_step": conv_ms, "step_ms": ms_max / args.steps},
+                     "conv_ms_per_step": conv_ms, "step_ms": step_ms,
+                     "conv_share_of_step": conv_ms / step_ms,
+                     "timing": "each conv launch timed in a CUDA graph of 10 back-to-back "
+                               "launches of itself (events on the replay stream); achieved = "
+                               "ops of the 53 convs / the sum of their launch times",
+                     "frac_of_nominal_int8_4500": achieved / 4500.0,
+                     "layer_us": {k: round(v * 1e3, 2) for k, v in net.layer_ms.items()}},
         "clocks": clocks.summary(),
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if workloads is not None:
+        line["workloads"] = workloads
     print(json.dumps(line), flush=True)
 
 
-def per_layer_times(net, layers, x_dev, steps, macs_img, batch):
-    """Times every convolution launch with external CUDA events captured into a
-    second graph of the stack; returns (ms of all conv launches per step,
-    MACs per step)."""
+def per_layer_times(net, layers, macs_img, batch, reps=10):
+    """Per-launch durations of the 53 convolutions in the regime the step runs
+    in: each layer's launch is captured `reps` times back to back into a CUDA
+    graph of its own, replayed once to warm, then timed with CUDA events on the
+    replay stream.  Returns (ms of one launch of every conv, summed; MACs per
+    step).  Unlike events recorded between the kernels of the step's graph,
+    this adds no event node between launches, so the sum can be compared with
+    the step time."""
     import torch
     L = net.L
     dev = net.device
-    stream_handle = None
-    evs = []
-    g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     torch.cuda.synchronize(dev)
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(g, stream=s):
-            stream_handle = torch.cuda.current_stream(dev).cuda_stream
-            cur = torch.cuda.current_stream(dev)
-            L.check(L.lib.ie_cuda_q8_stem_pack_input(x_dev.data_ptr(), net.stem_in.data_ptr(),
-                                                     net.batch, 3, net.image, net.image, 0x80,
-                                                     stream_handle))
-            for l in layers:
-                src = net.stem_in if l.src == "input" else net.acts[l.src]
-                a = torch.cuda.Event(enable_timing=True, external=True)
-                z = torch.cuda.Event(enable_timing=True, external=True)
-                a.record(cur)
-                L.check(L.lib.ie_cuda_conv2d_q8(net.descs[l.name], net.qp[l.name], src.data_ptr(),
-                                                net.packed[l.name].data_ptr(),
-                                                net.bias[l.name].data_ptr(),
-                                                net.mult[l.name].data_ptr(),
-                                                net.acts[l.name].data_ptr(), stream_handle))
-                z.record(cur)
-                evs.append((l, a, z))
-                if l.name == "stem":
-                    st = net.acts["stem"]
-                    L.check(L.lib.ie_cuda_q8_maxpool2d(st.data_ptr(), net.acts["pool"].data_ptr(),
-                                                       net.batch, st.shape[1], st.shape[2], 64, 3,
-                                                       2, 1, 0, stream_handle))
-    torch.cuda.synchronize(dev)
-    tot = {l.name: 0.0 for l in layers}
-    reps = max(3, min(steps, 10))
-    for _ in range(reps):
-        g.replay()
+    per = {}
+    for l in layers:
+        src = net.stem_in if l.src == "input" else net.acts[l.src]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                h = torch.cuda.current_stream(dev).cuda_stream
+                for _ in range(reps):
+                    L.check(L.lib.ie_cuda_conv2d_q8(net.descs[l.name], net.qp[l.name],
+                                                    src.data_ptr(), net.packed[l.name].data_ptr(),
+                                                    net.bias[l.name].data_ptr(),
+                                                    net.mult[l.name].data_ptr(),
+                                                    net.acts[l.name].data_ptr(), h))
+        with torch.cuda.stream(s):
+            g.replay()
+            a = torch.cuda.Event(enable_timing=True)
+            z = torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            g.replay()
+            z.record(s)
         torch.cuda.synchronize(dev)
-        for l, a, z in evs:
-            tot[l.name] += a.elapsed_time(z)
-    conv_ms = sum(tot.values()) / reps
-    net.layer_ms = {k: v / reps for k, v in tot.items()}
-    return conv_ms, macs_img * batch
+        per[l.name] = a.elapsed_time(z) / reps
+        del g
+    net.layer_ms = per
+    return sum(per.values()), macs_img * batch
 
 
 def main():
     args = parse_args()
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup(args.gpus, args.impl)
     try:
         if args.impl == "reference":
             run_reference_arm(args, world, rank)
         else:
             run_ours(args, world, rank, local)
     finally:
-        if world > 1:
+        if world > 1 and args.impl == "ours":
             import torch.distributed as dist
             dist.destroy_process_group()
 

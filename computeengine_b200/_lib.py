@@ -76,6 +76,9 @@ def _load() -> C.CDLL:
         "ie_cuda_q8_pack_weights": (C.c_int, [P(ConvDesc), _p, _p, _p]),
         "ie_cuda_q8_pack_input": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p]),
         "ie_cuda_q8_unpack_output": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
+        "ie_cuda_q8_halo_input_bytes": (C.c_size_t, [P(ConvDesc)]),
+        "ie_cuda_q8_pack_input_halo": (C.c_int, [P(ConvDesc), _p, _p, _i32, _p]),
+        "ie_cuda_q8_halo_nhwc": (C.c_int, [P(ConvDesc), _p, _p, _i32, _p]),
         "ie_cuda_conv2d_q8": (C.c_int, [P(ConvDesc), P(Q8Params), _p, _p, _p, _p, _p, _p]),
         "ie_cuda_conv2d_q8_acc": (C.c_int, [P(ConvDesc), P(Q8Params), _p, _p, _p, _p, _p]),
         "ie_cuda_dw_q8_packed_weight_bytes": (C.c_size_t, [P(ConvDesc)]),

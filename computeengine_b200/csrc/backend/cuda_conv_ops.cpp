@@ -593,17 +593,19 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   q.qmin = has_qmin_ ? static_cast<int32_t>(qmin_) : (y_signed_ ? -128 : 0);
   q.qmax = has_qmax_ ? static_cast<int32_t>(qmax_) : (y_signed_ ? 127 : 255);
   uint32_t xor_mask = 0;
+  bool halo = false;
   if (!depthwise) {
     if (d.group != 1) return ie::Error::unsupported("grouped int8 convolution (1 < group < C)");
     if (q.zp_x != 0) {
       // uint8 with zero point 128 is int8 with zero point 0 after flipping
-      // the top bit; other zero points are not on the tensor-core path
+      // the top bit; any other zero point reads a haloed input whose padding
+      // holds the zero point (the kernel folds -zp_x * sum(w) into the bias)
       if (q.x_signed == 0 && q.zp_x == 128) {
         xor_mask = 0x80;
         q.zp_x = 0;
         q.x_signed = 1;
       } else {
-        return ie::Error::unsupported("dense int8 path takes zero point 0, or 128 for uint8");
+        halo = true;
       }
     }
   } else if (!(d.group == d.c && d.c == d.m && w.shape.dims[1] == 1)) {
@@ -615,12 +617,12 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   auto xd = to_device(dev_, kSlotX, x, st);
   if (!xd.has_value()) return xd.error();
   const int64_t c_store = (d.c + 15) / 16 * 16, m_store = (d.m + 15) / 16 * 16;
-  auto xn = dev_.scratch(kSlotXPacked, static_cast<size_t>(d.n * d.h * d.w * c_store));
+  auto xn = dev_.scratch(kSlotXPacked, halo ? ie_cuda_q8_halo_input_bytes(&d)
+                                             : static_cast<size_t>(d.n * d.h * d.w * c_store));
   if (!xn.has_value()) return xn.error();
-  if (auto e = to_status(ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st));
-      !e.has_value()) {
-    return e;
-  }
+  const int prc = halo ? ie_cuda_q8_pack_input_halo(&d, *xd, *xn, q.zp_x, st)
+                       : ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st);
+  if (auto e = to_status(prc); !e.has_value()) return e;
   // packed weights, bias and multipliers: uploaded once per host buffer
   bool fresh = false;
   const size_t wbytes = depthwise ? ie_cuda_dw_q8_packed_weight_bytes(&d)

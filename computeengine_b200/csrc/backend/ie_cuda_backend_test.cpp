@@ -752,13 +752,15 @@ int run_gpu(const std::string& dir) {
   }
   // int8 post-training quantization of an fp32 Conv2D + ReLU: calibrate the
   // input and output ranges on the fp32 op, quantize, run the int8 op with
-  // the emitted attributes, dequantize
+  // the emitted attributes, dequantize.  The input range [-0.3, 1.0] is not
+  // symmetric about 0, so the calibrated activation zero point (about 59) is
+  // neither 0 nor 128 and the dense int8 kernel runs on its haloed input.
   {
     Lcg rng(4);
     const int64_t n = 2, c = 32, h = 20, w = 20, m = 48;
     HostTensor x({n, c, h, w}, ie::DType::F32), wt({m, c, 3, 3}, ie::DType::F32),
         b({m}, ie::DType::F32);
-    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-0.3f, 1.f);
     for (int64_t i = 0; i < wt.t.numel(); ++i) wt.data<float>()[i] = rng.uniform(-0.1f, 0.1f);
     for (int64_t i = 0; i < m; ++i) b.data<float>()[i] = rng.uniform(-0.05f, 0.05f);
     const ie::Attrs conv_attrs{{"pads", std::vector<int64_t>{1, 1, 1, 1}}};

@@ -67,6 +67,12 @@ struct IgemmArgs {
   int32_t m_tiles, n_tiles;
   // epilogue
   const int32_t* bias_i32;   // int8 path, may be null
+  // int8 path, activation zero point zp_x != 0: the A operand holds the raw
+  // stored activations (padding materialised as zp_x), and the epilogue adds
+  // -zp_x * wsum[ch] (wrapping int32, like the bias) so that the accumulator
+  // becomes sum (x - zp_x) * w
+  const int32_t* wsum;
+  int32_t zp_x;
   const float* bias_f32;     // fp32 path, may be null
   const float* mult;         // int8 path: per-channel requantize multiplier
   int32_t zp_y, qmin, qmax;  // int8 path: output zero point and clamp range
@@ -839,6 +845,11 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
             const int32_t ch = wcol0 + lane + 32 * r;
             const bool in = ch < args.m;
             bias[r] = (in && args.bias_i32 != nullptr) ? __ldg(args.bias_i32 + ch) : 0;
+            if (in && args.zp_x != 0) {
+              bias[r] = static_cast<int32_t>(static_cast<uint32_t>(bias[r]) -
+                                             static_cast<uint32_t>(args.zp_x) *
+                                                 static_cast<uint32_t>(__ldg(args.wsum + ch)));
+            }
             rc[r] = split_multiplier((in && args.mult != nullptr) ? __ldg(args.mult + ch) : 0.0f);
             if (rc[r].mant != 0) smin = min(smin, rc[r].shift);
             fast = fast && rc[r].mant >= 0;

@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 
 #include "conv_igemm.cuh"
 
@@ -80,6 +81,271 @@ __global__ void __launch_bounds__(256) dwconv_q8_nhwc(const uint8_t* __restrict_
     out[j >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (j & 3));
   }
   *reinterpret_cast<uint4*>(y + pix * a.c_store + c0) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// ------------------------------------------------ 3x3 depthwise, dp4a rows
+//
+// The MobileNetV2 depthwise layers (3x3, stride 1 or 2, dilation 1) on
+// packed-byte arithmetic.  A thread owns 4 channels (one 32-bit word of each
+// NHWC pixel) x 4 output columns and walks down a chunk of output rows.  Each
+// input row it needs is loaded once (6 or 9 pixel words, requested one output
+// row ahead), byte-transposed in registers so that a word holds 4 consecutive
+// pixels of one channel, and shifted by funnel shifts into the 4 windows
+// [x(ox-1), x(ox), x(ox+1), .] of its output columns; the windows of the
+// three input rows under an output row slide down as the thread moves on, and
+// one dp4a per (window, filter row) adds three taps.  Filter words and
+// requantize constants are set up once per thread.  The
+// activation zero point is handled like the dense kernel's: pixels outside
+// the image read as the zero point's byte and -zp_x * sum(w[c]) is folded
+// into the bias, so every tap contributes (x - zp_x) * w.  The requantize
+// constants of the thread's 4 channels stay in registers.
+struct Dw3Args {
+  int32_t n, h, w, c_store;  // input NHWC
+  int32_t out_h, out_w, pad_t, pad_l;
+  int32_t c;                 // real channels (== m)
+  int32_t zp_x;
+  uint32_t zp4;              // zp_x's byte, replicated
+  int32_t zp_y, qmin, qmax;
+  int32_t words, col_groups, row_strips;  // c_store / 4, ceil(out_w / 4), ceil(out_h / R)
+};
+
+template <bool kXSigned>
+__device__ __forceinline__ int32_t dp4a_xw(uint32_t x, uint32_t w, int32_t c) {
+  int32_t d;
+  if constexpr (kXSigned) {
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(w), "r"(c));
+  } else {
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(w), "r"(c));
+  }
+  return d;
+}
+
+// 4x4 byte transpose: out[j] = [p0.j, p1.j, p2.j, p3.j].
+__device__ __forceinline__ void transpose4x4(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3,
+                                             uint32_t (&out)[4]) {
+  const uint32_t t0 = __byte_perm(p0, p1, 0x5140), t1 = __byte_perm(p2, p3, 0x5140);
+  const uint32_t t2 = __byte_perm(p0, p1, 0x7362), t3 = __byte_perm(p2, p3, 0x7362);
+  out[0] = __byte_perm(t0, t1, 0x5410);
+  out[1] = __byte_perm(t0, t1, 0x7632);
+  out[2] = __byte_perm(t2, t3, 0x5410);
+  out[3] = __byte_perm(t2, t3, 0x7632);
+}
+
+// Windows of one input row for the thread's 4 output columns and 4 channels:
+// win[k][j] = [x(c0 + j) at the 4 pixels starting under output column k]
+// (stride 1: pixels k .. k+3 of the row segment; stride 2: 2k .. 2k+3).
+template <int kStride>
+__device__ __forceinline__ void dw_row_windows(const uint32_t (&p)[3 * kStride + 3],
+                                               uint32_t (&win)[4][4]) {
+  uint32_t A[4], B[4];
+  transpose4x4(p[0], p[1], p[2], p[3], A);
+  if constexpr (kStride == 1) {
+    const uint32_t u0 = __byte_perm(p[4], p[5], 0x5140), u1 = __byte_perm(p[4], p[5], 0x7362);
+    B[0] = u0;
+    B[1] = u0 >> 16;
+    B[2] = u1;
+    B[3] = u1 >> 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      win[0][j] = A[j];
+      win[1][j] = __funnelshift_r(A[j], B[j], 8);
+      win[2][j] = __funnelshift_r(A[j], B[j], 16);
+      win[3][j] = __funnelshift_r(A[j], B[j], 24);
+    }
+  } else {
+    transpose4x4(p[4], p[5], p[6], p[7], B);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      win[0][j] = A[j];
+      win[1][j] = __funnelshift_r(A[j], B[j], 16);
+      win[2][j] = B[j];
+      win[3][j] = __funnelshift_r(B[j], p[8] >> (8 * j), 16);
+    }
+  }
+}
+
+template <int kStride, int kChunk, bool kXSigned, bool kYSigned>
+__global__ void __launch_bounds__(128) dwconv3x3_q8_nhwc(const uint8_t* __restrict__ x,
+                                                         const int8_t* __restrict__ wp,
+                                                         const int32_t* __restrict__ bias,
+                                                         const float* __restrict__ mult,
+                                                         uint8_t* __restrict__ y, Dw3Args a) {
+  constexpr int kPix = 3 * kStride + 3;  // input pixels under 4 output columns
+  constexpr int kNew = kStride;          // input rows each further output row adds
+  // grid: x = (column group, channel word) with the word fastest, y = chunk
+  // of kChunk output rows, z = image; one 32-bit division splits x.
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<uint32_t>(a.col_groups * a.words)) return;
+  const int32_t grp = static_cast<int32_t>(idx / static_cast<uint32_t>(a.words));
+  const int32_t wd = static_cast<int32_t>(idx) - grp * a.words;
+  const int32_t img = blockIdx.z;
+  const int32_t c0 = wd * 4;
+  const int32_t ox0 = grp * 4, oy_begin = blockIdx.y * kChunk;
+  const int32_t oy_end = min(oy_begin + kChunk, a.out_h);
+
+  // filter rows of the 4 channels: wk[ky][j] = [w(ky,0), w(ky,1), w(ky,2), 0]
+  uint32_t wk[3][4];
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const uint32_t w0 = __ldg(reinterpret_cast<const uint32_t*>(wp + (ky * 3 + 0) * a.c_store + c0));
+    const uint32_t w1 = __ldg(reinterpret_cast<const uint32_t*>(wp + (ky * 3 + 1) * a.c_store + c0));
+    const uint32_t w2 = __ldg(reinterpret_cast<const uint32_t*>(wp + (ky * 3 + 2) * a.c_store + c0));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t t01 = __byte_perm(w0, w1, j | ((4 + j) << 4));
+      const uint32_t t2 = __byte_perm(w2, 0u, j | 0x4440);
+      wk[ky][j] = __byte_perm(t01, t2, 0x5410);
+    }
+  }
+
+  // Input row loader: pixel words of row iy under the thread's columns; rows
+  // and columns outside the image read as the zero point.
+  const uint8_t* const xb = x + static_cast<int64_t>(img) * a.h * a.w * a.c_store + c0;
+  const int32_t ix0 = ox0 * kStride - a.pad_l;
+  auto load_row = [&](int32_t iy, uint32_t (&p)[kPix]) {
+    const bool row_in = iy >= 0 && iy < a.h;
+    const uint8_t* const row = xb + static_cast<int64_t>(row_in ? iy : 0) * a.w * a.c_store;
+#pragma unroll
+    for (int q = 0; q < kPix; ++q) {
+      const int32_t ix = ix0 + q;
+      p[q] = (row_in && ix >= 0 && ix < a.w)
+                 ? __ldg(reinterpret_cast<const uint32_t*>(row + static_cast<int64_t>(ix) * a.c_store))
+                 : a.zp4;
+    }
+  };
+
+  // requantize constants (the implicit-GEMM epilogue's rules, per thread)
+  int32_t beff[4], mnt[4];
+  long long add[4];
+  RequantConst rq[4];
+  int32_t smin = 1 << 20;
+  bool fast = true, fits = true;
+  const long long acc_bound = 9ll * 255 * 128;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int32_t ch = c0 + j;
+    const bool in = ch < a.c;
+    const int32_t wsum = dp4a_xw<true>(wk[0][j], 0x01010101u,
+                                       dp4a_xw<true>(wk[1][j], 0x01010101u,
+                                                     dp4a_xw<true>(wk[2][j], 0x01010101u, 0)));
+    const int32_t b = (in && bias != nullptr) ? __ldg(bias + ch) : 0;
+    beff[j] = static_cast<int32_t>(static_cast<uint32_t>(b) -
+                                   static_cast<uint32_t>(a.zp_x) * static_cast<uint32_t>(wsum));
+    rq[j] = split_multiplier(in ? __ldg(mult + ch) : 0.0f);
+    if (rq[j].mant != 0) smin = min(smin, rq[j].shift);
+    fast = fast && rq[j].mant >= 0;
+    const long long bb = beff[j];
+    fits = fits && (bb < 0 ? -bb : bb) + acc_bound < (1ll << 31);
+  }
+  if (smin == (1 << 20)) smin = 33;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (rq[j].mant != 0 && rq[j].shift - smin > 7) fast = false;
+  }
+  fast = fast && smin >= 32 && smin <= 53;
+  const int mode = (fast && a.zp_y <= a.qmin && fits) ? kReqFold
+                   : (fast && smin >= 33)             ? kReqSigned
+                                                      : kReqExact;
+  const long long c_add = (1ll << (smin - 1)) + static_cast<long long>(a.zp_y) * (1ll << smin);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mnt[j] = (mode != kReqExact && rq[j].mant != 0) ? (rq[j].mant >> (rq[j].shift - smin)) : 0;
+    add[j] = static_cast<long long>(beff[j]) * mnt[j] + c_add;
+  }
+  const int32_t hi_c = static_cast<int32_t>(c_add >> 32), shm = smin - 32;
+
+  // Windows of the input rows under the current output row, kept in three
+  // slots: relative input row r lives in slot r % 3, so walking down by
+  // kStride rows only overwrites the slots of the rows that drop out.  The
+  // row loop is unrolled by three so every slot index is a constant (no
+  // register moves).  The kNew new rows of each output row are requested one
+  // output row ahead.
+  uint32_t win[3][4][4];
+  uint32_t pf[kNew][kPix];
+  const int32_t iy_base = oy_begin * kStride - a.pad_t;  // relative input row 0
+  {
+    uint32_t p[kPix];
+#pragma unroll
+    for (int r = 0; r < 3 - kNew; ++r) {
+      load_row(iy_base + r, p);
+      dw_row_windows<kStride>(p, win[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < kNew; ++r) load_row(iy_base + 3 - kNew + r, pf[r]);
+  }
+  const int64_t y_row_step = static_cast<int64_t>(a.out_w) * a.c_store;
+  const bool col_ok[4] = {ox0 < a.out_w, ox0 + 1 < a.out_w, ox0 + 2 < a.out_w, ox0 + 3 < a.out_w};
+
+  // One output row t of the chunk (T = t % 3 as a constant).
+  auto row = [&](auto phase, int32_t t) {
+    constexpr int T = decltype(phase)::value;
+    constexpr int s0 = (kStride * T) % 3, s1 = (kStride * T + 1) % 3, s2 = (kStride * T + 2) % 3;
+    const int32_t oy = oy_begin + t;
+#pragma unroll
+    for (int r = 0; r < kNew; ++r) {
+      constexpr int dummy = 0;
+      (void)dummy;
+      dw_row_windows<kStride>(pf[r], win[(kStride * T + 3 - kNew + r) % 3]);
+    }
+    if (oy + 1 < oy_end) {
+      const int32_t iy_next = iy_base + (t + 1) * kStride + 3 - kNew;
+#pragma unroll
+      for (int r = 0; r < kNew; ++r) load_row(iy_next + r, pf[r]);
+    }
+    uint8_t* const yrow = y + ((static_cast<int64_t>(img) * a.out_h + oy) * a.out_w + ox0) * a.c_store + c0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      int32_t acc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int32_t v = dp4a_xw<kXSigned>(win[s0][k][j], wk[0][j], 0);
+        v = dp4a_xw<kXSigned>(win[s1][k][j], wk[1][j], v);
+        acc[j] = dp4a_xw<kXSigned>(win[s2][k][j], wk[2][j], v);
+      }
+      int32_t q[4];
+      if (mode == kReqFold) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const long long pr = static_cast<long long>(acc[j]) * mnt[j] + add[j];
+          q[j] = min(max(static_cast<int32_t>(pr >> 32) >> shm, a.qmin), a.qmax);
+        }
+      } else if (mode == kReqSigned) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int32_t tt = static_cast<int32_t>(static_cast<uint32_t>(acc[j]) +
+                                                  static_cast<uint32_t>(beff[j]));
+          const int32_t sg = tt >> 31;
+          const long long cs = static_cast<long long>(
+              (static_cast<unsigned long long>(static_cast<uint32_t>(hi_c + sg)) << 32) |
+              static_cast<uint32_t>(sg));
+          const long long pr = static_cast<long long>(tt) * mnt[j] + cs;
+          q[j] = min(max(static_cast<int32_t>(pr >> 32) >> shm, a.qmin), a.qmax);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int32_t tt = static_cast<int32_t>(static_cast<uint32_t>(acc[j]) +
+                                                  static_cast<uint32_t>(beff[j]));
+          q[j] = requant_exact(tt, rq[j], a.zp_y, a.qmin, a.qmax);
+        }
+      }
+      if (col_ok[k]) {
+        const uint32_t lo = pack2_sat<kYSigned>(q[0], q[1]);
+        const uint32_t hi = pack2_sat<kYSigned>(q[2], q[3]);
+        *reinterpret_cast<uint32_t*>(yrow + k * a.c_store) = (lo & 0xFFFFu) | (hi << 16);
+      }
+    }
+  };
+  (void)y_row_step;
+  const int32_t rows = oy_end - oy_begin;
+#pragma unroll 1
+  for (int32_t t = 0; t < rows; t += 3) {
+    row(std::integral_constant<int, 0>{}, t);
+    if (t + 1 >= rows) break;
+    row(std::integral_constant<int, 1>{}, t + 1);
+    if (t + 2 >= rows) break;
+    row(std::integral_constant<int, 2>{}, t + 2);
+  }
 }
 
 // depthwise int8 weights [c, 1, kh, kw] -> [kh*kw][c_store], zero filled.

@@ -125,6 +125,7 @@ int igemm_max_bk(int bn, bool i8) {
 }
 
 constexpr int kSmemLimit = 227 * 1024;
+constexpr int kMaxDevices = 64;
 
 // One compiled variant of the implicit-GEMM kernel.
 struct Variant {
@@ -143,13 +144,23 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   const int smem = P::bytes(args.stages, args.num_k, args.out_bufs,
                             args.halo ? args.stage_bytes : P::kStage);
   if (smem > kSmemLimit) return fail(IE_UNSUPPORTED, "shared memory plan too large (%d)", smem);
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-  });
-  if (attr_err != cudaSuccess) {
-    return fail(IE_RUNTIME, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  // The shared-memory opt-in is a property of the function in each device's
+  // context: set it once per device this variant runs on.
+  static std::mutex mu;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(IE_RUNTIME, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(IE_UNSUPPORTED, "device ordinal %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      if (e != cudaSuccess) {
+        return fail(IE_RUNTIME, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      }
+      attr_set[dev] = true;
+    }
   }
   // producer, MMA issuer, EPI epilogue warps, output store warp
   kern<<<grid, 96 + EPI * 32, smem, st>>>(ta, tb, ty, args);
@@ -413,6 +424,24 @@ void packed_geom(const ie_conv2d_desc* d, int elem_bytes, int64_t* taps, int64_t
   *ck = ceil_div(c_store, bk_elems) * bk_elems;
 }
 
+// Bytes of the packed int8 weights proper; the per-channel weight sums
+// (int32 [round_up(m, 16)]) follow them in the same buffer.
+int64_t q8_packed_body_bytes(const ie_conv2d_desc* d) {
+  int64_t taps, ck;
+  packed_geom(d, 1, &taps, &ck);
+  return d->m * taps * ck;
+}
+
+// Fills the weight-sum trailer of a packed int8 weight buffer.
+int q8_write_weight_sums(const ie_conv2d_desc* d, void* packed, cudaStream_t st) {
+  const int64_t body = q8_packed_body_bytes(d);
+  const int64_t m_store = round_up(d->m, 16);
+  q8_weight_sums<<<static_cast<unsigned>(ceil_div(m_store * 32, 256)), 256, 0, st>>>(
+      static_cast<const int8_t*>(packed), reinterpret_cast<int32_t*>(static_cast<uint8_t*>(packed) + body),
+      static_cast<int32_t>(d->m), static_cast<int32_t>(m_store), body / d->m);
+  return check_launch("q8_weight_sums");
+}
+
 int check_dense(const ie_conv2d_desc* d) {
   if (d->group != 1) return fail(IE_UNSUPPORTED, "the tensor-core path runs group == 1 only");
   return IE_OK;
@@ -454,10 +483,8 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   if (rc != IE_OK) return rc;
   if ((rc = check_dense(d)) != IE_OK) return rc;
   if (q == nullptr) return fail(IE_INVALID_ARGUMENT, "null quantization parameters");
-  if (q->zp_x != 0) {
-    return fail(IE_UNSUPPORTED,
-                "the NHWC kernels take zero-point-0 activations; pack uint8/zp128 input with "
-                "ie_cuda_q8_pack_input(xor_mask=0x80)");
+  if (q->x_signed ? (q->zp_x < -128 || q->zp_x > 127) : (q->zp_x < 0 || q->zp_x > 255)) {
+    return fail(IE_INVALID_ARGUMENT, "activation zero point outside the storage type");
   }
   const int32_t lo_lim = q->y_signed ? -128 : 0, hi_lim = q->y_signed ? 127 : 255;
   if (q->qmin < lo_lim || q->qmax > hi_lim || q->qmin > q->qmax || q->zp_y < lo_lim ||
@@ -469,12 +496,31 @@ int run_q8(const ie_conv2d_desc* d, const ie_q8_params* q, const void* x, const 
   if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
   if (out_mode != kOutS32 && mult == nullptr) return fail(IE_INVALID_ARGUMENT, "mult is null");
   const int64_t c_store = round_up(d->c, 16);
+  // A nonzero activation zero point runs on the haloed input (padding stored
+  // as zp_x, see ie_cuda_q8_pack_input_halo): the same convolution with zero
+  // pads over an input grown by the pads, same output extent.
+  ie_conv2d_desc dh = *d;
+  ie_conv2d_shape sh = s;
+  if (q->zp_x != 0 && (s.pad_top | s.pad_left | s.pad_bottom | s.pad_right) != 0) {
+    dh.h = d->h + s.pad_top + s.pad_bottom;
+    dh.w = d->w + s.pad_left + s.pad_right;
+    dh.pad_top = dh.pad_left = dh.pad_bottom = dh.pad_right = 0;
+    dh.auto_pad = IE_PAD_NOTSET;
+    if ((rc = resolve(&dh, -1, &sh)) != IE_OK) return rc;
+    if (sh.out_h != s.out_h || sh.out_w != s.out_w) {
+      return fail(IE_RUNTIME, "haloed geometry changed the output extent");
+    }
+  }
   IgemmSetup su;
-  if ((rc = setup_igemm(d, s, 1, c_store, x, packed, &su, out_mode != kOutS32)) != IE_OK) {
+  if ((rc = setup_igemm(&dh, sh, 1, c_store, x, packed, &su, out_mode != kOutS32)) != IE_OK) {
     return rc;
   }
   IgemmArgs& a = su.args;
   a.bias_i32 = bias;
+  a.zp_x = q->zp_x;
+  a.wsum = q->zp_x != 0 ? reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(packed) +
+                                                           q8_packed_body_bytes(d))
+                        : nullptr;
   a.mult = mult;
   a.zp_y = q->zp_y;
   a.qmin = q->qmin;
@@ -525,13 +571,13 @@ namespace {
 // cudaGetSymbolAddress with that device current; it is looked up on the first
 // call made on each device and cached.
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[64] = {};
+void* g_noalloc_addr[kMaxDevices] = {};
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(IE_RUNTIME, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(IE_UNSUPPORTED, "device ordinal %d out of range", dev);
+  if (dev < 0 || dev >= kMaxDevices) return fail(IE_UNSUPPORTED, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_addr[dev] == nullptr) {
     void* p = nullptr;
@@ -585,10 +631,8 @@ int ie_cuda_take_device_error(uint32_t* code) {
 // -------------------------------------------------------------- int8
 
 size_t ie_cuda_q8_packed_weight_bytes(const ie_conv2d_desc* desc) {
-  if (desc == nullptr) return 0;
-  int64_t taps, ck;
-  packed_geom(desc, 1, &taps, &ck);
-  return static_cast<size_t>(desc->m * taps * ck);
+  if (desc == nullptr || desc->m <= 0) return 0;
+  return static_cast<size_t>(q8_packed_body_bytes(desc) + 4 * round_up(desc->m, 16));
 }
 
 int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
@@ -604,7 +648,8 @@ int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* p
   pack_weights_q8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
       w, static_cast<int8_t*>(packed), static_cast<int32_t>(desc->m),
       static_cast<int32_t>(desc->c), static_cast<int32_t>(taps), static_cast<int32_t>(ck));
-  return check_launch("pack_weights_q8");
+  if ((rc = check_launch("pack_weights_q8")) != IE_OK) return rc;
+  return q8_write_weight_sums(desc, packed, as_stream(stream));
 }
 
 int ie_cuda_q8_pack_input(const void* x_nchw, void* x_nhwc, int64_t n, int64_t c, int64_t h,
@@ -638,6 +683,60 @@ int ie_cuda_q8_unpack_output(const void* y_nhwc, void* y_nchw, int64_t n, int64_
       static_cast<const uint8_t*>(y_nhwc), static_cast<uint8_t*>(y_nchw),
       static_cast<int32_t>(c), hw, static_cast<int32_t>(c_store));
   return check_launch("unpack_nhwc_to_nchw_u8");
+}
+
+size_t ie_cuda_q8_halo_input_bytes(const ie_conv2d_desc* desc) {
+  ie_conv2d_shape s;
+  if (desc == nullptr || resolve(desc, -1, &s) != IE_OK) return 0;
+  return static_cast<size_t>(desc->n * (desc->h + s.pad_top + s.pad_bottom) *
+                             (desc->w + s.pad_left + s.pad_right) * round_up(desc->c, 16));
+}
+
+int ie_cuda_q8_pack_input_halo(const ie_conv2d_desc* desc, const void* x_nchw, void* x_halo,
+                               int32_t zp_x, void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if (x_nchw == nullptr || x_halo == nullptr) return fail(IE_INVALID_ARGUMENT, "null pointer");
+  if (zp_x < -128 || zp_x > 255) return fail(IE_INVALID_ARGUMENT, "zero point outside 8 bits");
+  const int64_t hp = desc->h + s.pad_top + s.pad_bottom, wp = desc->w + s.pad_left + s.pad_right;
+  const int64_t c_store = round_up(desc->c, 16);
+  if (hp > INT32_MAX || wp > INT32_MAX || hp * wp > (int64_t{1} << 40)) {
+    return fail(IE_UNSUPPORTED, "activation too large");
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(hp * wp, 32)), static_cast<unsigned>(ceil_div(c_store, 32)),
+            static_cast<unsigned>(desc->n));
+  if (grid.z > 65535 || grid.y > 65535) return fail(IE_UNSUPPORTED, "batch or channels too large");
+  pack_nchw_to_nhwc_halo_u8<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x_nchw), static_cast<uint8_t*>(x_halo),
+      static_cast<int32_t>(desc->c), static_cast<int32_t>(desc->h), static_cast<int32_t>(desc->w),
+      static_cast<int32_t>(c_store), static_cast<int32_t>(s.pad_top),
+      static_cast<int32_t>(s.pad_left), static_cast<int32_t>(hp), static_cast<int32_t>(wp),
+      static_cast<uint8_t>(zp_x & 0xFF));
+  return check_launch("pack_nchw_to_nhwc_halo_u8");
+}
+
+int ie_cuda_q8_halo_nhwc(const ie_conv2d_desc* desc, const void* x_nhwc, void* x_halo,
+                         int32_t zp_x, void* stream) {
+  ie_conv2d_shape s;
+  int rc = resolve(desc, -1, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_ptr(x_nhwc, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(x_halo, "x_halo", 16)) != IE_OK) return rc;
+  if (zp_x < -128 || zp_x > 255) return fail(IE_INVALID_ARGUMENT, "zero point outside 8 bits");
+  const int64_t hp = desc->h + s.pad_top + s.pad_bottom, wp = desc->w + s.pad_left + s.pad_right;
+  if (hp > INT32_MAX || wp > INT32_MAX || desc->n > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "activation too large");
+  }
+  const int64_t c_store = round_up(desc->c, 16);
+  const int64_t total = desc->n * hp * wp * (c_store / 16);
+  halo_nhwc_u8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint8_t*>(x_nhwc), static_cast<uint8_t*>(x_halo),
+      static_cast<int32_t>(desc->n), static_cast<int32_t>(desc->h), static_cast<int32_t>(desc->w),
+      static_cast<int32_t>(c_store), static_cast<int32_t>(s.pad_top),
+      static_cast<int32_t>(s.pad_left), static_cast<int32_t>(hp), static_cast<int32_t>(wp),
+      static_cast<uint8_t>(zp_x & 0xFF));
+  return check_launch("halo_nhwc_u8");
 }
 
 int ie_cuda_conv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
@@ -688,6 +787,52 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
   const int32_t lo_lim = q->y_signed ? -128 : 0, hi_lim = q->y_signed ? 127 : 255;
   if (q->qmin < lo_lim || q->qmax > hi_lim || q->qmin > q->qmax) {
     return fail(IE_INVALID_ARGUMENT, "output clamp range outside the storage type");
+  }
+  constexpr int kDwRows = 8;  // output rows per thread of the 3x3 row kernel
+  const bool zp_fits = q->x_signed ? (q->zp_x >= -128 && q->zp_x <= 127)
+                                   : (q->zp_x >= 0 && q->zp_x <= 255);
+  if (desc->kh == 3 && desc->kw == 3 && desc->dil_h == 1 && desc->dil_w == 1 &&
+      desc->stride_h == desc->stride_w && (desc->stride_h == 1 || desc->stride_h == 2) &&
+      zp_fits && desc->n <= 65535 && ceil_div(s.out_h, kDwRows) <= 65535 && desc->h <= INT32_MAX &&
+      desc->w <= INT32_MAX && ceil_div(s.out_w, 4) * round_up(desc->c, 16) / 4 <= INT32_MAX) {
+    // 3x3, stride 1 or 2: the packed-byte (dp4a) row kernel
+    constexpr int kRows = kDwRows;
+    Dw3Args a;
+    a.n = static_cast<int32_t>(desc->n);
+    a.h = static_cast<int32_t>(desc->h);
+    a.w = static_cast<int32_t>(desc->w);
+    a.c_store = static_cast<int32_t>(round_up(desc->c, 16));
+    a.out_h = static_cast<int32_t>(s.out_h);
+    a.out_w = static_cast<int32_t>(s.out_w);
+    a.pad_t = static_cast<int32_t>(s.pad_top);
+    a.pad_l = static_cast<int32_t>(s.pad_left);
+    a.c = static_cast<int32_t>(desc->c);
+    a.zp_x = q->zp_x;
+    a.zp4 = 0x01010101u * static_cast<uint32_t>(q->zp_x & 0xFF);
+    a.zp_y = q->zp_y;
+    a.qmin = q->qmin;
+    a.qmax = q->qmax;
+    a.words = a.c_store / 4;
+    a.col_groups = static_cast<int32_t>(ceil_div(s.out_w, 4));
+    a.row_strips = static_cast<int32_t>(ceil_div(s.out_h, kRows));
+    const auto xp = static_cast<const uint8_t*>(x);
+    const auto wpk = static_cast<const int8_t*>(packed);
+    const auto yp = static_cast<uint8_t*>(y);
+    const dim3 grid(static_cast<unsigned>(ceil_div(int64_t{a.col_groups} * a.words, 128)),
+                    static_cast<unsigned>(a.row_strips), static_cast<unsigned>(desc->n));
+    const cudaStream_t st = as_stream(stream);
+    const int sel = (desc->stride_h == 2 ? 4 : 0) + (q->x_signed ? 2 : 0) + (q->y_signed ? 1 : 0);
+    switch (sel) {
+      case 0: dwconv3x3_q8_nhwc<1, kRows, false, false><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 1: dwconv3x3_q8_nhwc<1, kRows, false, true><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 2: dwconv3x3_q8_nhwc<1, kRows, true, false><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 3: dwconv3x3_q8_nhwc<1, kRows, true, true><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 4: dwconv3x3_q8_nhwc<2, kRows, false, false><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 5: dwconv3x3_q8_nhwc<2, kRows, false, true><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      case 6: dwconv3x3_q8_nhwc<2, kRows, true, false><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+      default: dwconv3x3_q8_nhwc<2, kRows, true, true><<<grid, 128, 0, st>>>(xp, wpk, bias, mult, yp, a); break;
+    }
+    return check_launch("dwconv3x3_q8_nhwc");
   }
   DwArgs a;
   a.n = static_cast<int32_t>(desc->n);
@@ -776,7 +921,11 @@ int ie_cuda_q8_stem_pack_weights(const int8_t* w, void* packed, int64_t m, int64
   const int64_t total = m * 4 * 64;
   stem_pack_weights_q8<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
       w, static_cast<int8_t*>(packed), static_cast<int32_t>(m), static_cast<int32_t>(c));
-  return check_launch("stem_pack_weights_q8");
+  int rc = check_launch("stem_pack_weights_q8");
+  if (rc != IE_OK) return rc;
+  ie_conv2d_desc d;
+  if ((rc = ie_cuda_q8_stem_desc(1, c, 2, 2, m, &d)) != IE_OK) return rc;
+  return q8_write_weight_sums(&d, packed, as_stream(stream));
 }
 
 int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,

@@ -108,6 +108,96 @@ __global__ void pack_weights_q8(const int8_t* __restrict__ w, int8_t* __restrict
   }
 }
 
+// Per-output-channel sums of packed int8 weights: wsum[mo] = sum of the
+// k_row bytes of row mo (rows past m, up to m_store, get 0).  The epilogue
+// folds -zp_x * wsum[mo] into the int32 bias, which turns the accumulator of
+// raw stored activations into sum (x - zp_x) * w.  One warp per row; k_row is
+// a multiple of 16 and rows start 16-byte aligned.
+__global__ void q8_weight_sums(const int8_t* __restrict__ packed, int32_t* __restrict__ wsum,
+                               int32_t m, int32_t m_store, int64_t k_row) {
+  const int32_t row = static_cast<int32_t>((blockIdx.x * static_cast<int64_t>(blockDim.x) +
+                                            threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= m_store) return;
+  int32_t acc = 0;
+  if (row < m) {
+    const int4* r = reinterpret_cast<const int4*>(packed + static_cast<int64_t>(row) * k_row);
+    for (int64_t i = lane; i < k_row / 16; i += 32) {
+      const int4 v = __ldg(r + i);
+      // __dp4a with all-ones multipliers sums four signed bytes
+      acc = __dp4a(v.x, 0x01010101, acc);
+      acc = __dp4a(v.y, 0x01010101, acc);
+      acc = __dp4a(v.z, 0x01010101, acc);
+      acc = __dp4a(v.w, 0x01010101, acc);
+    }
+  }
+  acc = __reduce_add_sync(0xFFFFFFFFu, acc);
+  if (lane == 0) wsum[row] = acc;
+}
+
+// NCHW 8-bit -> NHWC with a halo: y is [n, hp, wp, c_store] and pixel (iy, ix)
+// of y holds x[., iy - pt, ix - pl] when that lies inside the image, else the
+// fill byte; channels past c hold the fill byte too.  With fill = zp_x the
+// padding of a convolution run over y with zero pads contributes
+// (zp_x - zp_x) * w = 0, the reference's "padding is real 0.0".
+__global__ void pack_nchw_to_nhwc_halo_u8(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                          int32_t c, int32_t h, int32_t w, int32_t c_store,
+                                          int32_t pt, int32_t pl, int32_t hp, int32_t wp,
+                                          uint8_t fill) {
+  __shared__ uint8_t tile[32][33];
+  const int64_t img = blockIdx.z;
+  const int64_t hw = static_cast<int64_t>(h) * w, hwp = static_cast<int64_t>(hp) * wp;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 32;  // halo pixel index
+  const int32_t c0 = blockIdx.y * 32;
+  const uint8_t* xi = x + img * c * hw;
+  uint8_t* yi = y + img * hwp * c_store;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int32_t ch = c0 + r;
+    const int64_t p = p0 + threadIdx.x;
+    uint8_t v = fill;
+    if (ch < c && p < hwp) {
+      const int32_t iy = static_cast<int32_t>(p / wp) - pt;
+      const int32_t ix = static_cast<int32_t>(p % wp) - pl;
+      if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+        v = xi[static_cast<int64_t>(ch) * hw + static_cast<int64_t>(iy) * w + ix];
+      }
+    }
+    tile[r][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t p = p0 + r;
+    const int32_t ch = c0 + threadIdx.x;
+    if (p < hwp && ch < c_store) yi[p * c_store + ch] = tile[threadIdx.x][r];
+  }
+}
+
+// NHWC 8-bit [n, h, w, c_store] -> the same with a halo, [n, hp, wp, c_store]
+// (pixel (iy, ix) from (iy - pt, ix - pl), the fill byte outside the image).
+// One thread per output pixel x 16 channels, 16-byte loads and stores.
+__global__ void halo_nhwc_u8(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int32_t n,
+                             int32_t h, int32_t w, int32_t c_store, int32_t pt, int32_t pl,
+                             int32_t hp, int32_t wp, uint8_t fill) {
+  const int32_t groups = c_store >> 4;
+  const int64_t total = static_cast<int64_t>(n) * hp * wp * groups;
+  const uint32_t f4 = 0x01010101u * fill;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t g = static_cast<int32_t>(i % groups);
+    const int64_t pix = i / groups;
+    const int32_t ix = static_cast<int32_t>(pix % wp) - pl;
+    const int64_t t = pix / wp;
+    const int32_t iy = static_cast<int32_t>(t % hp) - pt;
+    const int64_t img = t / hp;
+    uint4 v = make_uint4(f4, f4, f4, f4);
+    if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+      v = __ldg(reinterpret_cast<const uint4*>(
+          x + ((img * h + iy) * w + ix) * c_store + g * 16));
+    }
+    *reinterpret_cast<uint4*>(y + pix * c_store + g * 16) = v;
+  }
+}
+
 // fp32 weights [m, c, kh, kw] -> bf16 [m][kh*kw][hi (ck) | lo (ck)].
 __global__ void pack_weights_bf16x2(const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                     int32_t m, int32_t c, int32_t taps, int32_t ck) {

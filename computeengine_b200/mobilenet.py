@@ -21,7 +21,7 @@ from __future__ import annotations
 import argparse
 import json
 from dataclasses import dataclass
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import numpy as np
 
@@ -225,10 +225,11 @@ def benchmark(batch: int = 64, iters: int = 50) -> dict:
             "algorithmic_gbs": by["all"] * batch / ms / 1e6, "launches": net.launches}
 
 
-def layer_times(batch: int = 64, iters: int = 20) -> List[dict]:
+def layer_times(batch: int = 64, iters: int = 20, only: Optional[str] = None) -> List[dict]:
     """Times every launch of the sweep on its own (CUDA events around each
     launch, averaged over `iters` passes); bytes are the algorithmic bytes of
-    that layer (input + output once)."""
+    that layer (input + output once).  `only` restricts it to one layer (its
+    input is still produced by running the sweep once)."""
     import torch
     layers = mobilenetv2_layers()
     net = MobileNetV2Q8(batch, make_params(layers))
@@ -239,6 +240,8 @@ def layer_times(batch: int = 64, iters: int = 20) -> List[dict]:
     torch.cuda.synchronize()
     out = []
     for l in layers:
+        if only is not None and l.name != only:
+            continue
         src = net.x_nhwc if l.src == "input" else net.acts[l.src]
         fn = L.lib.ie_cuda_dwconv2d_q8 if l.kind == "dw" else L.lib.ie_cuda_conv2d_q8
         args = (net.descs[l.name], net.qp[l.name], src.data_ptr(), net.packed[l.name].data_ptr(),
@@ -264,7 +267,12 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--layers", action="store_true", help="also time each launch on its own")
+    ap.add_argument("--only", help="time this one layer (e.g. b02_dw) and nothing else")
     a = ap.parse_args()
+    if a.only:
+        for r in layer_times(a.batch, a.iters, a.only):
+            print(json.dumps(r))
+        return
     print(json.dumps(benchmark(a.batch, a.iters)))
     if a.layers:
         for r in layer_times(a.batch):

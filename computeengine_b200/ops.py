@@ -334,21 +334,29 @@ class QLinearConv2DOp(Op):
         stream = _stream_handle()
         c_store = (d.c + 15) // 16 * 16
         m_store = (d.m + 15) // 16 * 16
-        xor = 0
+        xor, halo = 0, False
         if not depthwise:
             if d.group != 1:
                 return Status.error(Code.Unsupported, "grouped int8 convolution (1 < group < C)")
             if qp.zp_x != 0:
+                # uint8 with zero point 128 is int8 with zero point 0 after
+                # flipping the top bit; any other zero point reads a haloed
+                # input whose padding holds the zero point
                 if not x_signed and qp.zp_x == 128:
                     xor, qp.zp_x, qp.x_signed = 0x80, 0, 1
                 else:
-                    return Status.error(Code.Unsupported,
-                                        "dense int8 path takes zero point 0, or 128 for uint8")
+                    halo = True
         elif not (d.group == d.c == d.m and int(w.shape[1]) == 1):
             return Status.error(Code.Unsupported, "grouped int8 convolution (1 < group < C)")
-        x_nhwc = torch.empty((d.n, d.h, d.w, c_store), dtype=torch.uint8, device=dev)
-        rc = lib.ie_cuda_q8_pack_input(x.contiguous().data_ptr(), x_nhwc.data_ptr(), d.n, d.c,
-                                       d.h, d.w, c_store, xor, stream)
+        if halo:
+            x_nhwc = torch.empty(int(lib.ie_cuda_q8_halo_input_bytes(d)), dtype=torch.uint8,
+                                 device=dev)
+            rc = lib.ie_cuda_q8_pack_input_halo(d, x.contiguous().data_ptr(), x_nhwc.data_ptr(),
+                                                qp.zp_x, stream)
+        else:
+            x_nhwc = torch.empty((d.n, d.h, d.w, c_store), dtype=torch.uint8, device=dev)
+            rc = lib.ie_cuda_q8_pack_input(x.contiguous().data_ptr(), x_nhwc.data_ptr(), d.n,
+                                           d.c, d.h, d.w, c_store, xor, stream)
         if rc:
             return _from_abi(rc)
         y_nhwc = torch.empty((d.n, s.out_h, s.out_w, m_store), dtype=torch.uint8, device=dev)

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define IE_CUDA_CONV_ABI_VERSION 1
+#define IE_CUDA_CONV_ABI_VERSION 2
 
 typedef enum ie_status {
   IE_OK = 0,
@@ -82,7 +82,9 @@ typedef struct ie_conv2d_shape {
  * ReLU folds in as qmin = zp_y, ReLU6 as qmax = zp_y + round(6 / s_y). */
 typedef struct ie_q8_params {
   int32_t x_signed; /* activations stored as int8 (1) or uint8 (0) */
-  int32_t zp_x;     /* must be 0 for the NHWC kernels; see ie_cuda_q8_pack_input */
+  int32_t zp_x;     /* activation zero point, any value of the storage type;
+                       for the dense kernel a nonzero zp_x with padding needs
+                       the haloed input (ie_cuda_q8_pack_input_halo) */
   int32_t y_signed; /* output stored as int8 (1) or uint8 (0) */
   int32_t zp_y;
   int32_t qmin, qmax;
@@ -100,12 +102,16 @@ int ie_conv2d_resolve(const ie_conv2d_desc* desc, int64_t bias_len, ie_conv2d_sh
 
 /* ------------------------------------------------------------ int8 path */
 
-/* Bytes of the packed weight buffer for ie_cuda_q8_pack_weights. */
+/* Bytes of the packed weight buffer for ie_cuda_q8_pack_weights: the packed
+ * weights followed by int32 per-output-channel weight sums
+ * [round_up(m, 16)] (used to fold a nonzero activation zero point into the
+ * bias). */
 size_t ie_cuda_q8_packed_weight_bytes(const ie_conv2d_desc* desc);
 
 /* Repacks int8 weights [m, c/group, kh, kw] (device) into the K-major layout
  * the implicit-GEMM kernel reads: [m][kh][kw][c padded to the channel block],
- * zero filled.  Dense convolutions (group == 1) only. */
+ * zero filled, then writes the weight-sum trailer.  Dense convolutions
+ * (group == 1) only. */
 int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* packed,
                             void* stream);
 
@@ -116,15 +122,38 @@ int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* p
 int ie_cuda_q8_pack_input(const void* x_nchw, void* x_nhwc, int64_t n, int64_t c, int64_t h,
                           int64_t w, int64_t c_store, int32_t xor_mask, void* stream);
 
+/* Haloed input for a nonzero activation zero point.  The reference's padding
+ * is real 0.0, i.e. the stored value zp_x; TMA fills out-of-image reads with
+ * byte 0, so for zp_x != 0 the dense kernel instead reads an input grown by
+ * the convolution's resolved pads whose border holds zp_x:
+ *   [n, h + pad_top + pad_bottom, w + pad_left + pad_right, c_store]
+ * (c_store = c rounded up to 16; channels past c also hold zp_x).  The
+ * kernel adds -zp_x * sum(w[m]) to the bias (the packed weights' trailer), so
+ * every tap contributes (x - zp_x) * w exactly.  Unpadded convolutions need
+ * no halo: the plain NHWC tensor is its own haloed form.
+ *   ie_cuda_q8_halo_input_bytes   bytes of that buffer (0 on a bad desc)
+ *   ie_cuda_q8_pack_input_halo    NCHW 8-bit [n, c, h, w] -> haloed NHWC
+ *   ie_cuda_q8_halo_nhwc          NHWC [n, h, w, c_store] (e.g. the previous
+ *                                 layer's output) -> haloed NHWC
+ * zp_x is the stored byte's value (-128..127 for int8, 0..255 for uint8). */
+size_t ie_cuda_q8_halo_input_bytes(const ie_conv2d_desc* desc);
+int ie_cuda_q8_pack_input_halo(const ie_conv2d_desc* desc, const void* x_nchw, void* x_halo,
+                               int32_t zp_x, void* stream);
+int ie_cuda_q8_halo_nhwc(const ie_conv2d_desc* desc, const void* x_nhwc, void* x_halo,
+                         int32_t zp_x, void* stream);
+
 /* NHWC (c_store channels per pixel) -> NCHW for 8-bit activations. */
 int ie_cuda_q8_unpack_output(const void* y_nhwc, void* y_nchw, int64_t n, int64_t c,
                              int64_t h, int64_t w, int64_t c_store, void* stream);
 
 /* int8 convolution, dense (group == 1), NHWC in and out.
- *   x      [n, h, w, c_store] int8/uint8, c_store = c rounded up to 16
+ *   x      [n, h, w, c_store] int8/uint8, c_store = c rounded up to 16;
+ *          with q->zp_x != 0 and nonzero pads, the haloed input above
  *   packed ie_cuda_q8_pack_weights output
  *   bias   [m] int32 or NULL;  mult [m] fp32
- *   y      [n, out_h, out_w, m] (m a multiple of 16)
+ *   y      [n, out_h, out_w, m_store], m_store = m rounded up to 16: the
+ *          buffer's last dimension is m_store whatever m is (the channels
+ *          past m are written too and hold no data)
  * Tensor cores: tcgen05.mma kind::i8, TMA im2col loads, TMEM accumulators,
  * bias + requantize + clamp fused into the epilogue.  Replaces
  * conv2d_forward for quantized graphs. */
@@ -132,7 +161,8 @@ int ie_cuda_conv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const v
                       const void* packed, const int32_t* bias, const float* mult, void* y,
                       void* stream);
 
-/* Same, writing raw int32 (acc + bias) instead of requantized bytes. */
+/* Same, writing raw int32 (acc + bias) instead of requantized bytes, y
+ * [n, out_h, out_w, m_store] int32. */
 int ie_cuda_conv2d_q8_acc(const ie_conv2d_desc* desc, const ie_q8_params* q, const void* x,
                           const void* packed, const int32_t* bias, int32_t* y, void* stream);
 
@@ -160,7 +190,10 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
  *   ie_cuda_q8_stem_pack_weights [m, c, 7, 7] int8 -> packed weights of the
  *                                equivalent layer (ie_cuda_q8_packed_weight_bytes
  *                                of the equivalent descriptor)
- * The result equals the direct 7x7 / stride 2 convolution bit for bit. */
+ * The result equals the direct 7x7 / stride 2 convolution bit for bit.  The
+ * re-layout zero-fills its padding, so it takes activations with zero point 0
+ * (uint8 with zero point 128: xor_mask 0x80 and x_signed = 1); run other zero
+ * points as a plain 7x7 / stride 2 convolution on the haloed input. */
 int ie_cuda_q8_stem_desc(int64_t n, int64_t c, int64_t h, int64_t w, int64_t m,
                          ie_conv2d_desc* out);
 int ie_cuda_q8_stem_pack_input(const void* x_nchw, void* x_packed, int64_t n, int64_t c,
@@ -252,7 +285,9 @@ int ie_cuda_conv2d_f32_residual(const ie_conv2d_desc* desc, int32_t act, const f
  *     any device work.
  *   - The first call on a device looks up the scratch's device address with
  *     that device current (cudaGetSymbolAddress); make that first call before
- *     any stream capture on that device.
+ *     any stream capture on that device.  The address is cached per device
+ *     for the life of the process: do not call cudaDeviceReset (or otherwise
+ *     tear down the primary context) and keep using this entry point.
  *   - All calls share the one scratch array, which keeps the last call's
  *     contents; every byte a call reads is rewritten by its own packing
  *     kernels first, so nothing needs clearing.  Calls that overlap on the

@@ -36,8 +36,12 @@ def desc_for(L, n, c, h, w, m, kh, kw, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1,
 
 def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1),
                     zp_x=128, zp_y=0, qmin=0, qmax=255, raw_acc=False, device="cuda",
-                    y_signed=False):
-    """Runs ie_cuda_conv2d_q8 (or _acc) on NCHW host arrays, returns NCHW host output."""
+                    y_signed=False, force_halo=False):
+    """Runs ie_cuda_conv2d_q8 (or _acc) on NCHW host arrays, returns NCHW host output.
+
+    uint8 with zero point 128 goes through the XOR re-basing (int8, zero point
+    0); any other nonzero zero point (or force_halo) through the haloed input
+    whose padding holds the zero point."""
     import torch
     from computeengine_b200 import _lib as L
 
@@ -53,12 +57,19 @@ def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=
     x_nhwc = torch.zeros((n, h, w, c_store), dtype=torch.uint8, device=device)
     q = L.Q8Params()
     q.y_signed, q.zp_y, q.qmin, q.qmax = int(y_signed), zp_y, qmin, qmax
-    if x.dtype == np.uint8 and zp_x == 128:
+    if x.dtype == np.uint8 and zp_x == 128 and not force_halo:
         xor, q.x_signed, q.zp_x = 0x80, 1, 0
     else:
         xor, q.x_signed, q.zp_x = 0, int(x.dtype == np.int8), zp_x
-    L.check(L.lib.ie_cuda_q8_pack_input(x_dev.data_ptr(), x_nhwc.data_ptr(), n, c, h, w, c_store,
-                                        xor, stream))
+    if q.zp_x != 0:
+        hb = int(L.lib.ie_cuda_q8_halo_input_bytes(d))
+        assert hb > 0
+        x_nhwc = torch.full((hb,), 0x5A, dtype=torch.uint8, device=device)
+        L.check(L.lib.ie_cuda_q8_pack_input_halo(d, x_dev.data_ptr(), x_nhwc.data_ptr(), q.zp_x,
+                                                 stream))
+    else:
+        L.check(L.lib.ie_cuda_q8_pack_input(x_dev.data_ptr(), x_nhwc.data_ptr(), n, c, h, w,
+                                            c_store, xor, stream))
     w_dev = torch.from_numpy(np.ascontiguousarray(wq)).to(device)
     packed = torch.zeros(int(L.lib.ie_cuda_q8_packed_weight_bytes(d)), dtype=torch.uint8,
                          device=device)

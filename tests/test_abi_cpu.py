@@ -85,11 +85,16 @@ def test_bias_length_and_error_text():
 
 def test_packed_sizes():
     from computeengine_b200 import _lib as L
+    # packed weights, then the int32 per-channel weight sums (m rounded up to 16)
     d = _desc(c=64, m=128, h=28, w=28, pads=(1, 1, 1, 1))
-    assert L.lib.ie_cuda_q8_packed_weight_bytes(d) == 128 * 9 * 64
+    assert L.lib.ie_cuda_q8_packed_weight_bytes(d) == 128 * 9 * 64 + 4 * 128
+    assert L.lib.ie_cuda_q8_halo_input_bytes(d) == 1 * 30 * 30 * 64
     d = _desc(c=3, m=64, kh=7, kw=7)
-    assert L.lib.ie_cuda_q8_packed_weight_bytes(d) == 64 * 49 * 32
+    assert L.lib.ie_cuda_q8_packed_weight_bytes(d) == 64 * 49 * 32 + 4 * 64
     assert L.lib.ie_cuda_f32_packed_weight_bytes(d) == 64 * 49 * 2 * 16 * 2
+    d = _desc(c=24, m=40, h=9, w=7, kh=3, kw=3, stride=(2, 2), pads=(1, 0, 2, 1))
+    assert L.lib.ie_cuda_q8_packed_weight_bytes(d) == 40 * 9 * 32 + 4 * 48
+    assert L.lib.ie_cuda_q8_halo_input_bytes(d) == 12 * 8 * 32
     sd = L.ConvDesc()
     assert L.lib.ie_cuda_q8_stem_desc(8, 3, 224, 224, 64, sd) == 0
     assert (sd.c, sd.h, sd.kh, sd.kw, sd.pad_top, sd.pad_bottom) == (64, 112, 4, 1, 2, 1)

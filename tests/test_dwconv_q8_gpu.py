@@ -8,13 +8,14 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def run_dw_gpu(x, w, bias, mult, *, stride, pad, zp_x, zp_y, qmin, qmax, y_signed=False):
+def run_dw_gpu(x, w, bias, mult, *, stride, pad, zp_x, zp_y, qmin, qmax, y_signed=False,
+               pads=None):
     import torch
     from computeengine_b200 import _lib as L
     from tests.qconv import desc_for
     n, c, h, ww = x.shape
     k = w.shape[2]
-    d = desc_for(L, n, c, h, ww, c, k, k, (stride, stride), (pad,) * 4, (1, 1), c, 0, 1)
+    d = desc_for(L, n, c, h, ww, c, k, k, (stride, stride), pads or (pad,) * 4, (1, 1), c, 0, 1)
     s = L.ConvShape()
     L.check(L.lib.ie_conv2d_resolve(d, c, s))
     cs = (c + 15) // 16 * 16
@@ -131,3 +132,30 @@ def test_depthwise_wide_rows_5x5_stride2(oracle):
                             group=c, depthwise=True)
     np.testing.assert_array_equal(got, want)
     assert (want == 0).any() and (want == 120).any()
+
+
+@pytest.mark.parametrize("stride,pads,signed_in,zp_x", [
+    (1, (0, 1, 1, 0), False, 255),   # asymmetric pads, zero point at the top of uint8
+    (2, (1, 0, 0, 1), True, -128),   # stride 2, int8 input at its lowest zero point
+    (2, (0, 0, 0, 0), False, 0),     # no padding, ragged column groups
+    (1, (1, 1, 1, 1), True, 33),
+])
+def test_depthwise_3x3_row_kernel_edges(oracle, stride, pads, signed_in, zp_x):
+    """The 3x3 row kernel (4 channels x 4 columns x 4 rows per thread): image
+    sizes that leave partial column groups and row strips, asymmetric pads and
+    extreme zero points (padding reads as the zero point's byte)."""
+    rng = np.random.default_rng(400 + stride + zp_x)
+    n, c, h, w = 3, 40, 13, 18
+    if signed_in:
+        x = rng.integers(-128, 128, (n, c, h, w)).astype(np.int8)
+    else:
+        x = rng.integers(0, 256, (n, c, h, w)).astype(np.uint8)
+    wq = rng.integers(-127, 128, (c, 1, 3, 3)).astype(np.int8)
+    bias = rng.integers(-3000, 3000, c).astype(np.int32)
+    mult = rng.uniform(0.0008, 0.004, c).astype(np.float32)
+    got = run_dw_gpu(x, wq, bias, mult, stride=stride, pad=0, pads=pads, zp_x=zp_x, zp_y=4,
+                     qmin=4, qmax=200)
+    want = oracle.conv2d_q8(x, wq, bias, mult, zp_x, 4, 4, 200, strides=(stride, stride),
+                            pads=pads, group=c, depthwise=True)
+    np.testing.assert_array_equal(got, want)
+    assert (want == 4).any() and (want == 200).any()

@@ -62,6 +62,34 @@ def test_noalloc_matches_regular_entry_point_twice():
     assert L.take_device_error() == 0
 
 
+def test_noalloc_matches_oracle_and_runs_grouped(oracle):
+    """The regular entry point shares the pack and bf16x3 kernels with this
+    one, so also check the no-allocation result against the fp32 oracle, and
+    run a grouped convolution (CUDA-core path, which needs no scratch)."""
+    import torch
+    from computeengine_b200 import _lib as L
+    from tests.qconv import desc_for
+    rng = np.random.default_rng(17)
+    stream = torch.cuda.current_stream().cuda_stream
+    for (n, c, h, w, m, k, pad, group) in ((2, 32, 20, 18, 48, 3, 1, 1),
+                                           (1, 32, 15, 15, 64, 3, 1, 4)):
+        x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+        wt = rng.normal(0, 0.1, (m, c // group, k, k)).astype(np.float32)
+        b = rng.normal(0, 0.01, m).astype(np.float32)
+        d = desc_for(L, n, c, h, w, m, k, k, (1, 1), (pad,) * 4, (1, 1), group)
+        s = L.ConvShape()
+        L.check(L.lib.ie_conv2d_resolve(d, m, s))
+        xd, wd, bd = (torch.from_numpy(a).cuda() for a in (x, wt, b))
+        got = torch.full((n, m, s.out_h, s.out_w), float("nan"), device="cuda")
+        L.check(L.lib.ie_cuda_conv2d_f32_noalloc(d, L.IE_ACT_NONE, xd.data_ptr(), wd.data_ptr(),
+                                                 bd.data_ptr(), got.data_ptr(), stream))
+        torch.cuda.synchronize()
+        want = oracle.conv2d_f32(x, wt, b, pads=(pad,) * 4, group=group)
+        err = float(np.abs(got.cpu().numpy() - want).max())
+        assert err <= REL_TOL * float(np.abs(want).max()), (group, err)
+    assert L.take_device_error() == 0
+
+
 def test_noalloc_rejects_oversized_convolution():
     from computeengine_b200 import _lib as L
     d = _desc(L, 8, 64, 112, 112, 64, 3, 1)  # ~26 MB of packed activations
