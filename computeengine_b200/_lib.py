@@ -99,6 +99,7 @@ def _load() -> C.CDLL:
         "ie_cuda_conv2d_f32_noalloc": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p]),
         "ie_cuda_last_error": (C.c_char_p, []),
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
+        "ie_cuda_bounded_wait_probe": (C.c_int, [C.c_uint64, P(C.c_uint64), _p]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
         "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
         "ie_cuda_conv2d_f32_residual": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p, _p,

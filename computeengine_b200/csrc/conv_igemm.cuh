@@ -48,6 +48,7 @@ enum : unsigned int {
   kErrWaitWeights = 0x105,
   kErrWaitOutFull = 0x106,
   kErrWaitOutFree = 0x107,
+  kErrWaitProbe = 0x1FF,  // the bounded-wait self-test (bounded_wait_probe)
 };
 
 constexpr int kMaxStages = 12;
@@ -99,6 +100,8 @@ struct IgemmArgs {
   // viewed as a [pixels, channels] matrix, loaded with 2D tiled TMA (rows past
   // the last pixel read as zero) instead of im2col.
   int32_t a_tiled;
+  // every bounded wait gives up after this many nanoseconds (kWaitLimitNs)
+  uint64_t wait_limit_ns;
 };
 
 __host__ __device__ constexpr uint32_t swizzle_layout_code(int row_bytes) {
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
             const int32_t img = m_tile / args.tiles_img;
             const int32_t oy0 = (m_tile - img * args.tiles_img) * args.rows_t;
             for (int cb = 0; cb < args.cblocks; ++cb, ++kiter) {
-              if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, kErrWaitEmpty)) {
+              if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, kErrWaitEmpty, args.wait_limit_ns)) {
                 ok = false;
                 break;
               }
@@ -602,7 +605,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
         const int32_t co0 = n_tile * BN;
         int tap = 0, cb = 0, ky = 0, kx = 0;
         for (int k = 0; k < args.num_k; ++k, ++kiter) {
-          if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, kErrWaitEmpty)) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, kErrWaitEmpty, args.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -659,7 +662,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       uint32_t ph = 0;
       bool ok = true;
       if constexpr (B_RES) {
-        ok = mbar_wait(bres_bar, 0, abort_flag, kErrWaitWeights);
+        ok = mbar_wait(bres_bar, 0, abort_flag, kErrWaitWeights, args.wait_limit_ns);
       }
       const uint64_t stage_desc0 = make_smem_desc(smem_u32(stage_base), 16, kSbo, kLayout);
       const uint64_t bres_desc0 = make_smem_desc(smem_u32(b_res), 16, kSbo, kLayout);
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       for (int j = 0; ok && tile_of(j, &m_tile, &n_tile); ++j) {
         const int buf = j & 1;
         const uint32_t aph = (j >> 1) & 1;
-        if (!mbar_wait(&acce_bar[buf], aph ^ 1u, abort_flag, kErrWaitAccEmpty)) break;
+        if (!mbar_wait(&acce_bar[buf], aph ^ 1u, abort_flag, kErrWaitAccEmpty, args.wait_limit_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * P::kAccCols;
         if constexpr (KIND_I8 && B_RES) {
@@ -683,7 +686,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
             const int row_jump = args.dil_h * args.wp - args.kw * args.dil_w;
             const uint64_t tap_b_step = static_cast<uint64_t>(args.cblocks * kB) >> 4;
             for (int cb = 0; cb < args.cblocks; ++cb, ++kiter) {
-              if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull)) {
+              if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull, args.wait_limit_ns)) {
                 ok = false;
                 break;
               }
@@ -719,7 +722,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
           }
         }
         for (int k = 0; k < args.num_k; ++k, ++kiter) {
-          if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull)) {
+          if (!mbar_wait(&full_bar[s], ph, abort_flag, kErrWaitFull, args.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -758,7 +761,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       // tensor memory can be released safely even on the abort path.
       tc_commit(drain_bar);
       int dummy_abort = 0;
-      mbar_wait(drain_bar, 0, &dummy_abort, kErrWaitFull);
+      mbar_wait(drain_bar, 0, &dummy_abort, kErrWaitFull, args.wait_limit_ns);
     }
   } else if (warp == 2 + EPI_WARPS) {
     // ------------------------------------------------ output store warp
@@ -770,7 +773,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
       for (int j = 0; tile_of(j, &m_tile, &n_tile); ++j) {
         const int ob = args.out_bufs == 2 ? (j & 1) : 0;
         const uint32_t oph = args.out_bufs == 2 ? ((j >> 1) & 1) : (j & 1);
-        if (!mbar_wait(&ofull_bar[ob], oph, abort_flag, kErrWaitOutFull)) break;
+        if (!mbar_wait(&ofull_bar[ob], oph, abort_flag, kErrWaitOutFull, args.wait_limit_ns)) break;
         const uint8_t* s_tile = out_stage + ob * P::kOutTile;
         const int32_t row0 = m_tile * P::kRows;
         const int32_t img = halo ? m_tile / args.tiles_img : 0;
@@ -904,7 +907,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
         loaded_n_tile = n_tile;
         __syncwarp();
       }
-      if (!mbar_wait_warp(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull)) break;
+      if (!mbar_wait_warp(&accf_bar[buf], aph, abort_flag, kErrWaitAccFull, args.wait_limit_ns)) break;
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(m_tile) * P::kRows + sub * 128 + quarter * 32;
       const int64_t pixel = row0 + lane;
@@ -914,7 +917,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
         // the staged tile buffer is free once its previous store has read it
         const int ob = args.out_bufs == 2 ? (j & 1) : 0;
         const uint32_t oph = args.out_bufs == 2 ? ((j >> 1) & 1) : (j & 1);
-        if (!mbar_wait_warp(&ofree_bar[ob], oph ^ 1u, abort_flag, kErrWaitOutFree)) break;
+        if (!mbar_wait_warp(&ofree_bar[ob], oph ^ 1u, abort_flag, kErrWaitOutFree, args.wait_limit_ns)) break;
         uint8_t* s_tile = out_stage + ob * P::kOutTile;
         const int r0 = sub * 128 + quarter * 32;
         const uint32_t t_q = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -972,14 +975,53 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
     // wait for them (bounded) before the CTA exits.
     int dummy_abort = 0;
     for (uint32_t k = *kiter_consumed; k < *kiter_issued; ++k) {
-      mbar_wait(&full_bar[k % stages], (k / stages) & 1u, &dummy_abort, kErrWaitFull);
+      mbar_wait(&full_bar[k % stages], (k / stages) & 1u, &dummy_abort, kErrWaitFull, args.wait_limit_ns);
     }
-    if (B_RES) mbar_wait(bres_bar, 0, &dummy_abort, kErrWaitWeights);
+    if (B_RES) mbar_wait(bres_bar, 0, &dummy_abort, kErrWaitWeights, args.wait_limit_ns);
   }
   if (warp == 1) {
     tc_fence_after();
     __syncwarp();
     tmem_dealloc(tmem_base, P::kTmemCols);
+  }
+}
+
+// Self-test of the bounded-wait path: one CTA allocates tensor memory, then
+// thread 0 waits on an mbarrier that nothing ever arrives on.  The wait gives
+// up after limit_ns, records kErrWaitProbe in the device error word and
+// raises the CTA's abort flag; the CTA then frees its tensor memory and
+// returns, exactly as the convolution kernel winds down when one of its waits
+// runs out.  out[0] = 1 if the wait (wrongly) completed, 2 if it gave up,
+// out[1] = nanoseconds waited.
+__global__ void __launch_bounds__(64, 1) bounded_wait_probe(uint64_t limit_ns, uint64_t* out) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, kErrWaitProbe, limit_ns);
+    out[0] = ok ? 1 : 2;
+    out[1] = globaltimer_ns() - t0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    __syncwarp();
+    tmem_dealloc(tmem_slot, 32);
   }
 }
 

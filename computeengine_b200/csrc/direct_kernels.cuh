@@ -106,8 +106,12 @@ struct Dw3Args {
   int32_t zp_x;
   uint32_t zp4;              // zp_x's byte, replicated
   int32_t zp_y, qmin, qmax;
-  int32_t words, col_groups, row_strips;  // c_store / 4, ceil(out_w / 4), ceil(out_h / R)
+  int32_t words, col_groups;  // c_store / 4, ceil(out_w / 4)
+  int32_t chunk, chunks;       // output rows per thread, ceil(out_h / chunk)
 };
+
+// Blocks of 128 threads the 3x3 row kernel is compiled to fit per SM.
+constexpr int kDwMinBlocks = 3;
 
 template <bool kXSigned>
 __device__ __forceinline__ int32_t dp4a_xw(uint32_t x, uint32_t w, int32_t c) {
@@ -164,8 +168,8 @@ __device__ __forceinline__ void dw_row_windows(const uint32_t (&p)[3 * kStride +
   }
 }
 
-template <int kStride, int kChunk, bool kXSigned, bool kYSigned>
-__global__ void __launch_bounds__(128) dwconv3x3_q8_nhwc(const uint8_t* __restrict__ x,
+template <int kStride, bool kXSigned, bool kYSigned>
+__global__ void __launch_bounds__(128, kDwMinBlocks) dwconv3x3_q8_nhwc(const uint8_t* __restrict__ x,
                                                          const int8_t* __restrict__ wp,
                                                          const int32_t* __restrict__ bias,
                                                          const float* __restrict__ mult,
@@ -173,15 +177,15 @@ __global__ void __launch_bounds__(128) dwconv3x3_q8_nhwc(const uint8_t* __restri
   constexpr int kPix = 3 * kStride + 3;  // input pixels under 4 output columns
   constexpr int kNew = kStride;          // input rows each further output row adds
   // grid: x = (column group, channel word) with the word fastest, y = chunk
-  // of kChunk output rows, z = image; one 32-bit division splits x.
+  // of a.chunk output rows, z = image; one 32-bit division splits x.
   const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= static_cast<uint32_t>(a.col_groups * a.words)) return;
   const int32_t grp = static_cast<int32_t>(idx / static_cast<uint32_t>(a.words));
   const int32_t wd = static_cast<int32_t>(idx) - grp * a.words;
   const int32_t img = blockIdx.z;
   const int32_t c0 = wd * 4;
-  const int32_t ox0 = grp * 4, oy_begin = blockIdx.y * kChunk;
-  const int32_t oy_end = min(oy_begin + kChunk, a.out_h);
+  const int32_t ox0 = grp * 4, oy_begin = blockIdx.y * a.chunk;
+  const int32_t oy_end = min(oy_begin + a.chunk, a.out_h);
 
   // filter rows of the 4 channels: wk[ky][j] = [w(ky,0), w(ky,1), w(ky,2), 0]
   uint32_t wk[3][4];

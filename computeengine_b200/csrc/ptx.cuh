@@ -16,7 +16,7 @@ namespace ie_cuda {
 // The host reads and clears the word after a launch (ie_cuda_take_device_error).
 static __device__ unsigned int g_device_error;
 
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // default limit: 1 s per wait
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -66,17 +66,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed.  Returns false
-// if the CTA's abort flag is raised or the wait runs past kWaitLimitNs; in the
-// latter case it records `site` and raises the abort flag.
+// if the CTA's abort flag is raised or the wait runs past limit_ns (a launch
+// argument of the kernels, kWaitLimitNs by default); in the latter case it
+// records `site` and raises the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, unsigned int site) {
+                                          volatile int* abort_flag, unsigned int site,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         record_error(site);
         *abort_flag = 1;
         return false;
@@ -88,9 +90,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // Warp-uniform bounded wait: lane 0 waits, every lane gets the same answer,
 // so a timeout can never split a warp before a .sync.aligned instruction.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort_flag, unsigned int site) {
+                                               volatile int* abort_flag, unsigned int site,
+                                               uint64_t limit_ns = kWaitLimitNs) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, site) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, site, limit_ns) ? 1 : 0;
   return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 

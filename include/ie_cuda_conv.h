@@ -308,6 +308,17 @@ const char* ie_cuda_last_error(void);
  * its output is invalid).  Synchronizes the device. */
 int ie_cuda_take_device_error(uint32_t* code);
 
+/* Self-test of the failure detection of the kernels' bounded waits (no
+ * counterpart in the reference; its failure detection is host-side only).
+ * Launches one CTA that allocates tensor memory and waits on an mbarrier that
+ * nothing ever arrives on; the wait gives up after wait_limit_ns (1 us to
+ * 2 s), records code 0x1FF in the device error word (read it with
+ * ie_cuda_take_device_error), frees the tensor memory and returns, the same
+ * wind-down the convolution kernels take when one of their waits runs out.
+ * Synchronizes `stream`; *waited_ns (may be NULL) receives the time the wait
+ * took.  IE_OK when the wait gave up as designed. */
+int ie_cuda_bounded_wait_probe(uint64_t wait_limit_ns, uint64_t* waited_ns, void* stream);
+
 /* Number of kernel launches this library issued on the calling host thread
  * since the last reset (for the benchmark's launch count). */
 uint64_t ie_cuda_launch_count(int reset);
