@@ -512,7 +512,7 @@ def run_ours(args, world, rank, local):
     from computeengine_b200 import _lib as L
     from computeengine_b200.resnet import (ResNet50Q8, macs_per_image, make_input_u8,
                                            make_q8_params, resnet50_layers)
-    from computeengine_b200.shard import (bind_to_pci_local_cpus, broadcast_from_rank0,
+    from computeengine_b200.shard import (bind_to_pci_local_cpus, broadcast_from_rank0_checked,
                                           input_seed, max_over_ranks, shard_batch)
 
     dev = torch.device("cuda", local)
@@ -529,7 +529,9 @@ def run_ours(args, world, rank, local):
     params = make_q8_params(layers, seed=0)
     net = ResNet50Q8(b, params, device=dev)
     # weights, biases and multipliers go out once from rank 0 (NCCL over NVLink)
-    broadcast_bytes = broadcast_from_rank0(net.tensors())
+    ok, msg, broadcast_bytes = broadcast_from_rank0_checked(net.tensors())
+    if not ok:
+        raise SystemExit(f"rank {rank}: weight broadcast failed: {msg}")
     torch.cuda.synchronize(dev)
 
     first, count = shard_batch(b * world, world, rank)

@@ -323,6 +323,13 @@ ie::Status to_status(int rc) {
   }
 }
 
+namespace {
+int cuda_malloc_default(void** p, size_t bytes) { return static_cast<int>(cudaMalloc(p, bytes)); }
+DeviceAllocFn g_device_alloc = cuda_malloc_default;
+}  // namespace
+
+void set_device_alloc(DeviceAllocFn fn) { g_device_alloc = fn != nullptr ? fn : cuda_malloc_default; }
+
 DeviceBuffers::~DeviceBuffers() {
   for (auto& kv : scratch_) cudaFree(kv.second.ptr);
   for (auto& kv : cache_) cudaFree(kv.second.ptr);
@@ -334,7 +341,7 @@ ie::Result<void*> DeviceBuffers::scratch(int slot, size_t bytes) {
     if (b.ptr != nullptr) cudaFree(b.ptr);
     b = Block{};
     void* p = nullptr;
-    if (auto s = cuda_status(cudaMalloc(&p, bytes == 0 ? 256 : bytes), "cudaMalloc");
+    if (auto s = cuda_status(static_cast<cudaError_t>(g_device_alloc(&p, bytes == 0 ? 256 : bytes)), "cudaMalloc");
         !s.has_value()) {
       return s.error();
     }
@@ -352,7 +359,7 @@ ie::Result<void*> DeviceBuffers::cached(const void* host_key, size_t bytes, int 
     return it->second.ptr;
   }
   void* p = nullptr;
-  if (auto s = cuda_status(cudaMalloc(&p, bytes == 0 ? 256 : bytes), "cudaMalloc"); !s.has_value()) {
+  if (auto s = cuda_status(static_cast<cudaError_t>(g_device_alloc(&p, bytes == 0 ? 256 : bytes)), "cudaMalloc"); !s.has_value()) {
     return s.error();
   }
   cache_[k] = Block{p, bytes};
@@ -938,8 +945,11 @@ ie::Status CudaGemmOp::forward(const std::vector<ie::Tensor*>& inputs,
   return download_f32(*ydev, ie::Shape{{m, n}}, context, outputs, st);
 }
 
-ie::Status register_cuda_ops(ie::OpRegistry& registry) {
-  const std::pair<ie::OpType, ie::OpRegistry::Creator> ops[] = {
+namespace {
+
+template <class Registry>
+ie::Status register_into(Registry& registry) {
+  const std::pair<ie::OpType, std::function<std::unique_ptr<ie::Op>()>> ops[] = {
       {ie::OpType::Conv2D, [] { return std::make_unique<CudaConv2DOp>(false); }},
       {ie::OpType::DepthwiseConv2D, [] { return std::make_unique<CudaConv2DOp>(true); }},
       {ie::OpType::MaxPool2D, [] { return std::make_unique<CudaPool2DOp>(true); }},
@@ -951,6 +961,39 @@ ie::Status register_cuda_ops(ie::OpRegistry& registry) {
     if (auto st = registry.register_op(type, creator); !st.has_value()) return st;
   }
   return {};
+}
+
+}  // namespace
+
+ie::Status register_cuda_ops(ie::OpRegistry& registry) { return register_into(registry); }
+ie::Status register_cuda_ops(CudaOpTable& table) { return register_into(table); }
+
+ie::Status CudaOpTable::register_op(ie::OpType op, Creator creator) {
+  if (!creator) return ie::Error::invalid_argument("empty op creator");
+  std::lock_guard<std::mutex> lock(mutex_);
+  if (creators_.count(op) != 0) return ie::Error::already_exists("op already registered");
+  creators_.emplace(op, std::move(creator));
+  return {};
+}
+
+ie::Result<std::unique_ptr<ie::Op>> CudaOpTable::create(ie::OpType op) {
+  Creator creator;
+  {
+    std::lock_guard<std::mutex> lock(mutex_);
+    auto it = creators_.find(op);
+    if (it == creators_.end()) return ie::Error::not_found("no CUDA kernel for op");
+    creator = it->second;
+  }
+  auto instance = creator();
+  if (!instance) return ie::Error::runtime("op factory returned null");
+  return instance;
+}
+
+std::vector<ie::OpType> CudaOpTable::list() const {
+  std::lock_guard<std::mutex> lock(mutex_);
+  std::vector<ie::OpType> out;
+  for (const auto& kv : creators_) out.push_back(kv.first);
+  return out;
 }
 
 }  // namespace ie_b200

@@ -21,7 +21,9 @@
 
 #include <array>
 #include <cstdint>
+#include <functional>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -54,8 +56,20 @@ ie::Status parse_conv_config(const ie::Attrs& attrs, ConvConfig& config);
 // last error message.
 ie::Status to_status(int rc);
 
+// Device allocation every DeviceBuffers goes through: a cudaMalloc-shaped
+// function returning a cudaError_t value (cudaMalloc by default).  Tests swap
+// in a failing one to check that forward() reports OutOfMemory (the reference
+// convention for a failed allocation, error.h:14) and leaves the op usable;
+// pass nullptr to restore cudaMalloc.  Not thread-safe against concurrent
+// forward() calls: set it while no op runs.
+using DeviceAllocFn = int (*)(void** ptr, size_t bytes);
+void set_device_alloc(DeviceAllocFn fn);
+
 // Device memory owned by one op: weights uploaded (and packed) once per host
-// buffer, scratch buffers that only grow.
+// buffer, scratch buffers that only grow.  Weight inputs are keyed by their
+// host buffer and size: they must be constants that outlive the op and keep
+// their contents (graph weights are; a runtime value reusing one address with
+// new contents would be served the old packed copy).
 class DeviceBuffers {
  public:
   DeviceBuffers() = default;
@@ -197,5 +211,26 @@ class CudaGemmOp final : public ie::Op {
 // register_builtin_ops, which skips types already present
 // (op_registry.cpp:62-66).
 ie::Status register_cuda_ops(ie::OpRegistry& registry);
+
+// The CUDA backend's own op table, with the reference OpRegistry's
+// register_op / create semantics (op_registry.cpp:23-50: AlreadyExists for a
+// taken type, NotFound for an unknown one).  Inside the reference engine the
+// OpRegistry is a process singleton whose constructor is private and which
+// the CPU executor also reads (executor.h:21-24); the CUDA backend keeps its
+// ops in a table of its own so that registering them leaves what the CPU
+// backend runs unchanged.
+class CudaOpTable {
+ public:
+  using Creator = std::function<std::unique_ptr<ie::Op>()>;
+  ie::Status register_op(ie::OpType op, Creator creator);
+  ie::Result<std::unique_ptr<ie::Op>> create(ie::OpType op);
+  std::vector<ie::OpType> list() const;
+
+ private:
+  mutable std::mutex mutex_;
+  std::unordered_map<ie::OpType, Creator> creators_;
+};
+
+ie::Status register_cuda_ops(CudaOpTable& table);
 
 }  // namespace ie_b200

@@ -81,7 +81,7 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
         ops_.push_back(nullptr);
         continue;
       }
-      auto op = registry_.create(node.op);
+      auto op = create_(node.op);
       if (!op.has_value()) {
         return ie::Error::unsupported("no CUDA op for a node of this graph (run the fusion pass first)");
       }

@@ -15,11 +15,13 @@
 #pragma once
 
 #include <cstddef>
+#include <functional>
 #include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
 
+#include "cuda_conv_ops.h"
 #include "ie_op_iface.h"
 
 namespace ie_b200 {
@@ -35,14 +37,20 @@ class CudaDeviceAllocator final : public ie::Allocator {
 
 class CudaExecutor {
  public:
-  explicit CudaExecutor(ie::OpRegistry& registry) : registry_(registry) {}
+  using OpFactory = std::function<ie::Result<std::unique_ptr<ie::Op>>(ie::OpType)>;
+  // Ops from a registry with register_cuda_ops applied (the standalone build's
+  // registry, or the reference singleton) or from the CUDA backend's own table.
+  explicit CudaExecutor(ie::OpRegistry& registry)
+      : create_([&registry](ie::OpType t) { return registry.create(t); }) {}
+  explicit CudaExecutor(CudaOpTable& table)
+      : create_([&table](ie::OpType t) { return table.create(t); }) {}
   ie::Result<std::vector<ie::Tensor>> run(const ie::Graph& graph,
                                           const std::unordered_map<std::string, ie::Tensor>& inputs,
                                           std::shared_ptr<ie::Allocator> host_allocator,
                                           void* stream = nullptr);
 
  private:
-  ie::OpRegistry& registry_;
+  OpFactory create_;
   std::shared_ptr<CudaDeviceAllocator> device_alloc_ = std::make_shared<CudaDeviceAllocator>();
   const ie::Graph* graph_ = nullptr;
   std::vector<std::unique_ptr<ie::Op>> ops_;  // one per node of graph_

@@ -549,6 +549,29 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "f32_b", b.t);
     dump(dir, manifest, "f32_y", y);
   }
+  // a failed device allocation is reported as OutOfMemory, and the op works
+  // again once allocation succeeds
+  {
+    Lcg rng(9);
+    HostTensor x({1, 16, 10, 10}, ie::DType::F32), w({16, 16, 3, 3}, ie::DType::F32);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    for (int64_t i = 0; i < w.t.numel(); ++i) w.data<float>()[i] = rng.uniform(-0.1f, 0.1f);
+    auto op = reg.create(ie::OpType::Conv2D);
+    if (!op.has_value()) return 3;
+    (*op)->configure({{"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+    ie_b200::set_device_alloc([](void** p, size_t) -> int {
+      *p = nullptr;
+      return static_cast<int>(cudaErrorMemoryAllocation);
+    });
+    ie::Tensor y;
+    std::vector<ie::Tensor*> outs{&y};
+    ie::Status st = (*op)->forward({&x.t, &w.t}, outs, ctx);
+    expect(!st.has_value() && st.error().code == ie::Error::Code::OutOfMemory,
+           "failed device allocation -> OutOfMemory");
+    ie_b200::set_device_alloc(nullptr);
+    st = (*op)->forward({&x.t, &w.t}, outs, ctx);
+    expect(st.has_value() && y.buffer != nullptr, "forward after the allocator recovers");
+  }
   // fp32 DepthwiseConv2D, stride 2, SAME_UPPER
   {
     Lcg rng(2);

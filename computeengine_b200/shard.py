@@ -43,6 +43,19 @@ def broadcast_from_rank0(tensors: Iterable) -> int:
     return total
 
 
+def broadcast_from_rank0_checked(tensors: Iterable) -> Tuple[bool, str, int]:
+    """broadcast_from_rank0 with a failed peer turned into a status instead of
+    a hang or an exception: (ok, message, bytes sent).  A rank that dies or
+    exits before the broadcast makes the collective end with an error, either
+    at once (its connection closed) or at the process group's timeout; the
+    surviving ranks report that and can shut down cleanly.  Call
+    dist.destroy_process_group() afterwards either way."""
+    try:
+        return True, "", broadcast_from_rank0(tensors)
+    except Exception as e:  # the backends raise RuntimeError subclasses (DistBackendError, ...)
+        return False, f"{type(e).__name__}: {e}".strip(), 0
+
+
 def max_over_ranks(value: float, device=None) -> float:
     """Maximum of a per-rank scalar (e.g. elapsed milliseconds)."""
     import torch

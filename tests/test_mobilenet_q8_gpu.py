@@ -1,6 +1,7 @@
 """MobileNetV2-style int8 block sweep (expand 1x1 -> depthwise 3x3 ->
 project 1x1) on the B200 against the int8 oracle, layer by layer (each layer
-fed with the GPU's own input for it) and end to end.  Bit-exact."""
+fed with the GPU's own input for it) and end to end.  Bit-exact.  At batch 2,
+every image; at the workload's batch of 64, sampled images."""
 import numpy as np
 import pytest
 
@@ -41,3 +42,25 @@ def test_mobilenet_sweep_every_layer(oracle):
     np.testing.assert_array_equal(gpu[last], chain[last])
     # the sweep must not degenerate to constant outputs
     assert len(np.unique(gpu[last])) > 16
+
+
+def test_mobilenet_sweep_batch64_sampled_images(oracle):
+    import torch
+    from computeengine_b200.mobilenet import MobileNetV2Q8, make_input, make_params, mobilenetv2_layers
+    layers = mobilenetv2_layers()
+    params = make_params(layers)
+    x = make_input(64, seed=0)
+    net = MobileNetV2Q8(64, params)
+    net.run(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    assert net.L.take_device_error() == 0
+    idx = [0, 29, 63]
+    gpu = {l.name: _gpu_nchw(net.acts[l.name], l.cout, l.y_signed)[idx] for l in layers}
+    chain = {}
+    for l in layers:
+        src_gpu = x[idx] if l.src == "input" else gpu[l.src]
+        np.testing.assert_array_equal(gpu[l.name], _oracle_layer(oracle, l, params[l.name], src_gpu),
+                                      err_msg=l.name)
+        src_chain = x[idx] if l.src == "input" else chain[l.src]
+        chain[l.name] = _oracle_layer(oracle, l, params[l.name], src_chain)
+    np.testing.assert_array_equal(gpu[layers[-1].name], chain[layers[-1].name])

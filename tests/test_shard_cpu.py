@@ -54,6 +54,44 @@ def test_two_gloo_ranks_broadcast_and_max():
         assert m == 4.5
 
 
+def _failing_worker(rank, world, port, q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                           timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # this rank fails after joining, before the weight broadcast
+    from computeengine_b200.shard import broadcast_from_rank0_checked
+    import time
+    t0 = time.time()
+    ok, msg, sent = broadcast_from_rank0_checked([torch.ones(1 << 16)])
+    q.put((ok, msg, sent, time.time() - t0))
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def test_rank_failure_before_broadcast_returns_status():
+    """Rank 1 exits after joining the group; rank 0's weight broadcast ends
+    with an error status (peer gone or the group's 10 s timeout) instead of
+    hanging.  Host-side failure injection only: no GPU is involved."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29800 + os.getpid() % 150
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert procs[1].exitcode == 3
+    ok, msg, sent, dt = q.get(timeout=5)
+    assert not ok and sent == 0 and msg
+    assert dt < 60
+    assert procs[0].exitcode == 0
+
+
 def test_parse_cpulist():
     from computeengine_b200.shard import parse_cpulist
     assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
