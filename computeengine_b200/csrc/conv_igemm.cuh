@@ -550,6 +550,9 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The next layer's kernel may be scheduled now; it waits for this one to
+  // complete before it reads anything this one writes.
+  grid_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -568,6 +571,9 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
           }
         }
       }
+      // The weights above are constants; the activations may come from the
+      // kernel launched just before this one.
+      grid_dependency_wait();
       const int32_t hw_out = args.out_h * args.out_w;
       uint32_t kiter = 0;
       int s = 0;
@@ -799,6 +805,7 @@ __global__ void __launch_bounds__(96 + EPI_WARPS * 32, 1)
     }
   } else {
     // ------------------------------------------------ epilogue warps
+    grid_dependency_wait();  // a residual input may come from the previous kernel
     const int ew = warp - 2;       // 0 .. EPI_WARPS-1
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int idx = ew / 4;

@@ -163,8 +163,26 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
       attr_set[dev] = true;
     }
   }
-  // producer, MMA issuer, EPI epilogue warps, output store warp
-  kern<<<grid, 96 + EPI * 32, smem, st>>>(ta, tb, ty, args);
+  // producer, MMA issuer, EPI epilogue warps, output store warp.  Launched
+  // with programmatic stream serialization: the prologue (barriers, tensor
+  // memory, tensor-map prefetch, resident weights) overlaps the tail of the
+  // kernel before it, which the producer waits for (griddepcontrol.wait)
+  // before its first activation load.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(96 + EPI * 32);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, args);
+  if (le != cudaSuccess) {
+    ++g_launches;
+    return fail(IE_RUNTIME, "conv_igemm_kernel launch: %s", cudaGetErrorString(le));
+  }
   return check_launch("conv_igemm_kernel");
 }
 

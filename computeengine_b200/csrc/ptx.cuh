@@ -97,6 +97,22 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
   return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 
+// ------------------------------------------- programmatic dependent launch
+//
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still finishing.  grid_dependency_wait
+// blocks until that kernel has completed and its writes are visible; it must
+// precede every read of data the previous kernel may have written.
+// launch_dependents lets the next such kernel start its own prologue early.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
