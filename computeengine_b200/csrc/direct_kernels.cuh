@@ -206,14 +206,25 @@ __global__ void __launch_bounds__(128, kDwMinBlocks) dwconv3x3_q8_nhwc(const uin
   // and columns outside the image read as the zero point.
   const uint8_t* const xb = x + static_cast<int64_t>(img) * a.h * a.w * a.c_store + c0;
   const int32_t ix0 = ox0 * kStride - a.pad_l;
+  // byte offsets of the thread's input columns within a row (the same for
+  // every row), and which of them lie inside the image
+  int32_t col_off[kPix];
+  uint32_t col_in = 0;
+#pragma unroll
+  for (int q = 0; q < kPix; ++q) {
+    const int32_t ix = ix0 + q;
+    const bool in = ix >= 0 && ix < a.w;
+    col_off[q] = (in ? ix : 0) * a.c_store;
+    col_in |= in ? (1u << q) : 0u;
+  }
+  const int64_t row_bytes = static_cast<int64_t>(a.w) * a.c_store;
   auto load_row = [&](int32_t iy, uint32_t (&p)[kPix]) {
     const bool row_in = iy >= 0 && iy < a.h;
-    const uint8_t* const row = xb + static_cast<int64_t>(row_in ? iy : 0) * a.w * a.c_store;
+    const uint8_t* const row = xb + (row_in ? iy : 0) * row_bytes;
 #pragma unroll
     for (int q = 0; q < kPix; ++q) {
-      const int32_t ix = ix0 + q;
-      p[q] = (row_in && ix >= 0 && ix < a.w)
-                 ? __ldg(reinterpret_cast<const uint32_t*>(row + static_cast<int64_t>(ix) * a.c_store))
+      p[q] = (row_in && ((col_in >> q) & 1u))
+                 ? __ldg(reinterpret_cast<const uint32_t*>(row + col_off[q]))
                  : a.zp4;
     }
   };

@@ -816,7 +816,8 @@ int ie_cuda_dwconv2d_q8(const ie_conv2d_desc* desc, const ie_q8_params* q, const
   if (desc->kh == 3 && desc->kw == 3 && desc->dil_h == 1 && desc->dil_w == 1 &&
       desc->stride_h == desc->stride_w && (desc->stride_h == 1 || desc->stride_h == 2) &&
       zp_fits && desc->n <= 65535 && s.out_h <= 65535 && desc->h <= INT32_MAX &&
-      desc->w <= INT32_MAX && ceil_div(s.out_w, 4) * round_up(desc->c, 16) / 4 <= INT32_MAX) {
+      desc->w * round_up(desc->c, 16) <= INT32_MAX &&
+      ceil_div(s.out_w, 4) * round_up(desc->c, 16) / 4 <= INT32_MAX) {
     // 3x3, stride 1 or 2: the packed-byte (dp4a) row kernel
     Dw3Args a;
     a.n = static_cast<int32_t>(desc->n);
