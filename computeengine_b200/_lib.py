@@ -52,6 +52,12 @@ class Q8Params(C.Structure):
     _fields_ = [(n, _i32) for n in ("x_signed", "zp_x", "y_signed", "zp_y", "qmin", "qmax")]
 
 
+class QAddParams(C.Structure):
+    _fields_ = [("a_signed", _i32), ("zp_a", _i32), ("mult_a", C.c_float),
+                ("b_signed", _i32), ("zp_b", _i32), ("mult_b", C.c_float),
+                ("y_signed", _i32), ("zp_y", _i32), ("qmin", _i32), ("qmax", _i32)]
+
+
 class ConvPlan(C.Structure):
     _fields_ = [(n, _i32) for n in ("bn", "bk_bytes", "m_sub", "stages", "resident_weights",
                                     "out_bufs", "row_band", "grid", "a_tiled")]
@@ -100,6 +106,7 @@ def _load() -> C.CDLL:
         "ie_cuda_last_error": (C.c_char_p, []),
         "ie_cuda_take_device_error": (C.c_int, [P(C.c_uint32)]),
         "ie_cuda_bounded_wait_probe": (C.c_int, [C.c_uint64, P(C.c_uint64), _p]),
+        "ie_cuda_qadd": (C.c_int, [P(QAddParams), _p, _p, _p, _i64, _p]),
         "ie_cuda_launch_count": (C.c_uint64, [C.c_int]),
         "ie_cuda_last_plan": (C.c_int, [P(ConvPlan)]),
         "ie_cuda_conv2d_f32_residual": (C.c_int, [P(ConvDesc), _i32, _p, _p, _p, _p, _p, _p,

@@ -599,20 +599,28 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   q.zp_y = static_cast<int32_t>(zp_y_);
   q.qmin = has_qmin_ ? static_cast<int32_t>(qmin_) : (y_signed_ ? -128 : 0);
   q.qmax = has_qmax_ ? static_cast<int32_t>(qmax_) : (y_signed_ ? 127 : 255);
+  const bool dev_mode = device_mode(context);
+  // x in the int8 activation layout (a previous int8 node's device output)
+  const bool x_nhwc = x.layout == ie::Layout::NHWC;
+  if (x_nhwc && x.device != ie::Device::CUDA) {
+    return ie::Error::invalid_argument("an NHWC int8 activation must be a device tensor");
+  }
+  const bool padded = (s.pad_top | s.pad_left | s.pad_bottom | s.pad_right) != 0;
   uint32_t xor_mask = 0;
   bool halo = false;
   if (!depthwise) {
     if (d.group != 1) return ie::Error::unsupported("grouped int8 convolution (1 < group < C)");
     if (q.zp_x != 0) {
       // uint8 with zero point 128 is int8 with zero point 0 after flipping
-      // the top bit; any other zero point reads a haloed input whose padding
+      // the top bit (while packing NCHW input); any other zero point, and
+      // every zero point of an NHWC input, reads a haloed input whose padding
       // holds the zero point (the kernel folds -zp_x * sum(w) into the bias)
-      if (q.x_signed == 0 && q.zp_x == 128) {
+      if (!x_nhwc && q.x_signed == 0 && q.zp_x == 128) {
         xor_mask = 0x80;
         q.zp_x = 0;
         q.x_signed = 1;
       } else {
-        halo = true;
+        halo = padded;
       }
     }
   } else if (!(d.group == d.c && d.c == d.m && w.shape.dims[1] == 1)) {
@@ -621,15 +629,30 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   if (auto st = require_device(); !st.has_value()) return st;
 
   cudaStream_t st = static_cast<cudaStream_t>(context.stream);
-  auto xd = to_device(dev_, kSlotX, x, st);
-  if (!xd.has_value()) return xd.error();
   const int64_t c_store = (d.c + 15) / 16 * 16, m_store = (d.m + 15) / 16 * 16;
-  auto xn = dev_.scratch(kSlotXPacked, halo ? ie_cuda_q8_halo_input_bytes(&d)
-                                             : static_cast<size_t>(d.n * d.h * d.w * c_store));
-  if (!xn.has_value()) return xn.error();
-  const int prc = halo ? ie_cuda_q8_pack_input_halo(&d, *xd, *xn, q.zp_x, st)
-                       : ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st);
-  if (auto e = to_status(prc); !e.has_value()) return e;
+  const void* xin = nullptr;  // the kernel's input: NHWC, haloed when `halo`
+  if (x_nhwc) {
+    if (halo) {
+      auto xh = dev_.scratch(kSlotXPacked, ie_cuda_q8_halo_input_bytes(&d));
+      if (!xh.has_value()) return xh.error();
+      if (auto e = to_status(ie_cuda_q8_halo_nhwc(&d, x.buffer, *xh, q.zp_x, st)); !e.has_value()) {
+        return e;
+      }
+      xin = *xh;
+    } else {
+      xin = x.buffer;
+    }
+  } else {
+    auto xd = to_device(dev_, kSlotX, x, st);
+    if (!xd.has_value()) return xd.error();
+    auto xn = dev_.scratch(kSlotXPacked, halo ? ie_cuda_q8_halo_input_bytes(&d)
+                                               : static_cast<size_t>(d.n * d.h * d.w * c_store));
+    if (!xn.has_value()) return xn.error();
+    const int prc = halo ? ie_cuda_q8_pack_input_halo(&d, *xd, *xn, q.zp_x, st)
+                         : ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st);
+    if (auto e = to_status(prc); !e.has_value()) return e;
+    xin = *xn;
+  }
   // packed weights, bias and multipliers: uploaded once per host buffer
   bool fresh = false;
   const size_t wbytes = depthwise ? ie_cuda_dw_q8_packed_weight_bytes(&d)
@@ -676,21 +699,40 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     }
     bd = static_cast<const int32_t*>(*bp);
   }
-  auto yn = dev_.scratch(kSlotYPacked, static_cast<size_t>(d.n * s.out_h * s.out_w * m_store));
-  if (!yn.has_value()) return yn.error();
+  const ie::DType y_dtype = y_signed_ ? ie::DType::I8 : ie::DType::U8;
+  const ie::Shape y_shape{{d.n, d.m, s.out_h, s.out_w}};
+  std::optional<ie::Tensor> dev_out;  // device mode: written in the activation layout
+  void* yn = nullptr;
+  if (dev_mode) {
+    auto t = ie::Tensor::allocate(ie::Shape{{d.n, s.out_h, s.out_w, m_store}}, y_dtype,
+                                  context.allocator);
+    if (!t.has_value()) return t.error();
+    t->shape = y_shape;
+    t->layout = ie::Layout::NHWC;
+    t->device = ie::Device::CUDA;
+    yn = t->buffer;
+    dev_out = std::move(*t);
+  } else {
+    auto ys = dev_.scratch(kSlotYPacked, static_cast<size_t>(d.n * s.out_h * s.out_w * m_store));
+    if (!ys.has_value()) return ys.error();
+    yn = *ys;
+  }
   const int rc = depthwise
-                     ? ie_cuda_dwconv2d_q8(&d, &q, *xn, *wp, bd, static_cast<const float*>(*md), *yn, st)
-                     : ie_cuda_conv2d_q8(&d, &q, *xn, *wp, bd, static_cast<const float*>(*md), *yn, st);
+                     ? ie_cuda_dwconv2d_q8(&d, &q, xin, *wp, bd, static_cast<const float*>(*md), yn, st)
+                     : ie_cuda_conv2d_q8(&d, &q, xin, *wp, bd, static_cast<const float*>(*md), yn, st);
   if (auto e = to_status(rc); !e.has_value()) return e;
+  if (dev_out) {
+    *outputs[0] = std::move(*dev_out);
+    return {};
+  }
   const size_t y_bytes = static_cast<size_t>(d.n * d.m * s.out_h * s.out_w);
   auto yd = dev_.scratch(kSlotY, y_bytes);
   if (!yd.has_value()) return yd.error();
-  if (auto e = to_status(ie_cuda_q8_unpack_output(*yn, *yd, d.n, d.m, s.out_h, s.out_w, m_store, st));
+  if (auto e = to_status(ie_cuda_q8_unpack_output(yn, *yd, d.n, d.m, s.out_h, s.out_w, m_store, st));
       !e.has_value()) {
     return e;
   }
-  auto out = ie::Tensor::allocate(ie::Shape{{d.n, d.m, s.out_h, s.out_w}},
-                                  y_signed_ ? ie::DType::I8 : ie::DType::U8, context.allocator);
+  auto out = ie::Tensor::allocate(y_shape, y_dtype, context.allocator);
   if (!out.has_value()) return out.error();
   if (auto e = cuda_status(cudaMemcpyAsync(out->buffer, *yd, y_bytes, cudaMemcpyDeviceToHost, st),
                            "cudaMemcpyAsync D2H");
@@ -700,6 +742,141 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   if (auto e = finish(st); !e.has_value()) return e;
   *outputs[0] = std::move(*out);
   return {};
+}
+
+// ------------------------------------------------ int8 Add
+
+ie::Status CudaQLinearAddOp::configure(const ie::Attrs& attrs) {
+  bool found_a = false, found_b = false;
+  std::vector<double> ma, mb;
+  if (auto st = read_double_list(attrs, "a_multiplier", &found_a, &ma); !st.has_value()) return st;
+  if (auto st = read_double_list(attrs, "b_multiplier", &found_b, &mb); !st.has_value()) return st;
+  if (!found_a && !found_b) {
+    return ie::Error::unsupported(
+        "Add of fp32 tensors runs fused into a convolution (ConvBnReluFusionPass) on this backend");
+  }
+  if (!found_a || !found_b || ma.size() != 1 || mb.size() != 1 || !std::isfinite(ma[0]) ||
+      !std::isfinite(mb[0])) {
+    return ie::Error::invalid_argument("int8 Add needs one finite a_multiplier and b_multiplier");
+  }
+  q_ = ie_qadd_params{};
+  q_.mult_a = static_cast<float>(ma[0]);
+  q_.mult_b = static_cast<float>(mb[0]);
+  bool found = false;
+  int64_t v = 0;
+  if (auto st = read_int(attrs, "a_zero_point", &found, &v); !st.has_value()) return st;
+  q_.zp_a = found ? static_cast<int32_t>(v) : 0;
+  if (auto st = read_int(attrs, "b_zero_point", &found, &v); !st.has_value()) return st;
+  q_.zp_b = found ? static_cast<int32_t>(v) : 0;
+  if (auto st = read_int(attrs, "y_zero_point", &found, &v); !st.has_value()) return st;
+  q_.zp_y = found ? static_cast<int32_t>(v) : 0;
+  if (auto st = read_int(attrs, "y_signed", &found, &v); !st.has_value()) return st;
+  q_.y_signed = found && v != 0 ? 1 : 0;
+  if (auto st = read_int(attrs, "qmin", &has_qmin_, &qmin_); !st.has_value()) return st;
+  if (auto st = read_int(attrs, "qmax", &has_qmax_, &qmax_); !st.has_value()) return st;
+  return {};
+}
+
+ie::Status CudaQLinearAddOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                     std::vector<ie::Tensor*>& outputs,
+                                     ie::ExecutionContext& context) {
+  if (inputs.size() != 2 || outputs.size() != 1 || outputs[0] == nullptr) {
+    return ie::Error::invalid_argument("Add expects two inputs and one output");
+  }
+  if (context.allocator == nullptr) return ie::Error::invalid_argument("Add requires an allocator");
+  for (const ie::Tensor* t : inputs) {
+    if (t == nullptr || t->buffer == nullptr) return ie::Error::invalid_argument("null tensor or buffer");
+    if (t->dtype != ie::DType::U8 && t->dtype != ie::DType::I8) {
+      return ie::Error::unsupported("int8 Add takes U8/I8 tensors");
+    }
+  }
+  const ie::Tensor& a = *inputs[0];
+  const ie::Tensor& b = *inputs[1];
+  if (a.shape.dims != b.shape.dims) return ie::Error::invalid_argument("Add operands differ in shape");
+  ie_qadd_params q = q_;
+  q.a_signed = a.dtype == ie::DType::I8 ? 1 : 0;
+  q.b_signed = b.dtype == ie::DType::I8 ? 1 : 0;
+  q.qmin = has_qmin_ ? static_cast<int32_t>(qmin_) : (q.y_signed ? -128 : 0);
+  q.qmax = has_qmax_ ? static_cast<int32_t>(qmax_) : (q.y_signed ? 127 : 255);
+  const bool a_nhwc = a.layout == ie::Layout::NHWC, b_nhwc = b.layout == ie::Layout::NHWC;
+  const bool nhwc = a_nhwc || b_nhwc;
+  if ((a_nhwc && a.device != ie::Device::CUDA) || (b_nhwc && b.device != ie::Device::CUDA)) {
+    return ie::Error::invalid_argument("an NHWC int8 activation must be a device tensor");
+  }
+  if (nhwc && a.shape.dims.size() != 4) {
+    return ie::Error::invalid_argument("the int8 activation layout is 4-D");
+  }
+  if (auto st = require_device(); !st.has_value()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  // operands in one layout: an NCHW operand meets an NHWC one after packing
+  int64_t count = a.numel();
+  int64_t n = 0, c = 0, h = 0, w = 0, c_store = 0;
+  if (nhwc) {
+    n = a.shape.dims[0];
+    c = a.shape.dims[1];
+    h = a.shape.dims[2];
+    w = a.shape.dims[3];
+    c_store = (c + 15) / 16 * 16;
+    count = n * h * w * c_store;
+  }
+  auto operand = [&](const ie::Tensor& t, bool t_nhwc, int slot) -> ie::Result<const void*> {
+    if (t_nhwc || !nhwc) return to_device(dev_, slot, t, st);
+    auto td = to_device(dev_, slot, t, st);
+    if (!td.has_value()) return td.error();
+    auto packed = dev_.scratch(slot == kSlotX ? kSlotXPacked : kSlotWork, static_cast<size_t>(count));
+    if (!packed.has_value()) return packed.error();
+    if (auto e = to_status(ie_cuda_q8_pack_input(*td, *packed, n, c, h, w, c_store, 0, st));
+        !e.has_value()) {
+      return e.error();
+    }
+    return static_cast<const void*>(*packed);
+  };
+  auto ad = operand(a, a_nhwc, kSlotX);
+  if (!ad.has_value()) return ad.error();
+  auto bd = operand(b, b_nhwc, kSlotResidual);
+  if (!bd.has_value()) return bd.error();
+  const ie::DType y_dtype = q.y_signed ? ie::DType::I8 : ie::DType::U8;
+  if (device_mode(context)) {
+    auto t = nhwc ? ie::Tensor::allocate(ie::Shape{{n, h, w, c_store}}, y_dtype, context.allocator)
+                  : ie::Tensor::allocate(a.shape, y_dtype, context.allocator);
+    if (!t.has_value()) return t.error();
+    t->shape = a.shape;
+    t->layout = nhwc ? ie::Layout::NHWC : ie::Layout::ROW_MAJOR;
+    t->device = ie::Device::CUDA;
+    if (auto e = to_status(ie_cuda_qadd(&q, *ad, *bd, t->buffer, count, st)); !e.has_value()) return e;
+    *outputs[0] = std::move(*t);
+    return {};
+  }
+  auto yd = dev_.scratch(kSlotY, static_cast<size_t>(count));
+  if (!yd.has_value()) return yd.error();
+  if (auto e = to_status(ie_cuda_qadd(&q, *ad, *bd, *yd, count, st)); !e.has_value()) return e;
+  const void* ysrc = *yd;
+  if (nhwc) {  // host mode returns NCHW
+    auto yc = dev_.scratch(kSlotYPacked, static_cast<size_t>(a.numel()));
+    if (!yc.has_value()) return yc.error();
+    if (auto e = to_status(ie_cuda_q8_unpack_output(*yd, *yc, n, c, h, w, c_store, st)); !e.has_value()) {
+      return e;
+    }
+    ysrc = *yc;
+  }
+  return deliver(ysrc, a.shape, y_dtype, context, outputs, st);
+}
+
+// ------------------------------------------------ Conv2D node dispatch
+
+ie::Status CudaConvNodeOp::configure(const ie::Attrs& attrs) {
+  if (attrs.count("multiplier") != 0) {
+    impl_ = std::make_unique<CudaQLinearConv2DOp>();
+  } else {
+    impl_ = std::make_unique<CudaConv2DOp>(depthwise_);
+  }
+  return impl_->configure(attrs);
+}
+
+ie::Status CudaConvNodeOp::forward(const std::vector<ie::Tensor*>& inputs,
+                                   std::vector<ie::Tensor*>& outputs, ie::ExecutionContext& context) {
+  if (!impl_) return ie::Error::invalid_argument("Conv2D used before configure()");
+  return impl_->forward(inputs, outputs, context);
 }
 
 // ------------------------------------------------ pooling and Gemm
@@ -950,8 +1127,9 @@ namespace {
 template <class Registry>
 ie::Status register_into(Registry& registry) {
   const std::pair<ie::OpType, std::function<std::unique_ptr<ie::Op>()>> ops[] = {
-      {ie::OpType::Conv2D, [] { return std::make_unique<CudaConv2DOp>(false); }},
-      {ie::OpType::DepthwiseConv2D, [] { return std::make_unique<CudaConv2DOp>(true); }},
+      {ie::OpType::Conv2D, [] { return std::make_unique<CudaConvNodeOp>(false); }},
+      {ie::OpType::DepthwiseConv2D, [] { return std::make_unique<CudaConvNodeOp>(true); }},
+      {ie::OpType::Add, [] { return std::make_unique<CudaQLinearAddOp>(); }},
       {ie::OpType::MaxPool2D, [] { return std::make_unique<CudaPool2DOp>(true); }},
       {ie::OpType::AvgPool2D, [] { return std::make_unique<CudaPool2DOp>(false); }},
       {ie::OpType::GlobalAvgPool, [] { return std::make_unique<CudaGlobalAvgPoolOp>(); }},

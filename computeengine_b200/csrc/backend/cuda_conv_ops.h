@@ -127,6 +127,14 @@ class CudaConv2DOp final : public ie::Op {
 // "y_zero_point", "y_signed" and the output clamp "qmin" / "qmax" (ReLU /
 // ReLU6 folded in).  Output U8 or I8 NCHW, bit-exact with the int8 oracle:
 // y = clamp(round_half_away((acc + bias) * multiplier) + y_zero_point).
+//
+// Device mode (ExecutionContext::device == CUDA, as CudaExecutor runs it):
+// x is a device tensor, NCHW or this backend's int8 activation layout, and
+// the output is returned in that layout without synchronizing.  The layout:
+// Tensor::layout == Layout::NHWC, shape the logical [N, C, H, W], buffer
+// [N, H, W, round_up(C, 16)] bytes (the padding channels hold no data) --
+// what the implicit-GEMM kernel reads and writes, so a chain of int8 nodes
+// runs without a layout pass between them.
 class CudaQLinearConv2DOp final : public ie::Op {
  public:
   ie::Status configure(const ie::Attrs& attrs) override;
@@ -142,6 +150,45 @@ class CudaQLinearConv2DOp final : public ie::Op {
   bool has_qmin_ = false, has_qmax_ = false;
   int64_t qmin_ = 0, qmax_ = 0;
   DeviceBuffers dev_;
+};
+
+// int8 Add of two quantized tensors (the shortcut Add of a quantized ResNet
+// block), on OpType::Add nodes that carry the int8 attributes:
+// "a_zero_point", "b_zero_point", "a_multiplier" (s_a / s_y), "b_multiplier"
+// (s_b / s_y), "y_zero_point", "y_signed", "qmin" / "qmax" (a following ReLU
+// folds into qmin).  y = clamp(round_half_away((a - zp_a) * m_a +
+// (b - zp_b) * m_b) + zp_y), exact (ie_cuda_qadd).  Inputs of one logical
+// shape, NCHW or the int8 activation layout (device mode); the output takes
+// the activation layout when either input has it.  An Add node without the
+// int8 attributes is an fp32 Add, which this backend runs only fused into a
+// convolution (ConvBnReluFusionPass): configure() returns Unsupported.
+class CudaQLinearAddOp final : public ie::Op {
+ public:
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  ie_qadd_params q_{};
+  bool has_qmin_ = false, has_qmax_ = false;
+  int64_t qmin_ = 0, qmax_ = 0;
+  DeviceBuffers dev_;
+};
+
+// Conv2D / DepthwiseConv2D node of the CUDA backend: a quantized node (one
+// with a "multiplier" attribute, as the int8 converter emits) runs as
+// CudaQLinearConv2DOp, any other as CudaConv2DOp.  The reference IR has one
+// Conv2D op type for both.
+class CudaConvNodeOp final : public ie::Op {
+ public:
+  explicit CudaConvNodeOp(bool depthwise) : depthwise_(depthwise) {}
+  ie::Status configure(const ie::Attrs& attrs) override;
+  ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
+                     ie::ExecutionContext& context) override;
+
+ private:
+  bool depthwise_;
+  std::unique_ptr<ie::Op> impl_;
 };
 
 // Fields and defaults of the reference PoolConfig (pool_ops.h:13-21).

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <optional>
 #include <utility>
 
 #include "ie_cuda_conv.h"
@@ -154,14 +155,34 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
     if (!v.is_output) continue;
     auto it = values.find(v.id);
     if (it == values.end()) return ie::Error::invalid_argument("output value was not produced");
-    const ie::Tensor& t = it->second;
-    auto h = ie::Tensor::allocate(t.shape, t.dtype, host_allocator);
+    const ie::Tensor* t = &it->second;
+    // an int8 activation in the backend's NHWC layout goes back to NCHW first
+    std::optional<ie::Tensor> nchw;
+    if (t->layout == ie::Layout::NHWC && t->device == ie::Device::CUDA &&
+        (t->dtype == ie::DType::U8 || t->dtype == ie::DType::I8) && t->shape.dims.size() == 4) {
+      auto d = ie::Tensor::allocate(t->shape, t->dtype, device_alloc_);
+      if (!d.has_value()) return d.error();
+      d->device = ie::Device::CUDA;
+      const auto& dims = t->shape.dims;
+      const int rc = ie_cuda_q8_unpack_output(t->buffer, d->buffer, dims[0], dims[1], dims[2], dims[3],
+                                              (dims[1] + 15) / 16 * 16, stream);
+      if (rc != IE_OK) return ie::Error::runtime(std::string("unpack int8 output: ") + ie_cuda_last_error());
+      nchw = std::move(*d);
+      t = &*nchw;
+    }
+    auto h = ie::Tensor::allocate(t->shape, t->dtype, host_allocator);
     if (!h.has_value()) return h.error();
-    const cudaMemcpyKind kind = t.device == ie::Device::CUDA ? cudaMemcpyDeviceToHost
-                                                             : cudaMemcpyHostToHost;
-    if (auto s = cuda_check(cudaMemcpyAsync(h->buffer, t.buffer, t.bytes(), kind, st), "cudaMemcpyAsync D2H");
+    const cudaMemcpyKind kind = t->device == ie::Device::CUDA ? cudaMemcpyDeviceToHost
+                                                              : cudaMemcpyHostToHost;
+    if (auto s = cuda_check(cudaMemcpyAsync(h->buffer, t->buffer, t->bytes(), kind, st), "cudaMemcpyAsync D2H");
         !s.has_value()) {
       return s.error();
+    }
+    if (nchw) {
+      // the temporary must outlive the copy
+      if (auto s = cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize"); !s.has_value()) {
+        return s.error();
+      }
     }
     outputs.push_back(std::move(*h));
   }

@@ -231,6 +231,81 @@ std::unique_ptr<NetGraph> make_net_graph() {
   return ng;
 }
 
+// A quantized ResNet bottleneck as the int8 converter would emit it: Conv2D
+// nodes carrying the int8 attributes (1x1 -> 3x3 -> 1x1) and an Add node with
+// the int8 Add attributes for the shortcut (ReLU folded into its qmin).  The
+// input's zero point (37) and conv1's output zero point (10) are neither 0 nor
+// 128, so the 3x3 reads a haloed NHWC input and the Add packs the NCHW graph
+// input to meet conv3's NHWC output.
+struct QGraph {
+  ie::Graph g;
+  std::vector<std::unique_ptr<HostTensor>> keep;
+  std::vector<std::vector<double>> mult;
+  std::vector<std::vector<int64_t>> bias;
+};
+
+std::unique_ptr<QGraph> make_q8_block_graph(int64_t c = 32, int64_t mid = 16) {
+  auto qg = std::make_unique<QGraph>();
+  ie::Graph& g = qg->g;
+  Lcg rng(41);
+  ie::ValueId next = 0;
+  auto value = [&](const std::string& name, bool in = false, bool out = false) {
+    ie::Value v;
+    v.id = next++;
+    v.name = name;
+    v.is_input = in;
+    v.is_output = out;
+    g.values.push_back(v);
+    return v.id;
+  };
+  auto weight = [&](const std::string& name, std::vector<int64_t> dims) {
+    qg->keep.push_back(std::make_unique<HostTensor>(dims, ie::DType::I8));
+    HostTensor& t = *qg->keep.back();
+    for (int64_t i = 0; i < t.t.numel(); ++i) {
+      t.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+    }
+    g.weights.emplace(name, t.t);
+    return value(name);
+  };
+  auto qattrs = [&](int64_t m, double mlo, double mhi, int64_t zp_x, int64_t zp_y, int64_t qmin,
+                    int64_t pad) {
+    std::vector<double> mult(static_cast<size_t>(m));
+    std::vector<int64_t> bias(static_cast<size_t>(m));
+    for (int64_t i = 0; i < m; ++i) {
+      mult[static_cast<size_t>(i)] = static_cast<double>(static_cast<float>(mlo + (mhi - mlo) * rng.uniform(0.f, 1.f)));
+      bias[static_cast<size_t>(i)] = static_cast<int64_t>(rng.next() % 4001) - 2000;
+    }
+    qg->mult.push_back(mult);
+    qg->bias.push_back(bias);
+    return ie::Attrs{{"multiplier", mult}, {"bias", bias}, {"x_zero_point", zp_x},
+                     {"y_zero_point", zp_y}, {"qmin", qmin}, {"qmax", int64_t{255}},
+                     {"pads", std::vector<int64_t>{pad, pad, pad, pad}}};
+  };
+  auto node = [&](ie::OpType op, std::vector<ie::ValueId> in, ie::ValueId out, ie::Attrs attrs) {
+    ie::Node n;
+    n.id = static_cast<ie::NodeId>(g.nodes.size());
+    n.op = op;
+    n.inputs = std::move(in);
+    n.outputs = {out};
+    n.attrs = std::move(attrs);
+    g.nodes.push_back(n);
+  };
+  const ie::ValueId x = value("x", true);
+  const ie::ValueId w1 = weight("qw1", {mid, c, 1, 1});
+  const ie::ValueId w2 = weight("qw2", {mid, mid, 3, 3});
+  const ie::ValueId w3 = weight("qw3", {c, mid, 1, 1});
+  const ie::ValueId c1 = value("qc1"), c2 = value("qc2"), c3 = value("qc3");
+  const ie::ValueId y = value("qy", false, true);
+  node(ie::OpType::Conv2D, {x, w1}, c1, qattrs(mid, 0.004, 0.008, 37, 10, 10, 0));
+  node(ie::OpType::Conv2D, {c1, w2}, c2, qattrs(mid, 0.0015, 0.003, 10, 0, 0, 1));
+  node(ie::OpType::Conv2D, {c2, w3}, c3, qattrs(c, 0.004, 0.008, 0, 128, 0, 0));
+  node(ie::OpType::Add, {c3, x}, y,
+       {{"a_multiplier", std::vector<double>{0.5}}, {"b_multiplier", std::vector<double>{0.75}},
+        {"a_zero_point", int64_t{128}}, {"b_zero_point", int64_t{37}},
+        {"y_zero_point", int64_t{0}}, {"qmin", int64_t{0}}});
+  return qg;
+}
+
 // ------------------------------------------------------------ cpu checks
 
 int run_cpu() {
@@ -695,6 +770,41 @@ int run_gpu(const std::string& dir) {
     auto bad = exec2.run(raw->g, in, std::make_shared<ie::MallocAllocator>(), stream);
     expect(!bad.has_value() && bad.error().code == Error::Code::Unsupported,
            "EXEC: unfused graph is Unsupported");
+  }
+  // the int8 bottleneck, device-resident through the executor (int8 values
+  // stay in the NHWC activation layout between nodes)
+  {
+    auto qg = make_q8_block_graph();
+    HostTensor x({2, 32, 14, 14}, ie::DType::U8);
+    Lcg rng(43);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<uint8_t>()[i] = static_cast<uint8_t>(rng.next() % 256);
+    ie_b200::CudaExecutor exec(reg);
+    std::unordered_map<std::string, ie::Tensor> in{{"x", x.t}};
+    auto r1 = exec.run(qg->g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r1.has_value() && r1->size() == 1, "Q8EXEC: run");
+    if (!r1.has_value()) {
+      std::printf("  %s\n", r1.error().message.c_str());
+      return 4;
+    }
+    auto r2 = exec.run(qg->g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r2.has_value() && std::memcmp((*r1)[0].buffer, (*r2)[0].buffer, (*r1)[0].bytes()) == 0,
+           "Q8EXEC: second run identical");
+    expect((*r1)[0].shape.dims == std::vector<int64_t>{2, 32, 14, 14} &&
+               (*r1)[0].dtype == ie::DType::U8 && (*r1)[0].device == ie::Device::CPU,
+           "Q8EXEC: host NCHW uint8 output");
+    dump(dir, manifest, "q8g_x", x.t);
+    for (const char* k : {"qw1", "qw2", "qw3"}) dump(dir, manifest, (std::string("q8g_") + k).c_str(), qg->g.weights.at(k));
+    for (size_t l = 0; l < 3; ++l) {
+      const int64_t m = static_cast<int64_t>(qg->mult[l].size());
+      HostTensor mt({m}, ie::DType::F32), bt({m}, ie::DType::F32);
+      for (int64_t i = 0; i < m; ++i) {
+        mt.data<float>()[i] = static_cast<float>(qg->mult[l][static_cast<size_t>(i)]);
+        bt.data<float>()[i] = static_cast<float>(qg->bias[l][static_cast<size_t>(i)]);
+      }
+      dump(dir, manifest, ("q8g_mult" + std::to_string(l + 1)).c_str(), mt.t);
+      dump(dir, manifest, ("q8g_bias" + std::to_string(l + 1)).c_str(), bt.t);
+    }
+    dump(dir, manifest, "q8g_y", (*r1)[0]);
   }
   // conv + BN + shortcut add + Relu fused, run with a residual input
   {

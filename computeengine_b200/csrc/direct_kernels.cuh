@@ -363,6 +363,71 @@ __global__ void __launch_bounds__(128, kDwMinBlocks) dwconv3x3_q8_nhwc(const uin
   }
 }
 
+// ------------------------------------------------------------ int8 Add
+//
+// y = clamp(round_half_away((a - zp_a) * mult_a + (b - zp_b) * mult_b) + zp_y)
+// over two quantized tensors of one layout, exactly: each fp32 multiplier is
+// mant * 2^-shift, the two products are brought to the common shift s and
+// summed in 128-bit integers (the host rejects shifts more than 60 apart).
+struct QAddArgs {
+  int64_t count;
+  long long ma, mb;  // significands (0 for a vanishing term)
+  int32_t da, db;    // s - shift_a, s - shift_b (0..60)
+  int32_t s;         // common shift
+  int32_t zp_a, zp_b, zp_y, qmin, qmax;
+  int32_t a_signed, b_signed, y_signed;
+};
+
+__device__ __forceinline__ uint32_t qadd_one(uint32_t av, uint32_t bv, const QAddArgs& k) {
+  const int32_t a = k.a_signed ? static_cast<int32_t>(static_cast<int8_t>(av)) : static_cast<int32_t>(av);
+  const int32_t b = k.b_signed ? static_cast<int32_t>(static_cast<int8_t>(bv)) : static_cast<int32_t>(bv);
+  const __int128 v = (static_cast<__int128>(static_cast<long long>(a - k.zp_a) * k.ma) << k.da) +
+                     (static_cast<__int128>(static_cast<long long>(b - k.zp_b) * k.mb) << k.db);
+  long long r;
+  if (k.s >= 127) {
+    r = 0;
+  } else if (k.s <= 0) {
+    r = v == 0 ? 0 : (v > 0 ? (1ll << 40) : -(1ll << 40));
+  } else {
+    const __int128 half = static_cast<__int128>(1) << (k.s - 1);
+    r = static_cast<long long>((v + half - (v < 0 ? 1 : 0)) >> k.s);
+  }
+  long long q = r + k.zp_y;
+  q = q < k.qmin ? k.qmin : (q > k.qmax ? k.qmax : q);
+  return static_cast<uint32_t>(q) & 0xFFu;
+}
+
+// 16 elements per thread when vec16 (pointers 16-byte aligned, count a
+// multiple of 16), else one.
+__global__ void __launch_bounds__(256) qadd_u8(const uint8_t* __restrict__ a,
+                                               const uint8_t* __restrict__ b,
+                                               uint8_t* __restrict__ y, QAddArgs k, int vec16) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (vec16) {
+    for (int64_t t = t0; t < k.count / 16; t += stride) {
+      const uint4 va = __ldg(reinterpret_cast<const uint4*>(a) + t);
+      const uint4 vb = __ldg(reinterpret_cast<const uint4*>(b) + t);
+      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+      uint32_t wy[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t o = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          o |= qadd_one((wa[q] >> (8 * i)) & 0xFFu, (wb[q] >> (8 * i)) & 0xFFu, k) << (8 * i);
+        }
+        wy[q] = o;
+      }
+      reinterpret_cast<uint4*>(y)[t] = make_uint4(wy[0], wy[1], wy[2], wy[3]);
+    }
+  } else {
+    for (int64_t t = t0; t < k.count; t += stride) {
+      y[t] = static_cast<uint8_t>(qadd_one(__ldg(a + t), __ldg(b + t), k));
+    }
+  }
+}
+
 // depthwise int8 weights [c, 1, kh, kw] -> [kh*kw][c_store], zero filled.
 __global__ void pack_dw_weights_q8(const int8_t* __restrict__ w, int8_t* __restrict__ out,
                                    int32_t c, int32_t taps, int32_t c_store) {

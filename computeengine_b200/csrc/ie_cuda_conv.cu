@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -1353,6 +1354,70 @@ int ie_cuda_conv2d_f32_residual(const ie_conv2d_desc* desc, int32_t act, const f
   if ((rc = ie_cuda_f32_pack_weights(desc, w, packed, stream)) != IE_OK) return rc;
   return ie_cuda_conv2d_bf16x3_residual(desc, act, x_split, packed, bias, residual, y,
                                         IE_Y_F32_NCHW, stream);
+}
+
+int ie_cuda_qadd(const ie_qadd_params* p, const void* a, const void* b, void* y, int64_t count,
+                 void* stream) {
+  if (p == nullptr) return fail(IE_INVALID_ARGUMENT, "null parameters");
+  if (count < 0) return fail(IE_INVALID_ARGUMENT, "negative element count");
+  if (count == 0) return IE_OK;
+  if (a == nullptr || b == nullptr || y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  auto in_type = [](int32_t sgn, int32_t v) { return sgn ? (v >= -128 && v <= 127) : (v >= 0 && v <= 255); };
+  if (!in_type(p->a_signed, p->zp_a) || !in_type(p->b_signed, p->zp_b)) {
+    return fail(IE_INVALID_ARGUMENT, "input zero point outside its storage type");
+  }
+  const int32_t lo = p->y_signed ? -128 : 0, hi = p->y_signed ? 127 : 255;
+  if (p->qmin < lo || p->qmax > hi || p->qmin > p->qmax || !in_type(p->y_signed, p->zp_y)) {
+    return fail(IE_INVALID_ARGUMENT, "output clamp range outside the storage type");
+  }
+  if (!std::isfinite(p->mult_a) || !std::isfinite(p->mult_b)) {
+    return fail(IE_INVALID_ARGUMENT, "multipliers must be finite");
+  }
+  // host split of the fp32 multipliers (the same rule as split_multiplier)
+  auto split = [](float m, long long* mant, int* shift) {
+    if (m == 0.0f) {
+      *mant = 0;
+      *shift = 32;
+      return;
+    }
+    int e = 0;
+    const double f = std::frexp(static_cast<double>(m), &e);
+    *mant = static_cast<long long>(std::ldexp(f, 31));
+    *shift = 31 - e;
+  };
+  long long ma, mb;
+  int sa, sb;
+  split(p->mult_a, &ma, &sa);
+  split(p->mult_b, &mb, &sb);
+  if (ma == 0) sa = sb;
+  if (mb == 0) sb = sa;
+  const int sh = std::max(sa, sb);
+  if (sh - std::min(sa, sb) > 60) {
+    return fail(IE_UNSUPPORTED, "multipliers more than 2^60 apart");
+  }
+  QAddArgs k;
+  k.count = count;
+  k.ma = ma;
+  k.mb = mb;
+  k.da = sh - sa;
+  k.db = sh - sb;
+  k.s = sh;
+  k.zp_a = p->zp_a;
+  k.zp_b = p->zp_b;
+  k.zp_y = p->zp_y;
+  k.qmin = p->qmin;
+  k.qmax = p->qmax;
+  k.a_signed = p->a_signed;
+  k.b_signed = p->b_signed;
+  k.y_signed = p->y_signed;
+  const bool vec = count % 16 == 0 && reinterpret_cast<uintptr_t>(a) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(b) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  const int64_t work = vec ? count / 16 : count;
+  const int blocks = static_cast<int>(std::min<int64_t>(ceil_div(work, 256), int64_t{num_sms()} * 16));
+  qadd_u8<<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const uint8_t*>(a),
+                                                 static_cast<const uint8_t*>(b),
+                                                 static_cast<uint8_t*>(y), k, vec ? 1 : 0);
+  return check_launch("qadd_u8");
 }
 
 int ie_cuda_bounded_wait_probe(uint64_t wait_limit_ns, uint64_t* waited_ns, void* stream) {

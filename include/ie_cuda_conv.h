@@ -216,6 +216,24 @@ int ie_cuda_f32x2_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_
                             int64_t c_store, int64_t k, int64_t stride, int64_t pad,
                             void* stream);
 
+/* int8 Add of two quantized tensors of one layout and size (the shortcut Add
+ * of a quantized ResNet block; the reference has no int8 Add, the rule is this
+ * backend's, exact like the convolution's requantize):
+ *   v  = (a - zp_a) * mult_a + (b - zp_b) * mult_b   (mult = s_in / s_y, fp32;
+ *        both are dyadic rationals, summed exactly in 128-bit integers)
+ *   yq = clamp(round_half_away(v) + zp_y, qmin, qmax)
+ * count = elements (bytes) of each tensor.  IE_UNSUPPORTED when the two
+ * nonzero multipliers differ by more than 2^60. */
+typedef struct ie_qadd_params {
+  int32_t a_signed, zp_a;
+  float mult_a;
+  int32_t b_signed, zp_b;
+  float mult_b;
+  int32_t y_signed, zp_y, qmin, qmax;
+} ie_qadd_params;
+int ie_cuda_qadd(const ie_qadd_params* p, const void* a, const void* b, void* y, int64_t count,
+                 void* stream);
+
 /* ------------------------------------------------------------ fp32 path */
 
 /* Output formats of ie_cuda_conv2d_bf16x3. */

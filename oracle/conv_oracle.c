@@ -370,3 +370,43 @@ int orc_conv2d_q8(const orc_conv_geom* g, const void* x, int x_signed,
                            (size_t)(g->out_h * g->out_w) * sizeof(int16_t);
     return orc_for_images(g->n, nthreads, scratch, orc_q8_image, &ctx);
 }
+
+int orc_qadd(const void* a, int a_signed, int32_t zp_a, float mult_a, const void* b,
+             int b_signed, int32_t zp_b, float mult_b, int32_t zp_y, int32_t qmin,
+             int32_t qmax, int y_signed, void* y, int64_t count) {
+    if (count < 0 || (count > 0 && (a == NULL || b == NULL || y == NULL))) {
+        return ORC_INVALID_ARGUMENT;
+    }
+    int64_t ma, mb;
+    int sa, sb;
+    orc_split_multiplier(mult_a, &ma, &sa);
+    orc_split_multiplier(mult_b, &mb, &sb);
+    if (ma == 0) sa = sb;  /* a vanishing term puts no constraint on the shift */
+    if (mb == 0) sb = sa;
+    const int s = sa > sb ? sa : sb;
+    if (s - (sa < sb ? sa : sb) > 60) return ORC_UNSUPPORTED;
+    for (int64_t i = 0; i < count; ++i) {
+        const int32_t av = a_signed ? ((const int8_t*)a)[i] : ((const uint8_t*)a)[i];
+        const int32_t bv = b_signed ? ((const int8_t*)b)[i] : ((const uint8_t*)b)[i];
+        const __int128 v = ((__int128)(av - zp_a) * ma) * ((__int128)1 << (s - sa)) +
+                           ((__int128)(bv - zp_b) * mb) * ((__int128)1 << (s - sb));
+        int64_t r;
+        if (s >= 127) {
+            r = 0;                                   /* |v| < 2^103 <= 2^(s-1) */
+        } else if (s <= 0) {
+            r = v == 0 ? 0 : (v > 0 ? INT64_C(1) << 40 : -(INT64_C(1) << 40));
+        } else {
+            const __int128 half = (__int128)1 << (s - 1);
+            r = (int64_t)((v + half - (v < 0 ? 1 : 0)) >> s);
+        }
+        int64_t q = r + zp_y;
+        if (q < qmin) q = qmin;
+        if (q > qmax) q = qmax;
+        if (y_signed) {
+            ((int8_t*)y)[i] = (int8_t)q;
+        } else {
+            ((uint8_t*)y)[i] = (uint8_t)q;
+        }
+    }
+    return ORC_OK;
+}

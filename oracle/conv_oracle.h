@@ -98,6 +98,20 @@ int orc_conv2d_q8(const orc_conv_geom* g, const void* x, int x_signed,
 int32_t orc_requantize(int32_t acc, int32_t bias, float mult, int32_t zp_y,
                        int32_t qmin, int32_t qmax);
 
+/* int8 addition of two quantized tensors of the same shape (the shortcut Add
+ * of a quantized ResNet block; the reference has no int8 Add, so the rule is
+ * this project's, in the style of the requantize above):
+ *   v  = (a - zp_a) * mult_a + (b - zp_b) * mult_b   exact: both fp32
+ *        multipliers are dyadic rationals mant * 2^-shift, summed over the
+ *        common shift in 128-bit integers
+ *   yq = clamp(round_half_away_from_zero(v) + zp_y, qmin, qmax)
+ * mult_a = s_a / s_y and mult_b = s_b / s_y, each rounded once to fp32.
+ * ORC_UNSUPPORTED when the two nonzero multipliers' shifts differ by more
+ * than 60 (one term below 2^-60 of the other). */
+int orc_qadd(const void* a, int a_signed, int32_t zp_a, float mult_a, const void* b,
+             int b_signed, int32_t zp_b, float mult_b, int32_t zp_y, int32_t qmin,
+             int32_t qmax, int y_signed, void* y, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

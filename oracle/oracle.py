@@ -136,6 +136,22 @@ class Oracle:
     def requantize(self, acc, bias, mult, zp_y, qmin, qmax):
         return self.lib.orc_requantize(acc, bias, mult, zp_y, qmin, qmax)
 
+    def qadd(self, a, zp_a, mult_a, b, zp_b, mult_b, zp_y, qmin, qmax, y_signed=False):
+        """int8 Add of two quantized tensors of one shape (orc_qadd)."""
+        assert a.shape == b.shape and a.dtype in (np.uint8, np.int8) and b.dtype in (np.uint8, np.int8)
+        a = np.ascontiguousarray(a)
+        b = np.ascontiguousarray(b)
+        y = np.empty(a.shape, np.int8 if y_signed else np.uint8)
+        f = self.lib.orc_qadd
+        f.restype = C.c_int
+        f.argtypes = [_p, C.c_int, C.c_int32, C.c_float, _p, C.c_int, C.c_int32, C.c_float,
+                      C.c_int32, C.c_int32, C.c_int32, C.c_int, _p, _i64]
+        rc = f(_ptr(a), int(a.dtype == np.int8), zp_a, mult_a, _ptr(b), int(b.dtype == np.int8),
+               zp_b, mult_b, zp_y, qmin, qmax, int(y_signed), _ptr(y), a.size)
+        if rc != OK:
+            raise OracleError(rc)
+        return y
+
 
 class RefConv:
     """The reference Conv2DOp / DepthwiseConv2DOp, compiled from its sources."""

@@ -56,6 +56,25 @@ def test_cpp_ops_match_oracle(oracle, tmp_path):
     assert err.mean() <= 0.005 * scale, (err.mean(), scale)
 
 
+def test_cpp_q8_block_graph_device_resident(oracle, tmp_path):
+    """A quantized ResNet bottleneck graph (int8 Conv2D nodes 1x1 -> 3x3 ->
+    1x1 and an int8 shortcut Add with ReLU) run by CudaExecutor with every
+    int8 value in device memory, bit-exact with the oracle chain (the input's
+    and conv1's zero points are neither 0 nor 128)."""
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    x = t["q8g_x"]
+    p = [(t[f"q8g_qw{i}"], t[f"q8g_bias{i}"].astype(np.int32), t[f"q8g_mult{i}"]) for i in (1, 2, 3)]
+    c1 = oracle.conv2d_q8(x, *p[0], 37, 10, 10, 255)
+    c2 = oracle.conv2d_q8(c1, *p[1], 10, 0, 0, 255, pads=(1, 1, 1, 1))
+    c3 = oracle.conv2d_q8(c2, *p[2], 0, 128, 0, 255)
+    want = oracle.qadd(c3, 128, np.float32(0.5), x, 37, np.float32(0.75), 0, 0, 255)
+    np.testing.assert_array_equal(t["q8g_y"], want)
+    assert (want == 0).mean() < 0.9 and len(np.unique(want)) > 32
+
+
 def test_cpp_head_ops_match_reference(refconv, tmp_path):
     """MaxPool2D, AvgPool2D (ceil_mode, count_include_pad), GlobalAvgPool and
     Gemm (transB, bias) through the registry against the reference's own ops:

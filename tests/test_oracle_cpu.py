@@ -165,3 +165,29 @@ def test_requantize_edges(oracle):
         for acc, b, m in cases:
             assert oracle.requantize(acc, b, m, zp, lo, hi) == _requant_exact(acc, b, m, zp, lo, hi), \
                 (acc, b, m, zp, lo, hi)
+
+
+def test_qadd_matches_fraction_restatement(oracle):
+    """The int8 Add rule (round half away from zero of the exact sum of the two
+    rescaled operands, then zero point and clamp), checked on random values and
+    on multipliers that make exact .5 ties of either sign."""
+    import math
+    from fractions import Fraction as F
+    rng = np.random.default_rng(7)
+
+    def rha(v):
+        return int(math.floor(abs(v) + F(1, 2))) * (1 if v >= 0 else -1)
+
+    for (ma, mb, zp_a, zp_b, zp_y, lo, hi, a_s, b_s, y_s) in [
+            (0.37, 0.0213, 31, -5, 7, 0, 255, False, True, False),
+            (0.5, 0.25, 128, 0, 0, 0, 255, False, False, False),      # ties
+            (0.5, 1.5, -3, 9, -4, -128, 127, True, True, True),      # ties, signed output
+            (2.0 ** -40, 3.0, 0, 1, 0, 0, 255, False, False, False),  # shifts 42 apart
+            (0.0, 0.8, 5, 6, 1, 0, 200, False, False, False)]:        # a vanishing term
+        a = rng.integers(-128, 128, 700).astype(np.int8) if a_s else rng.integers(0, 256, 700).astype(np.uint8)
+        b = rng.integers(-128, 128, 700).astype(np.int8) if b_s else rng.integers(0, 256, 700).astype(np.uint8)
+        y = oracle.qadd(a, zp_a, np.float32(ma), b, zp_b, np.float32(mb), zp_y, lo, hi, y_signed=y_s)
+        want = [min(max(rha((int(av) - zp_a) * F(float(np.float32(ma))) +
+                            (int(bv) - zp_b) * F(float(np.float32(mb)))) + zp_y, lo), hi)
+                for av, bv in zip(a, b)]
+        np.testing.assert_array_equal(y.astype(np.int64), np.array(want, np.int64))
