@@ -482,12 +482,16 @@ def gpu_workloads(peaks: dict) -> dict:
     return {
         "1": {"workload": r1["workload"], "value": r1["gflops"] / 1e3, "unit": "TFLOP/s",
               "us_per_call": r1["us"], "dtype": "f32 (bf16x3)",
+              "e2e": {"value": 2 * 64 * 64 * 9 * 56 * 56 / r1["e2e_us"] / 1e6, "unit": "TFLOP/s",
+                      "us_per_call": r1["e2e_us"], "how": r1["e2e"]},
               "roofline": {"bound": "latency (0.23 GFLOP, three launches)",
                            "frac": r1["frac_of_bf16_peak_over_3"],
                            "denominator": f"bf16 burst / 3 = {bf16 / 3:.0f} TFLOP/s ({src})"}},
         "2": {"workload": r2["workload"], "value": r2["kernel_tops"], "unit": "TOPS",
               "kernel_us": r2["kernel_us"], "drop_in_us": r2["drop_in_us"],
               "drop_in_tops": r2["drop_in_tops"], "dtype": "int8",
+              "e2e": {"value": 2 * 8 * 128 * 128 * 9 * 28 * 28 / r2["e2e_us"] / 1e6, "unit": "TOPS",
+                      "us_per_call": r2["e2e_us"], "how": r2["e2e"]},
               "roofline": {"bound": "tensor", "frac": r2["frac_of_2x_bf16_peak"],
                            "denominator": f"2 x bf16 burst = {2 * bf16:.0f} TOPS ({src})"}},
         "3": {"workload": f3["workload"], "value": f3["tflops"], "unit": "TFLOP/s",
@@ -668,10 +672,12 @@ def run_ours(args, world, rank, local):
     achieved = conv_ops * 2 / (conv_ms / 1e3) / 1e12  # TOPS over the conv launches
     step_ms = ms_max / args.steps
     traffic = None
+    traffic_note = None
     if PROFILE_JSON.exists():
         prof = json.loads(PROFILE_JSON.read_text())
-        if prof.get("batch") == b:
+        if prof.get("scale_to_batch", prof.get("batch")) == b:
             traffic = prof.get("dram_bytes_per_launch")
+            traffic_note = prof.get("note")
     line = {
         "metric": "int8 conv TOPS (ResNet-50 conv stack, 53 convs)",
         "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
@@ -699,7 +705,7 @@ def run_ours(args, world, rank, local):
         "roofline": {"bound": "tensor", "kernel": "conv_igemm_kernel (int8, all 53 layers)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src,
-                     "traffic": traffic,
+                     "traffic": traffic, "traffic_note": traffic_note,
                      "conv_ms_per_step": conv_ms, "step_ms": step_ms,
                      "conv_share_of_step": conv_ms / step_ms,
                      "timing": "each conv launch timed in a CUDA graph of 10 back-to-back "

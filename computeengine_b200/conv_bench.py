@@ -137,9 +137,28 @@ def bench_configs(iters: int = 200) -> list:
                                                         b.data_ptr(), y.data_ptr(), ws.data_ptr(),
                                                         ws.numel(), stream)), iters)
     flops = 2 * 64 * 64 * 9 * 56 * 56
+    # end to end through the operator API with host buffers: pinned H2D of x
+    # and w, Conv2DOp.forward, pinned D2H of y, every call
+    from .ops import Conv2DOp, QLinearConv2DOp
+    op = Conv2DOp()
+    op.configure({"pads": [1, 1, 1, 1], "activation": "RELU"})
+    xh, wh, bh = (t.cpu().pin_memory() for t in (x, w, b))
+    yh = torch.empty((1, 64, 56, 56)).pin_memory()
+    xo, wo, bo = torch.empty_like(x), torch.empty_like(w), torch.empty_like(b)
+
+    def op_e2e():
+        xo.copy_(xh, non_blocking=True)
+        wo.copy_(wh, non_blocking=True)
+        bo.copy_(bh, non_blocking=True)
+        res = [None]
+        assert op.forward([xo, wo, bo], res)
+        yh.copy_(res[0], non_blocking=True)
+    us_e2e = _time(op_e2e, iters)
     out.append({"config": 1, "workload": "fp32 conv [1,64,56,56] 3x3 -> 64, ReLU, NCHW drop-in "
                 "(pack input + pack weights + bf16x3 conv)", "us": us,
-                "gflops": flops / us / 1e3, "frac_of_bf16_peak_over_3": flops / us / 1e6 / (bf16 / 3)})
+                "gflops": flops / us / 1e3, "frac_of_bf16_peak_over_3": flops / us / 1e6 / (bf16 / 3),
+                "e2e_us": us_e2e, "e2e": "Conv2DOp.forward with host buffers (pinned H2D of x, w, b "
+                                         "and D2H of y inside the timed region)"})
     # config 2
     d2 = L.ConvDesc()
     d2.n, d2.c, d2.h, d2.w, d2.m, d2.kh, d2.kw = 8, 128, 28, 28, 128, 3, 3
@@ -172,10 +191,27 @@ def bench_configs(iters: int = 200) -> list:
     ops = 2 * 8 * 128 * 128 * 9 * 28 * 28
     us_k = _time(conv_only, iters)
     us_d = _time(drop_in, iters)
+    qop = QLinearConv2DOp()
+    qop.configure({"pads": [1, 1, 1, 1], "multiplier": [float(v) for v in mult.cpu().numpy()],
+                   "x_zero_point": 128, "y_zero_point": 0, "qmin": 0, "qmax": 255})
+    xqh, wqh, bqh = (t.cpu().pin_memory() for t in (xq, wq, bq))
+    yqh = torch.empty((8, 128, 28, 28), dtype=torch.uint8).pin_memory()
+    xqo, wqo, bqo = torch.empty_like(xq), torch.empty_like(wq), torch.empty_like(bq)
+
+    def qop_e2e():
+        xqo.copy_(xqh, non_blocking=True)
+        wqo.copy_(wqh, non_blocking=True)
+        bqo.copy_(bqh, non_blocking=True)
+        res = [None]
+        assert qop.forward([xqo, wqo, bqo], res)
+        yqh.copy_(res[0], non_blocking=True)
+    us_qe = _time(qop_e2e, iters)
     out.append({"config": 2, "workload": "int8 conv [8,128,28,28] 3x3 -> 128, requantized, ReLU",
                 "kernel_us": us_k, "kernel_tops": ops / us_k / 1e6,
                 "frac_of_2x_bf16_peak": ops / us_k / 1e6 / (2 * bf16),
-                "drop_in_us": us_d, "drop_in_tops": ops / us_d / 1e6})
+                "drop_in_us": us_d, "drop_in_tops": ops / us_d / 1e6,
+                "e2e_us": us_qe, "e2e": "QLinearConv2DOp.forward with host buffers (pinned H2D of "
+                                        "x, w, bias and D2H of y inside the timed region)"})
     return out
 
 
