@@ -345,9 +345,12 @@ __global__ void __launch_bounds__(128, kDwMinBlocks) dwconv3x3_q8_nhwc(const uin
         }
       }
       if (col_ok[k]) {
-        const uint32_t lo = pack2_sat<kYSigned>(q[0], q[1]);
-        const uint32_t hi = pack2_sat<kYSigned>(q[2], q[3]);
-        *reinterpret_cast<uint32_t*>(yrow + k * a.c_store) = (lo & 0xFFFFu) | (hi << 16);
+        // every q is already clamped to [qmin, qmax] inside the storage type:
+        // its low byte is the stored value (two's complement for int8)
+        const uint32_t w = __byte_perm(__byte_perm(static_cast<uint32_t>(q[0]), static_cast<uint32_t>(q[1]), 0x0040),
+                                       __byte_perm(static_cast<uint32_t>(q[2]), static_cast<uint32_t>(q[3]), 0x0040),
+                                       0x5410);
+        *reinterpret_cast<uint32_t*>(yrow + k * a.c_store) = w;
       }
     }
   };
