@@ -4,6 +4,7 @@ src/benchmarks lacks: ie_bench.cpp only times the CPU matmul row kernel).
     python -m computeengine_b200.conv_bench --layer s1b1_conv3 [--batch 256] [--iters 50]
     python -m computeengine_b200.conv_bench --shape 256,64,56,56,256,1,1 --stride 1 --pad 0
     python -m computeengine_b200.conv_bench --layer s2b2_conv2 --dtype f32
+    python -m computeengine_b200.conv_bench --layer stem   # the 4x1 layer of the stem re-layout
 
 Times one layer of the ResNet-50 stack (or an explicit shape) with CUDA
 events, after warm-up, and prints one JSON line: microseconds per launch,
@@ -44,9 +45,17 @@ def bench_layer(l: ConvLayer, batch: int, iters: int, dtype: str = "int8", seed:
     c_store = (l.cin + 15) // 16 * 16
     m_store = (l.cout + 15) // 16 * 16
     oh = l.out_h
+    in_h, w_shape = l.h, (l.cout, l.cin, l.k, l.k)
+    if l.name == "stem":
+        # the 7x7 / 2 stem as the 4x1 layer over its space-to-depth re-layout
+        # (the re-layout kernel itself is not timed here)
+        if dtype != "int8":
+            raise SystemExit("the stem re-layout is int8 only")
+        L.check(L.lib.ie_cuda_q8_stem_desc(batch, l.cin, l.h, l.h, l.cout, d))
+        in_h, c_store, w_shape = d.h, d.c, (l.cout, d.c, d.kh, d.kw)
     if dtype == "int8":
-        x = torch.randint(0, 256, (batch, l.h, l.h, c_store), dtype=torch.uint8, device=dev)
-        w = torch.from_numpy(rng.integers(-127, 128, (l.cout, l.cin, l.k, l.k)).astype(np.int8)).to(dev)
+        x = torch.randint(0, 256, (batch, in_h, in_h, c_store), dtype=torch.uint8, device=dev)
+        w = torch.from_numpy(rng.integers(-127, 128, w_shape).astype(np.int8)).to(dev)
         packed = torch.zeros(int(L.lib.ie_cuda_q8_packed_weight_bytes(d)), dtype=torch.uint8, device=dev)
         L.check(L.lib.ie_cuda_q8_pack_weights(d, w.data_ptr(), packed.data_ptr(), stream))
         bias = torch.zeros(l.cout, dtype=torch.int32, device=dev)
@@ -239,8 +248,8 @@ def main():
         todo.append((ConvLayer("custom", c, m, kh, a.stride, a.pad, h, "x"), n))
     names = list(layers) if a.all else a.layer
     for name in names:
-        if name == "stem":
-            continue  # the stem runs through its own re-layout; see bench.py
+        if name == "stem" and a.dtype != "int8":
+            continue  # the stem re-layout is int8 only
         todo.append((layers[name], a.batch))
     for l, n in todo:
         print(json.dumps(bench_layer(l, n, a.iters, a.dtype)), flush=True)

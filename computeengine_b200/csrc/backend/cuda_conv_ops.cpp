@@ -957,9 +957,30 @@ ie::Status CudaPool2DOp::configure(const ie::Attrs& attrs) { return parse_pool_c
 ie::Status CudaPool2DOp::forward(const std::vector<ie::Tensor*>& inputs,
                                  std::vector<ie::Tensor*>& outputs,
                                  ie::ExecutionContext& context) {
+  const bool q8 = inputs.size() == 1 && inputs[0] != nullptr &&
+                  (inputs[0]->dtype == ie::DType::U8 || inputs[0]->dtype == ie::DType::I8);
+  if (q8) return forward_q8(*inputs[0], outputs, context);
   if (auto st = validate_unary(inputs, outputs, context, "Pooling"); !st.has_value()) return st;
   if (!config_.has_kernel_shape) return ie::Error::invalid_argument("kernel_shape is required");
   const ie::Tensor& x = *inputs[0];
+  const ie_pool2d_desc d = pool_desc(x);
+  ie_conv2d_shape s;
+  if (auto st = to_status(ie_pool2d_resolve(&d, &s)); !st.has_value()) return st;
+  if (auto st = require_device(); !st.has_value()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(d.n * d.c * s.out_h * s.out_w) * sizeof(float));
+  if (!ydev.has_value()) return ydev.error();
+  if (auto e = to_status(ie_cuda_pool2d_f32(&d, max_pool_ ? 1 : 0, static_cast<const float*>(*xd),
+                                            static_cast<float*>(*ydev), st));
+      !e.has_value()) {
+    return e;
+  }
+  return download_f32(*ydev, ie::Shape{{d.n, d.c, s.out_h, s.out_w}}, context, outputs, st);
+}
+
+ie_pool2d_desc CudaPool2DOp::pool_desc(const ie::Tensor& x) const {
   ie_pool2d_desc d;
   std::memset(&d, 0, sizeof(d));
   d.n = x.shape.dims[0];
@@ -980,20 +1001,75 @@ ie::Status CudaPool2DOp::forward(const std::vector<ie::Tensor*>& inputs,
                                                         : IE_PAD_NOTSET;
   d.ceil_mode = config_.ceil_mode ? 1 : 0;
   d.count_include_pad = config_.count_include_pad ? 1 : 0;
+  return d;
+}
+
+// MaxPool2D of an int8 activation: NCHW (host or device) or the int8
+// activation layout (device).  Device mode returns the activation layout
+// without synchronizing, like CudaQLinearConv2DOp; host mode returns NCHW.
+ie::Status CudaPool2DOp::forward_q8(const ie::Tensor& x, std::vector<ie::Tensor*>& outputs,
+                                    ie::ExecutionContext& context) {
+  if (outputs.size() != 1 || outputs[0] == nullptr) {
+    return ie::Error::invalid_argument("Pooling expects one input and one output");
+  }
+  if (context.allocator == nullptr) return ie::Error::invalid_argument("Pooling requires an allocator");
+  if (x.buffer == nullptr) return ie::Error::invalid_argument("null tensor or buffer");
+  if (!max_pool_) {
+    return ie::Error::unsupported("average pooling of int8 activations has no requantize rule");
+  }
+  if (x.shape.dims.size() != 4) return ie::Error::invalid_argument("Pooling expects 4D NCHW tensors");
+  for (int64_t v : x.shape.dims) {
+    if (v <= 0) return ie::Error::invalid_argument("Pooling expects positive dimensions");
+  }
+  if (!config_.has_kernel_shape) return ie::Error::invalid_argument("kernel_shape is required");
+  const bool x_nhwc = x.layout == ie::Layout::NHWC;
+  if (x_nhwc && x.device != ie::Device::CUDA) {
+    return ie::Error::invalid_argument("an NHWC int8 activation must be a device tensor");
+  }
+  const ie_pool2d_desc d = pool_desc(x);
   ie_conv2d_shape s;
   if (auto st = to_status(ie_pool2d_resolve(&d, &s)); !st.has_value()) return st;
   if (auto st = require_device(); !st.has_value()) return st;
   cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  const int32_t is_signed = x.dtype == ie::DType::I8 ? 1 : 0;
+  const int64_t c_store = (d.c + 15) / 16 * 16;
   auto xd = to_device(dev_, kSlotX, x, st);
   if (!xd.has_value()) return xd.error();
-  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(d.n * d.c * s.out_h * s.out_w) * sizeof(float));
-  if (!ydev.has_value()) return ydev.error();
-  if (auto e = to_status(ie_cuda_pool2d_f32(&d, max_pool_ ? 1 : 0, static_cast<const float*>(*xd),
-                                            static_cast<float*>(*ydev), st));
+  const void* xn = *xd;
+  if (!x_nhwc) {
+    auto packed = dev_.scratch(kSlotXPacked, static_cast<size_t>(d.n * d.h * d.w * c_store));
+    if (!packed.has_value()) return packed.error();
+    if (auto e = to_status(ie_cuda_q8_pack_input(*xd, *packed, d.n, d.c, d.h, d.w, c_store, 0, st));
+        !e.has_value()) {
+      return e;
+    }
+    xn = *packed;
+  }
+  const ie::Shape logical{{d.n, d.c, s.out_h, s.out_w}};
+  const size_t y_bytes = static_cast<size_t>(d.n * s.out_h * s.out_w * c_store);
+  if (device_mode(context)) {
+    auto t = ie::Tensor::allocate(ie::Shape{{d.n, s.out_h, s.out_w, c_store}}, x.dtype,
+                                  context.allocator);
+    if (!t.has_value()) return t.error();
+    t->shape = logical;
+    t->layout = ie::Layout::NHWC;
+    t->device = ie::Device::CUDA;
+    if (auto e = to_status(ie_cuda_q8_maxpool2d_nhwc(&d, is_signed, xn, t->buffer, st)); !e.has_value()) {
+      return e;
+    }
+    *outputs[0] = std::move(*t);
+    return {};
+  }
+  auto yd = dev_.scratch(kSlotY, y_bytes);
+  if (!yd.has_value()) return yd.error();
+  if (auto e = to_status(ie_cuda_q8_maxpool2d_nhwc(&d, is_signed, xn, *yd, st)); !e.has_value()) return e;
+  auto yc = dev_.scratch(kSlotYPacked, static_cast<size_t>(d.n * d.c * s.out_h * s.out_w));
+  if (!yc.has_value()) return yc.error();
+  if (auto e = to_status(ie_cuda_q8_unpack_output(*yd, *yc, d.n, d.c, s.out_h, s.out_w, c_store, st));
       !e.has_value()) {
     return e;
   }
-  return download_f32(*ydev, ie::Shape{{d.n, d.c, s.out_h, s.out_w}}, context, outputs, st);
+  return deliver(*yc, logical, x.dtype, context, outputs, st);
 }
 
 ie::Status CudaGlobalAvgPoolOp::forward(const std::vector<ie::Tensor*>& inputs,

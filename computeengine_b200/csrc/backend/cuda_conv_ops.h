@@ -210,7 +210,11 @@ ie::Status parse_pool_config(const ie::Attrs& attrs, PoolConfig& config);
 // CudaPool2DOp(true)  replaces MaxPool2DOp (pool_ops.h:37-51)
 // CudaPool2DOp(false) replaces AvgPool2DOp (pool_ops.h:54-68)
 // NCHW F32 host (or device) tensor in, host NCHW F32 out; bit-exact with the
-// reference (same window order and arithmetic).
+// reference (same window order and arithmetic).  MaxPool2D also takes a U8 /
+// I8 activation of a quantized graph (NCHW, or the int8 activation layout in
+// device mode; ie_cuda_q8_maxpool2d_nhwc): the output keeps the input's
+// dtype, scale and zero point and equals the reference pool run on the same
+// integers as floats.  Average pooling of int8 is Unsupported.
 class CudaPool2DOp final : public ie::Op {
  public:
   explicit CudaPool2DOp(bool max_pool) : max_pool_(max_pool) {}
@@ -219,6 +223,10 @@ class CudaPool2DOp final : public ie::Op {
                      ie::ExecutionContext& context) override;
 
  private:
+  ie_pool2d_desc pool_desc(const ie::Tensor& x) const;
+  ie::Status forward_q8(const ie::Tensor& x, std::vector<ie::Tensor*>& outputs,
+                        ie::ExecutionContext& context);
+
   PoolConfig config_{};
   bool max_pool_;
   DeviceBuffers dev_;

@@ -294,15 +294,19 @@ std::unique_ptr<QGraph> make_q8_block_graph(int64_t c = 32, int64_t mid = 16) {
   const ie::ValueId w1 = weight("qw1", {mid, c, 1, 1});
   const ie::ValueId w2 = weight("qw2", {mid, mid, 3, 3});
   const ie::ValueId w3 = weight("qw3", {c, mid, 1, 1});
-  const ie::ValueId c1 = value("qc1"), c2 = value("qc2"), c3 = value("qc3");
+  const ie::ValueId c1 = value("qc1"), c2 = value("qc2"), c3 = value("qc3"), sum = value("qsum");
   const ie::ValueId y = value("qy", false, true);
   node(ie::OpType::Conv2D, {x, w1}, c1, qattrs(mid, 0.004, 0.008, 37, 10, 10, 0));
   node(ie::OpType::Conv2D, {c1, w2}, c2, qattrs(mid, 0.0015, 0.003, 10, 0, 0, 1));
   node(ie::OpType::Conv2D, {c2, w3}, c3, qattrs(c, 0.004, 0.008, 0, 128, 0, 0));
-  node(ie::OpType::Add, {c3, x}, y,
+  node(ie::OpType::Add, {c3, x}, sum,
        {{"a_multiplier", std::vector<double>{0.5}}, {"b_multiplier", std::vector<double>{0.75}},
         {"a_zero_point", int64_t{128}}, {"b_zero_point", int64_t{37}},
         {"y_zero_point", int64_t{0}}, {"qmin", int64_t{0}}});
+  // the stem's pool shape on the int8 activation layout
+  node(ie::OpType::MaxPool2D, {sum}, y,
+       {{"kernel_shape", std::vector<int64_t>{3, 3}}, {"strides", std::vector<int64_t>{2, 2}},
+        {"pads", std::vector<int64_t>{1, 1, 1, 1}}});
   return qg;
 }
 
@@ -789,7 +793,7 @@ int run_gpu(const std::string& dir) {
     auto r2 = exec.run(qg->g, in, std::make_shared<ie::MallocAllocator>(), stream);
     expect(r2.has_value() && std::memcmp((*r1)[0].buffer, (*r2)[0].buffer, (*r1)[0].bytes()) == 0,
            "Q8EXEC: second run identical");
-    expect((*r1)[0].shape.dims == std::vector<int64_t>{2, 32, 14, 14} &&
+    expect((*r1)[0].shape.dims == std::vector<int64_t>{2, 32, 7, 7} &&
                (*r1)[0].dtype == ie::DType::U8 && (*r1)[0].device == ie::Device::CPU,
            "Q8EXEC: host NCHW uint8 output");
     dump(dir, manifest, "q8g_x", x.t);
@@ -882,6 +886,32 @@ int run_gpu(const std::string& dir) {
     dump(dir, manifest, "head_wfc", wfc.t);
     dump(dir, manifest, "head_bfc", bfc.t);
     dump(dir, manifest, "head_fc", yf);
+    // int8 MaxPool2D on a host NCHW tensor: rectangular kernel, asymmetric
+    // pads, ceil_mode, a channel count that is not a multiple of 16
+    HostTensor xq({2, 5, 13, 11}, ie::DType::I8);
+    for (int64_t i = 0; i < xq.t.numel(); ++i) {
+      xq.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 256) - 128);
+    }
+    auto mq = reg.create(ie::OpType::MaxPool2D);
+    auto aq = reg.create(ie::OpType::AvgPool2D);
+    if (!mq.has_value() || !aq.has_value()) return 3;
+    (*mq)->configure({{"kernel_shape", std::vector<int64_t>{2, 3}},
+                      {"strides", std::vector<int64_t>{2, 1}},
+                      {"pads", std::vector<int64_t>{0, 1, 1, 0}},
+                      {"ceil_mode", int64_t{1}}});
+    (*aq)->configure({{"kernel_shape", std::vector<int64_t>{2, 2}}});
+    ie::Tensor yq, yqa;
+    std::vector<ie::Tensor*> oq{&yq}, oqa{&yqa};
+    const ie::Status qst = (*mq)->forward({&xq.t}, oq, ctx);
+    expect(qst.has_value() && yq.dtype == ie::DType::I8 && yq.device == ie::Device::CPU,
+           "int8 MaxPool2D forward");
+    if (!qst.has_value()) std::printf("  %s\n", qst.error().message.c_str());
+    const ie::Status ast = (*aq)->forward({&xq.t}, oqa, ctx);
+    expect(!ast.has_value() && ast.error().code == ie::Error::Code::Unsupported,
+           "int8 AvgPool2D is Unsupported");
+    if (yq.buffer == nullptr) return 4;
+    dump(dir, manifest, "head_q8x", xq.t);
+    dump(dir, manifest, "head_q8max", yq);
   }
   // int8 post-training quantization of an fp32 Conv2D + ReLU: calibrate the
   // input and output ranges on the fp32 op, quantize, run the int8 op with

@@ -960,6 +960,35 @@ int ie_cuda_q8_stem_pack_weights(const int8_t* w, void* packed, int64_t m, int64
   return q8_write_weight_sums(&d, packed, as_stream(stream));
 }
 
+namespace {
+
+// The row-walking 3x3 / stride-2 pool: 4 output rows per thread (oh, ow and
+// the arguments already checked to fit int32; pad < 3 keeps every window's
+// first row and column inside the image).
+int launch_maxpool3x3s2(const void* x, void* y, int64_t n, int64_t h, int64_t w,
+                        int64_t c_store, int64_t oh, int64_t ow, int64_t pad, int32_t is_signed,
+                        void* stream) {
+  constexpr int64_t kRows = 4;
+  const int64_t chunks = ceil_div(oh, kRows);
+  const int64_t total = n * chunks * ow * (c_store / 16);
+  const auto xp = static_cast<const uint8_t*>(x);
+  const auto yp = static_cast<uint8_t*>(y);
+  const auto nn = static_cast<int32_t>(n), hh = static_cast<int32_t>(h), ww = static_cast<int32_t>(w),
+             cs = static_cast<int32_t>(c_store), ohh = static_cast<int32_t>(oh),
+             oww = static_cast<int32_t>(ow), pp = static_cast<int32_t>(pad),
+             rr = static_cast<int32_t>(kRows), ch = static_cast<int32_t>(chunks);
+  if (is_signed) {
+    maxpool3x3s2_q8_nhwc<true><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        xp, yp, nn, hh, ww, cs, ohh, oww, pp, rr, ch);
+  } else {
+    maxpool3x3s2_q8_nhwc<false><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        xp, yp, nn, hh, ww, cs, ohh, oww, pp, rr, ch);
+  }
+  return check_launch("maxpool3x3s2_q8_nhwc");
+}
+
+}  // namespace
+
 int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w,
                          int64_t c_store, int64_t k, int64_t stride, int64_t pad,
                          int32_t is_signed, void* stream) {
@@ -972,12 +1001,27 @@ int ie_cuda_q8_maxpool2d(const void* x, void* y, int64_t n, int64_t h, int64_t w
   }
   const int64_t oh = (h + 2 * pad - k) / stride + 1, ow = (w + 2 * pad - k) / stride + 1;
   if (oh <= 0 || ow <= 0) return fail(IE_INVALID_ARGUMENT, "pooling produces an empty output");
+  if (n > INT32_MAX || h > INT32_MAX || w > INT32_MAX || c_store > INT32_MAX || k > INT32_MAX ||
+      stride > INT32_MAX || (oh - 1) * stride > INT32_MAX || (ow - 1) * stride > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "pooling extent too large");
+  }
+  if (k == 3 && stride == 2) {
+    return launch_maxpool3x3s2(x, y, n, h, w, c_store, oh, ow, pad, is_signed, stream);
+  }
   const int64_t total = n * oh * ow * (c_store / 16);
-  maxpool_q8_nhwc<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), static_cast<int32_t>(n),
-      static_cast<int32_t>(h), static_cast<int32_t>(w), static_cast<int32_t>(c_store),
-      static_cast<int32_t>(oh), static_cast<int32_t>(ow), static_cast<int32_t>(k),
-      static_cast<int32_t>(stride), static_cast<int32_t>(pad), is_signed);
+  const auto xp = static_cast<const uint8_t*>(x);
+  const auto yp = static_cast<uint8_t*>(y);
+  const auto nn = static_cast<int32_t>(n), hh = static_cast<int32_t>(h), ww = static_cast<int32_t>(w),
+             cs = static_cast<int32_t>(c_store), ohh = static_cast<int32_t>(oh),
+             oww = static_cast<int32_t>(ow), kk = static_cast<int32_t>(k),
+             ss = static_cast<int32_t>(stride), pp = static_cast<int32_t>(pad);
+  if (is_signed) {
+    maxpool_q8_nhwc<true><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        xp, yp, nn, hh, ww, cs, ohh, oww, kk, ss, pp);
+  } else {
+    maxpool_q8_nhwc<false><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        xp, yp, nn, hh, ww, cs, ohh, oww, kk, ss, pp);
+  }
   return check_launch("maxpool_q8_nhwc");
 }
 
@@ -1233,6 +1277,52 @@ int ie_cuda_pool2d_f32(const ie_pool2d_desc* d, int32_t max_pool, const float* x
   const int64_t total = a.planes * s.out_h * s.out_w;
   pool2d_f32_nchw<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(x, y, a);
   return check_launch("pool2d_f32_nchw");
+}
+
+int ie_cuda_q8_maxpool2d_nhwc(const ie_pool2d_desc* d, int32_t is_signed, const void* x,
+                              void* y, void* stream) {
+  ie_conv2d_shape s;
+  int rc = ie_pool2d_resolve(d, &s);
+  if (rc != IE_OK) return rc;
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if ((rc = check_ptr(y, "y", 16)) != IE_OK) return rc;
+  const int64_t c_store = round_up(d->c, 16);
+  if (d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX || c_store > INT32_MAX ||
+      d->kh > INT32_MAX || d->kw > INT32_MAX || d->stride_h > INT32_MAX ||
+      d->stride_w > INT32_MAX || s.out_h > INT32_MAX || s.out_w > INT32_MAX ||
+      s.pad_top + s.pad_bottom + d->h > INT32_MAX || s.pad_left + s.pad_right + d->w > INT32_MAX ||
+      (s.out_h - 1) * d->stride_h > INT32_MAX || (s.out_w - 1) * d->stride_w > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "pooling extent too large");
+  }
+  Q8PoolArgs a;
+  a.n = static_cast<int32_t>(d->n);
+  a.h = static_cast<int32_t>(d->h);
+  a.w = static_cast<int32_t>(d->w);
+  a.c_store = static_cast<int32_t>(c_store);
+  a.out_h = static_cast<int32_t>(s.out_h);
+  a.out_w = static_cast<int32_t>(s.out_w);
+  a.kh = static_cast<int32_t>(d->kh);
+  a.kw = static_cast<int32_t>(d->kw);
+  a.stride_h = static_cast<int32_t>(d->stride_h);
+  a.stride_w = static_cast<int32_t>(d->stride_w);
+  a.pad_t = static_cast<int32_t>(s.pad_top);
+  a.pad_l = static_cast<int32_t>(s.pad_left);
+  if (a.kh == 3 && a.kw == 3 && a.stride_h == 2 && a.stride_w == 2 && a.pad_t == a.pad_l &&
+      s.pad_top < 3 && s.pad_bottom < 3 && s.pad_left < 3 && s.pad_right < 3) {
+    // every pad below the kernel size: each window holds an in-image pixel,
+    // and its bottom / right edge clips at the image
+    return launch_maxpool3x3s2(x, y, d->n, d->h, d->w, c_store, s.out_h, s.out_w, a.pad_t,
+                               is_signed, stream);
+  }
+  const int64_t total = d->n * s.out_h * s.out_w * (c_store / 16);
+  if (is_signed) {
+    maxpool_q8_nhwc_any<true><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), a);
+  } else {
+    maxpool_q8_nhwc_any<false><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+        static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), a);
+  }
+  return check_launch("maxpool_q8_nhwc_any");
 }
 
 int ie_cuda_global_avg_pool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h,

@@ -226,16 +226,18 @@ namespace ie_cuda {
 // Space-to-depth by 2 plus a 4-column unroll turns the stem into a 4x1,
 // stride-1 convolution over 16*c channels (stored as 64), so it runs on the
 // same implicit-GEMM kernel as every other layer:
-//   out[i][j][((b*2+dy)*2+dx)*c + ch] = x[ch][2i+dy][2(j+b-2)+dx]   (0 if j+b-2
-//   is outside [0, w/2)), i in [0, h/2), j in [0, w/2)
-// For a fixed (ch, dy) the eight bytes b = 0..3, dx = 0..1 are the input
-// columns 2j-4 .. 2j+3 of one row.  One block per (image, output row i): input
-// rows 2i and 2i+1 of every channel are staged in shared memory between
+//   out[i][j][(ch*2+dy)*8 + 2b+dx] = x[ch][2i+dy][2(j+b-2)+dx]   (0 if j+b-2
+//   is outside [0, w/2)), i in [0, h/2), j in [0, w/2); channels 16c..63 are 0
+// For a fixed (ch, dy) the eight bytes 2b+dx = 0..7 are the input columns
+// 2j-4 .. 2j+3 of one row, in order, so every output word is one
+// funnel-shifted word of that row.  One block per (image, output row i):
+// input rows 2i and 2i+1 of every channel are staged in shared memory between
 // 16-byte zero margins (so columns outside the image read as 0), each thread
-// builds one output pixel's 64 bytes as whole words from one funnel-shifted
-// word pair per (ch, dy), and the row (w/2 pixels x 64 bytes) is staged with a
-// 16-byte-chunk swizzle (conflict-free 128-bit shared stores and loads) and
-// written with coalesced 16-byte stores.
+// builds one output pixel's 64 bytes from one funnel-shifted word pair per
+// (ch, dy), and the row (w/2 pixels x 64 bytes) is staged with a 16-byte-chunk
+// swizzle (conflict-free 128-bit shared stores and loads) and written with
+// coalesced 16-byte stores.  The channel order is this layout's own; the
+// weights are packed to match (stem_pack_weights_q8).
 constexpr int kStemMargin = 16;
 
 __host__ __device__ constexpr int stem_row_stride(int w) {
@@ -301,22 +303,13 @@ __global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restric
         hi[cc][dy] = __funnelshift_r(w1, w2, sh);
       }
     }
+    // word (ch * 2 + dy) * 2 + half = input columns 2j-4+4*half .. +3 of
+    // row 2i+dy of channel ch; words 4C..15 are zero
     uint32_t o[16];
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
-      uint32_t v = 0;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int chan = 4 * q + kk;
-        if (chan < 16 * C) {
-          const int cc = chan % C, rest = chan / C;
-          const int dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
-          const int k = 2 * b + dx;
-          const uint32_t src = k < 4 ? lo[cc][dy] : hi[cc][dy];
-          v |= ((src >> (8 * (k & 3))) & 0xFFu) << (8 * kk);
-        }
-      }
-      o[q] = v;
+      const int cc = q >> 2, dy = (q >> 1) & 1;
+      o[q] = q < 4 * C ? ((q & 1) ? hi[cc < C ? cc : 0][dy] : lo[cc < C ? cc : 0][dy]) : 0u;
     }
     const int32_t swz = (j >> 1) & 3;
 #pragma unroll
@@ -346,9 +339,8 @@ __global__ void stem_pack_weights_q8(const int8_t* __restrict__ w, int8_t* __res
   const int32_t mo = static_cast<int32_t>(idx / 256);
   int8_t v = 0;
   if (chan < 16 * c) {
-    const int32_t cc = chan % c;
-    const int32_t rest = chan / c;
-    const int32_t dx = rest & 1, dy = (rest >> 1) & 1, b = rest >> 2;
+    const int32_t cc = chan >> 4, dy = (chan >> 3) & 1, k = chan & 7;
+    const int32_t b = k >> 1, dx = k & 1;
     const int32_t ky = 2 * a + dy - 1, kx = 2 * b + dx - 1;
     if (ky >= 0 && ky < 7 && kx >= 0 && kx < 7) {
       v = w[((static_cast<int64_t>(mo) * c + cc) * 7 + ky) * 7 + kx];
@@ -357,8 +349,6 @@ __global__ void stem_pack_weights_q8(const int8_t* __restrict__ w, int8_t* __res
   out[idx] = v;
 }
 
-// Max pooling over 8-bit NHWC activations, 16 channels per thread; windows
-// only cover real pixels (padding never wins).
 // Max pooling over split fp32 activations: bf16 NHWC with [hi plane (c_store)
 // | lo plane (c_store)] per pixel.  The pair with the largest hi + lo (exact
 // in fp32) is copied, so the pool keeps the stored values bit for bit.  One
@@ -409,72 +399,199 @@ __global__ void maxpool_f32x2_nhwc(const __nv_bfloat16* __restrict__ x,
   *reinterpret_cast<uint4*>(out + c_store + g * 8) = bl;
 }
 
+// Byte-wise maximum of 16-byte channel vectors on 16-bit lanes: a vector is
+// spread over 8 words of two lanes (even and odd bytes, zero- or
+// sign-extended by one byte permute each), the maximum is the sm_90+ SIMD
+// max.u16x2 / max.s16x2, and the low bytes of the lanes are packed back.
+struct Lanes16 {
+  uint32_t v[8];
+};
+
+// prmt.b32 with the full 4-bit selectors: a selector's top bit replicates the
+// sign of the selected byte (the __byte_perm intrinsic reads 3 bits only).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+template <bool kSigned>
+__device__ __forceinline__ Lanes16 lanes_of(uint4 q) {
+  // selectors: bytes 0 and 2 (1 and 3) of the word, each followed by a zero
+  // byte (unsigned) or by its own sign replicated (signed)
+  constexpr uint32_t kEven = kSigned ? 0xA280u : 0x4240u;
+  constexpr uint32_t kOdd = kSigned ? 0xB391u : 0x4341u;
+  Lanes16 l;
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    l.v[2 * i] = prmt(w[i], 0u, kEven);
+    l.v[2 * i + 1] = prmt(w[i], 0u, kOdd);
+  }
+  return l;
+}
+
+template <bool kSigned>
+__device__ __forceinline__ uint32_t max16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (kSigned) {
+    asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  } else {
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  }
+  return d;
+}
+
+template <bool kSigned>
+__device__ __forceinline__ void lanes_max(Lanes16& acc, const Lanes16& l) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc.v[i] = max16x2<kSigned>(acc.v[i], l.v[i]);
+}
+
+// The identity of the maximum: every lane at the storage type's minimum.
+template <bool kSigned>
+__device__ __forceinline__ Lanes16 lanes_min() {
+  Lanes16 l;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) l.v[i] = kSigned ? 0xFF80FF80u : 0u;
+  return l;
+}
+
+__device__ __forceinline__ uint4 lanes_pack(const Lanes16& l) {
+  // byte 0 of each lane: even lane words give bytes 0 / 2, odd ones 1 / 3
+  return make_uint4(__byte_perm(l.v[0], l.v[1], 0x6240u), __byte_perm(l.v[2], l.v[3], 0x6240u),
+                    __byte_perm(l.v[4], l.v[5], 0x6240u), __byte_perm(l.v[6], l.v[7], 0x6240u));
+}
+
+// Max pooling over 8-bit NHWC activations (k x k, stride, symmetric pad),
+// 16 channels per thread, one output pixel per thread; windows only cover
+// real pixels (padding never wins).
+template <bool kSigned>
 __global__ void maxpool_q8_nhwc(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
                                 int32_t n, int32_t h, int32_t w, int32_t c_store, int32_t oh,
-                                int32_t ow, int32_t k, int32_t stride, int32_t pad,
-                                int32_t is_signed) {
+                                int32_t ow, int32_t k, int32_t stride, int32_t pad) {
   const int32_t groups = c_store >> 4;
   const int64_t total = static_cast<int64_t>(n) * oh * ow * groups;
-  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (idx >= total) return;
-  const int32_t g = static_cast<int32_t>(idx % groups);
-  const int64_t pix = idx / groups;
-  const int32_t ox = static_cast<int32_t>(pix % ow);
-  const int32_t oy = static_cast<int32_t>((pix / ow) % oh);
-  const int32_t img = static_cast<int32_t>(pix / (static_cast<int64_t>(ow) * oh));
-  const uint32_t init = is_signed ? 0x80808080u : 0u;
-  uint4 best = make_uint4(init, init, init, init);
-  if (k == 3) {
-    // All nine window loads in flight at once.  The first in-bounds pixel of
-    // the window (it always exists: pad < k) stands in for out-of-bounds
-    // taps, which leaves the maximum unchanged.
-    const int32_t y0 = oy * stride - pad, x0 = ox * stride - pad;
-    const int32_t fy = y0 < 0 ? 0 : y0, fx = x0 < 0 ? 0 : x0;
-    const uint8_t* base = x + static_cast<int64_t>(img) * h * w * c_store + g * 16;
-    uint4 v[9];
-#pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        int32_t iy = y0 + ky, ix = x0 + kx;
-        const bool in = iy >= 0 && iy < h && ix >= 0 && ix < w;
-        iy = in ? iy : fy;
-        ix = in ? ix : fx;
-        v[ky * 3 + kx] = __ldg(reinterpret_cast<const uint4*>(
-            base + (static_cast<int64_t>(iy) * w + ix) * c_store));
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t g = static_cast<int32_t>(idx % groups);
+    const int64_t pix = idx / groups;
+    const int32_t ox = static_cast<int32_t>(pix % ow);
+    const int32_t oy = static_cast<int32_t>((pix / ow) % oh);
+    const int64_t img = pix / (static_cast<int64_t>(ow) * oh);
+    Lanes16 best = lanes_min<kSigned>();
+    for (int ky = 0; ky < k; ++ky) {
+      const int32_t iy = oy * stride - pad + ky;
+      if (iy < 0 || iy >= h) continue;
+      for (int kx = 0; kx < k; ++kx) {
+        const int32_t ix = ox * stride - pad + kx;
+        if (ix < 0 || ix >= w) continue;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+            x + ((img * h + iy) * w + ix) * c_store + g * 16));
+        lanes_max<kSigned>(best, lanes_of<kSigned>(v));
       }
     }
-#pragma unroll
-    for (int t = 0; t < 9; ++t) {
-      if (is_signed) {
-        best.x = __vmaxs4(best.x, v[t].x); best.y = __vmaxs4(best.y, v[t].y);
-        best.z = __vmaxs4(best.z, v[t].z); best.w = __vmaxs4(best.w, v[t].w);
-      } else {
-        best.x = __vmaxu4(best.x, v[t].x); best.y = __vmaxu4(best.y, v[t].y);
-        best.z = __vmaxu4(best.z, v[t].z); best.w = __vmaxu4(best.w, v[t].w);
-      }
-    }
-    reinterpret_cast<uint4*>(y)[pix * groups + g] = best;
-    return;
+    reinterpret_cast<uint4*>(y)[idx] = lanes_pack(best);
   }
-  for (int ky = 0; ky < k; ++ky) {
-    const int32_t iy = oy * stride - pad + ky;
-    if (iy < 0 || iy >= h) continue;
-    for (int kx = 0; kx < k; ++kx) {
-      const int32_t ix = ox * stride - pad + kx;
-      if (ix < 0 || ix >= w) continue;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(
-          x + ((static_cast<int64_t>(img) * h + iy) * w + ix) * c_store + g * 16));
-      if (is_signed) {
-        best.x = __vmaxs4(best.x, v.x); best.y = __vmaxs4(best.y, v.y);
-        best.z = __vmaxs4(best.z, v.z); best.w = __vmaxs4(best.w, v.w);
-      } else {
-        best.x = __vmaxu4(best.x, v.x); best.y = __vmaxu4(best.y, v.y);
-        best.z = __vmaxu4(best.z, v.z); best.w = __vmaxu4(best.w, v.w);
+}
+
+// The 3x3 / stride-2 pool of the ResNet stem (pad < 3).  Each thread walks
+// `rows` output rows of one 16-channel group at one output column: the
+// maximum of each input row over the window's three columns is taken once,
+// and the last row of one window is the first row of the next, so an output
+// row costs two new input rows (six 16-byte loads) instead of nine taps.
+// Columns outside the image are replaced by the window's first in-image
+// column (always present: pad < 3), which leaves the maximum unchanged.
+template <bool kSigned>
+__global__ void __launch_bounds__(256) maxpool3x3s2_q8_nhwc(
+    const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int32_t n, int32_t h, int32_t w,
+    int32_t c_store, int32_t oh, int32_t ow, int32_t pad, int32_t rows, int32_t chunks) {
+  const int32_t groups = c_store >> 4;
+  const int64_t total = static_cast<int64_t>(n) * chunks * ow * groups;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t g = static_cast<int32_t>(idx % groups);
+    int64_t t = idx / groups;
+    const int32_t ox = static_cast<int32_t>(t % ow);
+    t /= ow;
+    const int32_t chunk = static_cast<int32_t>(t % chunks);
+    const int64_t img = t / chunks;
+    const int32_t x0 = 2 * ox - pad;
+    const int32_t fx = min(max(x0, 0), w - 1);
+    const int32_t c0 = fx, c1 = (x0 + 1 >= 0 && x0 + 1 < w) ? x0 + 1 : fx;
+    const int32_t c2 = x0 + 2 < w ? x0 + 2 : fx;
+    const uint8_t* base = x + img * h * static_cast<int64_t>(w) * c_store + g * 16;
+    auto row_max = [&](int32_t iy) {
+      const uint8_t* r = base + static_cast<int64_t>(iy) * w * c_store;
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(r + static_cast<int64_t>(c0) * c_store));
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(r + static_cast<int64_t>(c1) * c_store));
+      const uint4 c = __ldg(reinterpret_cast<const uint4*>(r + static_cast<int64_t>(c2) * c_store));
+      Lanes16 m = lanes_of<kSigned>(a);
+      lanes_max<kSigned>(m, lanes_of<kSigned>(b));
+      lanes_max<kSigned>(m, lanes_of<kSigned>(c));
+      return m;
+    };
+    const int32_t oy0 = chunk * rows;
+    const int32_t oy1 = min(oh, oy0 + rows);
+    Lanes16 carry = lanes_min<kSigned>();  // row max of the window's first row
+    bool have_carry = false;
+    for (int32_t oy = oy0; oy < oy1; ++oy) {
+      const int32_t y0 = 2 * oy - pad;
+      Lanes16 acc = lanes_min<kSigned>();
+      if (have_carry) {
+        acc = carry;
+      } else if (y0 >= 0 && y0 < h) {
+        acc = row_max(y0);
       }
+      if (y0 + 1 >= 0 && y0 + 1 < h) lanes_max<kSigned>(acc, row_max(y0 + 1));
+      carry = lanes_min<kSigned>();
+      if (y0 + 2 >= 0 && y0 + 2 < h) {
+        carry = row_max(y0 + 2);
+        lanes_max<kSigned>(acc, carry);
+      }
+      have_carry = true;
+      reinterpret_cast<uint4*>(y)[((img * oh + oy) * ow + ox) * groups + g] = lanes_pack(acc);
     }
   }
-  reinterpret_cast<uint4*>(y)[pix * groups + g] = best;
+}
+
+// Max pooling of 8-bit NHWC activations under any resolved pooling
+// configuration (rectangular kernel, per-axis strides, asymmetric padding,
+// ceil_mode output size): the window of output (oy, ox) starts at
+// (oy * stride_h - pad_t, ox * stride_w - pad_l), out-of-image positions are
+// skipped, and a window with no in-image position gives the storage type's
+// minimum (the 8-bit counterpart of the fp32 pool's -inf start).
+struct Q8PoolArgs {
+  int32_t n, h, w, c_store, out_h, out_w;
+  int32_t kh, kw, stride_h, stride_w, pad_t, pad_l;
+};
+
+template <bool kSigned>
+__global__ void maxpool_q8_nhwc_any(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                    const Q8PoolArgs a) {
+  const int32_t groups = a.c_store >> 4;
+  const int64_t total = static_cast<int64_t>(a.n) * a.out_h * a.out_w * groups;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t g = static_cast<int32_t>(idx % groups);
+    const int64_t pix = idx / groups;
+    const int32_t ox = static_cast<int32_t>(pix % a.out_w);
+    const int32_t oy = static_cast<int32_t>((pix / a.out_w) % a.out_h);
+    const int64_t img = pix / (static_cast<int64_t>(a.out_w) * a.out_h);
+    const int32_t y0 = oy * a.stride_h - a.pad_t, x0 = ox * a.stride_w - a.pad_l;
+    const int32_t ky0 = max(0, -y0), ky1 = min(a.kh, a.h - y0);
+    const int32_t kx0 = max(0, -x0), kx1 = min(a.kw, a.w - x0);
+    const uint8_t* base = x + img * a.h * static_cast<int64_t>(a.w) * a.c_store + g * 16;
+    Lanes16 best = lanes_min<kSigned>();
+    for (int32_t ky = ky0; ky < ky1; ++ky) {
+      const uint8_t* row = base + static_cast<int64_t>(y0 + ky) * a.w * a.c_store;
+      for (int32_t kx = kx0; kx < kx1; ++kx) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(row + static_cast<int64_t>(x0 + kx) * a.c_store));
+        lanes_max<kSigned>(best, lanes_of<kSigned>(v));
+      }
+    }
+    reinterpret_cast<uint4*>(y)[idx] = lanes_pack(best);
+  }
 }
 
 }  // namespace ie_cuda

@@ -370,6 +370,19 @@ int ie_pool2d_resolve(const ie_pool2d_desc* desc, ie_conv2d_shape* out);
 int ie_cuda_pool2d_f32(const ie_pool2d_desc* desc, int32_t max_pool, const float* x, float* y,
                        void* stream);
 
+/* Max pooling of 8-bit activations in the int8 activation layout (NHWC with
+ * c_store = round_up(desc->c, 16) bytes per pixel; padding channels carry no
+ * data) under the same configurations as ie_cuda_pool2d_f32: the MaxPool2D
+ * node of a quantized graph.  The maximum of quantized values is the
+ * quantized maximum (the quantization is monotonic and the output keeps the
+ * input's scale and zero point), so the result equals the reference
+ * MaxPool2DOp run on the same integers as floats, bit for bit; a window with
+ * no in-image position (possible only when a pad reaches the kernel size)
+ * gives the storage type's minimum where the fp32 pool gives -inf.
+ * x, y 16-byte aligned; y holds [n, out_h, out_w, c_store]. */
+int ie_cuda_q8_maxpool2d_nhwc(const ie_pool2d_desc* desc, int32_t is_signed, const void* x,
+                              void* y, void* stream);
+
 /* [n, c, h, w] -> [n, c, 1, 1] mean over each plane (global_avg_pool_forward,
  * pool_ops.cpp:217-270, behind GlobalAvgPoolOp): one sequential fp32 sum per
  * plane, bit-exact with the reference. */

@@ -56,11 +56,12 @@ def test_cpp_ops_match_oracle(oracle, tmp_path):
     assert err.mean() <= 0.005 * scale, (err.mean(), scale)
 
 
-def test_cpp_q8_block_graph_device_resident(oracle, tmp_path):
+def test_cpp_q8_block_graph_device_resident(oracle, refconv, tmp_path):
     """A quantized ResNet bottleneck graph (int8 Conv2D nodes 1x1 -> 3x3 ->
-    1x1 and an int8 shortcut Add with ReLU) run by CudaExecutor with every
-    int8 value in device memory, bit-exact with the oracle chain (the input's
-    and conv1's zero points are neither 0 nor 128)."""
+    1x1, an int8 shortcut Add with ReLU and a 3x3 / 2 MaxPool2D) run by
+    CudaExecutor with every int8 value in device memory, bit-exact with the
+    oracle chain and the reference pool (the input's and conv1's zero points
+    are neither 0 nor 128)."""
     r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
@@ -70,9 +71,13 @@ def test_cpp_q8_block_graph_device_resident(oracle, tmp_path):
     c1 = oracle.conv2d_q8(x, *p[0], 37, 10, 10, 255)
     c2 = oracle.conv2d_q8(c1, *p[1], 10, 0, 0, 255, pads=(1, 1, 1, 1))
     c3 = oracle.conv2d_q8(c2, *p[2], 0, 128, 0, 255)
-    want = oracle.qadd(c3, 128, np.float32(0.5), x, 37, np.float32(0.75), 0, 0, 255)
-    np.testing.assert_array_equal(t["q8g_y"], want)
-    assert (want == 0).mean() < 0.9 and len(np.unique(want)) > 32
+    s = oracle.qadd(c3, 128, np.float32(0.5), x, 37, np.float32(0.75), 0, 0, 255)
+    assert (s == 0).mean() < 0.9 and len(np.unique(s)) > 32
+    # the graph ends in MaxPool2D 3x3 / 2, pads 1: the reference pool on the
+    # same integers as floats
+    rc, want = refconv.pool2d(s.astype(np.float32), (3, 3), (2, 2), (1, 1, 1, 1), kind="max")
+    assert rc == 0
+    np.testing.assert_array_equal(t["q8g_y"], want.astype(np.uint8))
 
 
 def test_cpp_head_ops_match_reference(refconv, tmp_path):
@@ -98,6 +103,12 @@ def test_cpp_head_ops_match_reference(refconv, tmp_path):
     assert rc == 0
     err = float(np.abs(t["head_fc"] - want).max())
     assert err <= REL_TOL * float(np.abs(want).max()), err
+    # int8 MaxPool2D, host NCHW I8: 2x3 kernel, strides (2, 1), pads
+    # (0, 1, 1, 0), ceil_mode
+    rc, want = refconv.pool2d(t["head_q8x"].astype(np.float32), (2, 3), (2, 1), (0, 1, 1, 0),
+                              ceil_mode=1, kind="max")
+    assert rc == 0
+    np.testing.assert_array_equal(t["head_q8max"], want.astype(np.int8))
 
 
 def test_conv_bn_relu_fusion_pass(oracle, tmp_path):

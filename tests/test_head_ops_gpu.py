@@ -3,7 +3,8 @@ compiled from its sources (pool_ops.cpp, gemm_op.cpp):
 
 * max / average pooling and global average pooling are bit-exact (same window
   order and arithmetic): the ResNet stem pool, SAME padding, ceil_mode,
-  count_include_pad, the 7x7 head average;
+  count_include_pad, the 7x7 head average; int8 max pooling on the int8
+  activation layout against the same pool on the integers as floats;
 * Gemm runs as bf16x3 on the tensor cores: max |err| <= 1e-3 * max |ref|,
   over transA / transB, alpha / beta and every C broadcast, the fused
   column-bias path (the ResNet FC layer 2048 -> 1000) and sizes that are not
@@ -55,6 +56,59 @@ def test_pool2d_bit_exact(refconv, case):
     rc, want = refconv.pool2d(x, kernel, strides, pads, auto, ceil_mode, cip, kind=kind)
     assert rc == 0
     np.testing.assert_array_equal(got, want)
+
+
+Q8_POOLS = [
+    # shape, kernel, strides, pads, auto_pad, ceil, signed
+    ((2, 64, 112, 112), (3, 3), (2, 2), (1, 1, 1, 1), "NOTSET", 0, 0),  # ResNet stem pool
+    ((2, 5, 13, 11), (2, 3), (2, 1), (0, 1, 1, 0), "NOTSET", 1, 1),
+    ((1, 40, 9, 10), (3, 2), (1, 2), (0, 0, 0, 0), "SAME_LOWER", 0, 0),
+    ((1, 24, 8, 8), (3, 3), (3, 3), (0, 0, 0, 0), "SAME_UPPER", 1, 1),
+    ((2, 16, 6, 7), (2, 2), (1, 1), (3, 0, 0, 2), "NOTSET", 0, 1),  # windows in the padding only
+    ((2, 24, 17, 14), (3, 3), (2, 2), (1, 1, 2, 0), "NOTSET", 0, 1),  # 3x3 / 2 row walk, uneven pads
+    ((1, 16, 12, 12), (3, 3), (2, 2), (1, 1, 1, 1), "NOTSET", 1, 0),  # 3x3 / 2 row walk, ceil_mode
+    ((1, 16, 9, 9), (3, 3), (2, 2), (1, 1, 3, 3), "NOTSET", 0, 0),    # 3x3 / 2, pads 3: general kernel
+]
+
+
+@pytest.mark.parametrize("case", Q8_POOLS, ids=lambda c: f"c{c[0][1]}_k{c[1][0]}x{c[1][1]}_{c[4]}_c{c[5]}_s{c[6]}")
+def test_q8_maxpool_nhwc_bit_exact(refconv, case):
+    """int8 max pooling over the int8 activation layout (NHWC, channels padded
+    to 16) equals the reference MaxPool2DOp on the same integers as floats;
+    a window with no in-image position gives the type's minimum (-inf in
+    the reference)."""
+    import torch
+    from computeengine_b200 import _lib as L
+    shape, kernel, strides, pads, auto, ceil_mode, signed = case
+    n, c, h, w = shape
+    rng = np.random.default_rng(sum(shape) + signed)
+    dt = np.int8 if signed else np.uint8
+    lo, hi = (-128, 128) if signed else (0, 256)
+    x = rng.integers(lo, hi, shape).astype(dt)
+    d = L.PoolDesc()
+    d.n, d.c, d.h, d.w = shape
+    d.kh, d.kw = kernel
+    d.stride_h, d.stride_w = strides
+    d.pad_top, d.pad_left, d.pad_bottom, d.pad_right = pads
+    d.auto_pad, d.ceil_mode, d.count_include_pad = AUTO[auto], ceil_mode, 0
+    s = L.ConvShape()
+    L.check(L.lib.ie_pool2d_resolve(d, s))
+    cs = (c + 15) // 16 * 16
+    xn = np.zeros((n, h, w, cs), np.uint8)
+    xn[..., :c] = x.view(np.uint8).transpose(0, 2, 3, 1)
+    xd = torch.from_numpy(xn).cuda()
+    y = torch.full((n, s.out_h, s.out_w, cs), 0x5A, dtype=torch.uint8, device="cuda")
+    L.check(L.lib.ie_cuda_q8_maxpool2d_nhwc(d, signed, xd.data_ptr(), y.data_ptr(), None))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()[..., :c].transpose(0, 3, 1, 2).view(dt)
+    rc, want = refconv.pool2d(x.astype(np.float32), kernel, strides, pads, auto, ceil_mode, 0,
+                              kind="max")
+    assert rc == 0
+    empty = np.isneginf(want)
+    want = np.where(empty, lo, want).astype(dt)
+    np.testing.assert_array_equal(got, want)
+    if pads[0] >= kernel[0]:
+        assert empty.any()
 
 
 @pytest.mark.parametrize("shape", [(4, 2048, 7, 7), (2, 64, 56, 56), (3, 5, 1, 1)])

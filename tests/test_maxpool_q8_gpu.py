@@ -1,6 +1,7 @@
 """8-bit NHWC max pooling on the B200 against numpy, bit-exact: uint8 and
-int8 values, the 3x3 windows of the ResNet stem (stride 2, pad 1) and of a
-stride-1 pool, a non-3x3 window (the general loop), odd sizes whose last
+int8 values, the 3x3 / stride-2 windows of the ResNet stem (the row-walking
+kernel, pads 0, 1 and 2, output heights that leave a short last chunk) and of
+a stride-1 pool, a non-3x3 window (the general loop), odd sizes whose last
 windows hang over the bottom and right edges, and a value range that puts the
 maximum in the padding corners' reach.  Padding never wins, like the
 reference's MaxPool2D (pool_ops.cpp)."""
@@ -31,6 +32,9 @@ CASES = [
     (2, 7, 11, 16, 3, 1, 1, False),     # stride 1
     (1, 10, 10, 48, 2, 2, 0, True),     # general path (k = 2)
     (1, 9, 7, 16, 5, 2, 2, False),      # general path, wide padding
+    (3, 17, 9, 16, 3, 2, 1, False),     # 3x3 / 2 row walk: 9 output rows, a short last chunk
+    (1, 15, 15, 32, 3, 2, 0, True),     # 3x3 / 2 without padding
+    (2, 10, 12, 16, 3, 2, 2, True),     # 3x3 / 2, pad 2: windows with one in-image row
 ]
 
 

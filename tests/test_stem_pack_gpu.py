@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 
 def stem_pack_numpy(x: np.ndarray, xor_mask: int) -> np.ndarray:
-    """out[n][i][j][((b*2+dy)*2+dx)*c + ch] = x[n][ch][2i+dy][2(j+b-2)+dx] ^ mask,
+    """out[n][i][j][(ch*2+dy)*8 + 2b+dx] = x[n][ch][2i+dy][2(j+b-2)+dx] ^ mask,
     0 where j+b-2 is outside [0, w/2); channels 16c..63 are 0."""
     n, c, h, w = x.shape
     ho, wo = h // 2, w // 2
@@ -21,7 +21,7 @@ def stem_pack_numpy(x: np.ndarray, xor_mask: int) -> np.ndarray:
         for dy in range(2):
             for dx in range(2):
                 for ch in range(c):
-                    chan = ((b * 2 + dy) * 2 + dx) * c + ch
+                    chan = (ch * 2 + dy) * 8 + 2 * b + dx
                     src = xs[:, ch, dy::2, dx::2]  # [n, ho, wo], column jj
                     shift = b - 2                   # out column j reads jj = j + shift
                     j0, j1 = max(0, -shift), min(wo, wo - shift)
