@@ -24,6 +24,7 @@ STATUS_NAMES = {0: "Ok", 1: "InvalidArgument", 2: "Unsupported", 3: "NotFound",
 IE_PAD = {"NOTSET": 0, "": 0, "VALID": 1, "SAME_UPPER": 2, "SAME_LOWER": 3}
 IE_ACT_NONE, IE_ACT_RELU, IE_ACT_RELU6 = 0, 1, 2
 IE_Y_F32_NHWC, IE_Y_F32_NCHW, IE_Y_BF16X2_NHWC = 0, 1, 2
+IE_TILE_FILL, IE_TILE_DEFAULT = 0, 1
 
 _i64 = C.c_int64
 _i32 = C.c_int32
@@ -116,6 +117,7 @@ def _load() -> C.CDLL:
         "ie_pool2d_resolve": (C.c_int, [P(PoolDesc), P(ConvShape)]),
         "ie_cuda_pool2d_f32": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
         "ie_cuda_q8_maxpool2d_nhwc": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
+        "ie_cuda_set_tile_policy": (C.c_int, [_i32, P(_i32)]),
         "ie_cuda_global_avg_pool_f32": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _p]),
         "ie_cuda_gemm_f32_workspace_bytes": (C.c_size_t, [_i64, _i64, _i64, _i32, _i32]),
         "ie_cuda_gemm_f32": (C.c_int, [_i64, _i64, _i64, _i32, _i32, C.c_float, C.c_float, _p,
@@ -146,6 +148,14 @@ def take_device_error() -> int:
 
 def launch_count(reset: bool = False) -> int:
     return int(lib.ie_cuda_launch_count(1 if reset else 0))
+
+
+def set_tile_policy(policy: int) -> int:
+    """Sets the int8 tile policy (IE_TILE_FILL / IE_TILE_DEFAULT); returns the
+    previous one."""
+    prev = _i32()
+    check(lib.ie_cuda_set_tile_policy(policy, C.byref(prev)))
+    return prev.value
 
 
 def last_plan() -> ConvPlan:

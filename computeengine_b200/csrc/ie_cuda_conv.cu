@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "conv_igemm.cuh"
@@ -199,11 +200,14 @@ LaunchFn pick_bn_bk(int m_sub, bool b_res) {
     // interleave more requantize chains, which measured 3-12% faster per
     // layer than twice the warps.
     if constexpr (BN <= 128) {
+      // 256 positions per tile by default; 128 where the default tiles cannot
+      // fill the GPU
       if (m_sub == 2) {
         return b_res ? launch_variant<BN, BKB, 8, 2, true, I8, AS>
                      : launch_variant<BN, BKB, 8, 2, false, I8, AS>;
       }
-      return nullptr;
+      return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
+                   : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
     } else {
       return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
                    : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
@@ -254,29 +258,45 @@ struct IgemmSetup {
 //   elem_bytes: 1 (int8) or 2 (bf16; activation and weights hold hi|lo planes)
 //   allow_halo: the caller's output goes through the staged TMA store (int8
 //   requantized), so the row-band mode may be used
-int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
-                int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out,
-                bool allow_halo = false) {
-  const bool i8 = elem_bytes == 1;
-  Variant& v = out->v;
-  v = Variant{};
+std::atomic<int32_t> g_tile_policy{IE_TILE_FILL};
+
+// One tile plan of the implicit GEMM: the kernel variant, its pipeline depth,
+// the row-band geometry when that mode is used, the tile counts and grid, and
+// a cycle estimate used to choose between plans.
+struct TilePlan {
+  Variant v;
+  int stages = 0;
+  int64_t h_wp = 0, h_rows_t = 0, h_rows_box = 0, h_tiles_img = 0, h_band = 0;
+  int64_t m_tiles = 0, n_tiles = 0;
+  int grid = 0;
+  double est = 0.0;
+  double mma_cycles = 0.0;  // estimated MMA time of one tile
+};
+
+// Builds the plan for tiles of bn output channels x 128 * m_sub positions.
+// Returns false when no pipeline of that shape fits in shared memory.
+//
+// The estimate: the CTAs of a persistent grid each run ceil(tiles / CTAs)
+// tiles; a tile costs its 32-byte K steps times the measured cycles of one
+// 128-row MMA step at that width (the shared-memory operand rate bounds N=64
+// and N=128, the tensor pipe N=256: ~68, ~91 and ~137 cycles), its outputs at
+// the epilogue's ~11.7 per cycle per SM, and ~1000 cycles of hand-offs; a
+// CTA with resident weights first loads its bn x K slice at ~64 B/cycle.
+bool plan_tiles(const ie_conv2d_desc* d, const ie_conv2d_shape& s, bool i8, int elem_bytes,
+                int64_t x_c_store, bool allow_halo, int bn, int m_sub, int sms, TilePlan* p) {
+  *p = TilePlan{};
+  Variant& v = p->v;
   v.i8 = i8;
-  v.bn = choose_bn(d->m);
-  v.bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(v.bn, i8));
-  if (v.bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
-                              static_cast<long long>(x_c_store));
-  v.m_sub = (i8 && v.bn <= 128) ? 2 : 1;
+  v.bn = bn;
+  v.bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(bn, i8));
+  if (v.bkb == 0) return false;
+  v.m_sub = m_sub;
   v.epi = i8 ? 8 : (v.bn >= 256 ? 8 : 4);
   const int64_t bk_elems = v.bkb / elem_bytes;
   const int64_t cblocks = ceil_div(x_c_store, bk_elems);
   const int64_t taps = d->kh * d->kw;
-  const int64_t ck = cblocks * bk_elems;
   const int64_t num_k = taps * cblocks;
   const int64_t m_total = d->n * s.out_h * s.out_w;
-  if (m_total > (int64_t{1} << 40) || d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX ||
-      num_k > (1 << 20)) {
-    return fail(IE_UNSUPPORTED, "tensor too large");
-  }
   // Weights resident in shared memory when the CTA's slice fits beside a
   // pipeline of at least 4 activation stages; two staged output tiles (the
   // epilogue never waits for a store) unless that costs pipeline depth below 4.
@@ -302,16 +322,13 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
     v.out_bufs = 1;
     stages = max_stages();
   }
-  if (plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) {
-    return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
-  }
+  if (plan_bytes(v, stages, static_cast<int>(num_k)) > kSmemLimit) return false;
   // Row-band mode for stride-1 multi-tap int8 convolutions: tiles of whole
   // output rows in a (w + pad_l + pad_r)-wide position space, one band load
   // per channel block.  Used when the rows fill the tiles well and the
   // natural tile width keeps the weights resident with at least 3 stages
   // (measured: narrowing the tiles to make the weights fit costs more than
   // the band saves).
-  int64_t h_wp = 0, h_rows_t = 0, h_rows_box = 0, h_tiles_img = 0, h_band = 0;
   if (allow_halo && i8 && d->stride_h == 1 && d->stride_w == 1 && taps > 1) {
     const int64_t wp = d->w + s.pad_left + s.pad_right;
     do {
@@ -337,13 +354,98 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
       }
       v = hv;
       stages = st;
-      h_wp = wp;
-      h_rows_t = rows_t;
-      h_rows_box = rows_box;
-      h_tiles_img = tiles_img;
-      h_band = rows_box * wp * v.bkb;
+      p->h_wp = wp;
+      p->h_rows_t = rows_t;
+      p->h_rows_box = rows_box;
+      p->h_tiles_img = tiles_img;
+      p->h_band = rows_box * wp * v.bkb;
     } while (false);
   }
+  p->stages = stages;
+  p->m_tiles = p->h_wp > 0 ? d->n * p->h_tiles_img : ceil_div(m_total, 128 * v.m_sub);
+  p->n_tiles = ceil_div(d->m, v.bn);
+  int64_t waves;
+  if (v.b_res) {
+    // each CTA keeps one n_tile: the grid is a multiple of n_tiles
+    const int64_t per_n = std::max<int64_t>(
+        1, std::min<int64_t>(p->m_tiles, std::max<int64_t>(1, sms / p->n_tiles)));
+    p->grid = static_cast<int>(per_n * p->n_tiles);
+    waves = ceil_div(p->m_tiles, per_n);
+  } else {
+    p->grid = static_cast<int>(std::min<int64_t>(p->m_tiles * p->n_tiles, sms));
+    waves = ceil_div(p->m_tiles * p->n_tiles, static_cast<int64_t>(p->grid));
+  }
+  const double k_steps = static_cast<double>(num_k) * (v.bkb / 32.0);
+  const double mma = v.bn <= 64 ? 68.0 : (v.bn <= 128 ? 91.0 : 137.0);
+  const double rows = 128.0 * v.m_sub;
+  p->mma_cycles = k_steps * mma * v.m_sub;
+  const double t_tile = p->mma_cycles + rows * v.bn / 11.7 + 1000.0;
+  p->est = static_cast<double>(waves) * t_tile +
+           (v.b_res ? static_cast<double>(v.bn) * num_k * v.bkb / 64.0 : 0.0);
+  return true;
+}
+
+// Shared set-up of the implicit GEMM for both element kinds.
+//   elem_bytes: 1 (int8) or 2 (bf16; activation and weights hold hi|lo planes)
+//   allow_halo: the caller's output goes through the staged TMA store (int8
+//   requantized), so the row-band mode may be used
+//
+// The int8 path considers narrower or shorter tiles beside the default (the
+// widest channel tile that wastes least, 256 positions below 256 channels):
+// a launch whose default tiles cannot fill the GPU and carry at least ~2000
+// cycles of MMA work each takes the plan with the smallest estimate when that
+// is at least 10% below the default's.  Shallower launches keep the default:
+// they are bound by launch and pipeline latency, and a narrow grid leaves
+// SMs to the next launch's prologue (measured: MobileNetV2's K = 160-192 1x1
+// layers at batch 64 ran 13-16% slower on twice the CTAs).  The packed int8
+// weights do not depend on the tile shape.
+int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
+                int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out,
+                bool allow_halo = false) {
+  const bool i8 = elem_bytes == 1;
+  const int64_t m_total = d->n * s.out_h * s.out_w;
+  {
+    const int bkb = choose_bk_bytes(x_c_store, elem_bytes, !i8, igemm_max_bk(choose_bn(d->m), i8));
+    if (bkb == 0) return fail(IE_UNSUPPORTED, "no channel block divides c_store=%lld",
+                              static_cast<long long>(x_c_store));
+    const int64_t num_k = d->kh * d->kw * ceil_div(x_c_store, static_cast<int64_t>(bkb / elem_bytes));
+    if (m_total > (int64_t{1} << 40) || d->n > INT32_MAX || d->h > INT32_MAX || d->w > INT32_MAX ||
+        num_k > (1 << 20)) {
+      return fail(IE_UNSUPPORTED, "tensor too large");
+    }
+  }
+  const int sms = num_sms();
+  const int bn0 = choose_bn(d->m);
+  const int ms0 = (i8 && bn0 <= 128) ? 2 : 1;
+  TilePlan plan;
+  if (!plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, bn0, ms0, sms, &plan)) {
+    return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
+  }
+  if (i8 && plan.grid < sms && plan.mma_cycles >= 2000.0 &&
+      g_tile_policy.load(std::memory_order_relaxed) == IE_TILE_FILL) {
+    const double limit = 0.9 * plan.est;
+    const int cand[][2] = {{bn0, 1}, {128, 1}, {64, 2}, {64, 1}};
+    TilePlan best = plan;
+    for (const auto& c : cand) {
+      if (c[0] > bn0 || (c[0] == bn0 && c[1] == ms0)) continue;
+      TilePlan t;
+      if (plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, c[0], c[1], sms, &t) &&
+          t.est < limit && t.est < best.est) {
+        best = t;
+      }
+    }
+    plan = best;
+  }
+  Variant& v = out->v;
+  v = plan.v;
+  const int stages = plan.stages;
+  const int64_t h_wp = plan.h_wp, h_rows_t = plan.h_rows_t, h_rows_box = plan.h_rows_box;
+  const int64_t h_tiles_img = plan.h_tiles_img, h_band = plan.h_band;
+  const int64_t bk_elems = v.bkb / elem_bytes;
+  const int64_t cblocks = ceil_div(x_c_store, bk_elems);
+  const int64_t taps = d->kh * d->kw;
+  const int64_t ck = cblocks * bk_elems;
+  const int64_t num_k = taps * cblocks;
   const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int64_t a_chan = i8 ? x_c_store : 2 * x_c_store;
   int rc;
@@ -410,8 +512,8 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   a.m_total = m_total;
   // |x| <= 255 (uint8) or 128 (int8), |w| <= 128: |acc| <= K * 255 * 128
   a.acc_bound = d->kh * d->kw * d->c * 255 * 128;
-  a.m_tiles = static_cast<int32_t>(ceil_div(m_total, 128 * v.m_sub));
-  a.n_tiles = static_cast<int32_t>(ceil_div(d->m, v.bn));
+  a.m_tiles = static_cast<int32_t>(plan.m_tiles);
+  a.n_tiles = static_cast<int32_t>(plan.n_tiles);
   a.a_tiled = a_tiled ? 1 : 0;
   if (h_wp > 0) {
     a.halo = 1;
@@ -421,17 +523,8 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
     a.tiles_img = static_cast<int32_t>(h_tiles_img);
     a.stage_bytes = v.halo_stage;
     a.band_bytes = static_cast<int32_t>(h_band);
-    a.m_tiles = static_cast<int32_t>(d->n * h_tiles_img);
   }
-  const int sms = num_sms();
-  if (v.b_res) {
-    // each CTA keeps one n_tile: the grid is a multiple of n_tiles
-    const int per_n = static_cast<int>(std::max<int64_t>(
-        1, std::min<int64_t>(a.m_tiles, std::max(1, sms / a.n_tiles))));
-    out->grid = per_n * a.n_tiles;
-  } else {
-    out->grid = static_cast<int>(std::min<int64_t>(int64_t{a.m_tiles} * a.n_tiles, sms));
-  }
+  out->grid = plan.grid;
   return IE_OK;
 }
 
@@ -626,6 +719,15 @@ int ie_conv2d_resolve(const ie_conv2d_desc* desc, int64_t bias_len, ie_conv2d_sh
 }
 
 const char* ie_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int ie_cuda_set_tile_policy(int32_t policy, int32_t* previous) {
+  if (policy != IE_TILE_FILL && policy != IE_TILE_DEFAULT) {
+    return fail(IE_INVALID_ARGUMENT, "unknown tile policy %d", policy);
+  }
+  const int32_t old = g_tile_policy.exchange(policy);
+  if (previous != nullptr) *previous = old;
+  return IE_OK;
+}
 
 int ie_cuda_last_plan(ie_conv_plan* out) {
   if (out == nullptr) return fail(IE_INVALID_ARGUMENT, "null plan");

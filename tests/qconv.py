@@ -3,6 +3,8 @@ that call the CUDA kernels through the C ABI (ctypes) with torch-owned device
 buffers."""
 from __future__ import annotations
 
+from contextlib import contextmanager
+
 import numpy as np
 
 
@@ -90,3 +92,15 @@ def run_conv_q8_gpu(x, wq, bias, mult, *, stride=(1, 1), pads=(0, 0, 0, 0), dil=
     assert L.take_device_error() == 0
     out = y[..., :m].permute(0, 3, 1, 2).contiguous().cpu().numpy()
     return out.view(np.int8) if (y_signed and not raw_acc) else out
+
+
+@contextmanager
+def tile_policy(policy: int):
+    """Runs the block under an int8 tile policy (ie_cuda_set_tile_policy) and
+    restores the previous one."""
+    from computeengine_b200 import _lib as L
+    prev = L.set_tile_policy(policy)
+    try:
+        yield
+    finally:
+        L.set_tile_policy(prev)

@@ -99,3 +99,17 @@ def test_packed_sizes():
     assert L.lib.ie_cuda_q8_stem_desc(8, 3, 224, 224, 64, sd) == 0
     assert (sd.c, sd.h, sd.kh, sd.kw, sd.pad_top, sd.pad_bottom) == (64, 112, 4, 1, 2, 1)
     assert L.lib.ie_cuda_q8_stem_desc(8, 5, 224, 224, 64, sd) == L.IE_UNSUPPORTED
+
+
+def test_tile_policy_values():
+    """ie_cuda_set_tile_policy is host-only: returns the previous policy and
+    rejects unknown values."""
+    from computeengine_b200 import _lib as L
+    prev = L.set_tile_policy(L.IE_TILE_DEFAULT)
+    try:
+        assert L.set_tile_policy(L.IE_TILE_DEFAULT) == L.IE_TILE_DEFAULT
+        with pytest.raises(L.CudaConvError):
+            L.set_tile_policy(7)
+        assert L.set_tile_policy(L.IE_TILE_FILL) == L.IE_TILE_DEFAULT
+    finally:
+        L.set_tile_policy(prev)

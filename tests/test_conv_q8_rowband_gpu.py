@@ -8,7 +8,7 @@ asymmetric padding and signed / clamped outputs."""
 import numpy as np
 import pytest
 
-from tests.qconv import make_q8_problem, run_conv_q8_gpu
+from tests.qconv import make_q8_problem, run_conv_q8_gpu, tile_policy
 
 pytestmark = pytest.mark.gpu
 
@@ -41,10 +41,18 @@ def _run(case, seed, s_y_scale=3.0, **q):
     return x, wq, bias, mult, got, plan
 
 
+@pytest.mark.parametrize("policy", ["default", "fill"])
 @pytest.mark.parametrize("case", CASES, ids=_ids)
-def test_row_band_bit_exact(oracle, case):
-    x, wq, bias, mult, got, plan = _run(case, 31 + case[1] + case[5] * 7)
-    assert plan.row_band == 1, "row-band mode not selected"
+def test_row_band_bit_exact(oracle, case, policy):
+    """Under the default tiles every case runs the row-band mode; under the
+    fill-the-GPU policy these small launches take 128-position tiles (row band
+    or im2col, as the plan estimate decides) and give the same bytes."""
+    from computeengine_b200 import _lib as L
+    with tile_policy(L.IE_TILE_DEFAULT if policy == "default" else L.IE_TILE_FILL):
+        x, wq, bias, mult, got, plan = _run(case, 31 + case[1] + case[5] * 7)
+    if policy == "default":
+        assert plan.row_band == 1, "row-band mode not selected"
+        assert plan.m_sub == 2 or plan.bn == 256
     n, c, h, w, m, kh, kw, dil, pads = case
     want = oracle.conv2d_q8(x, wq, bias, mult, 128, 0, 0, 255, pads=pads, dilations=(dil, dil))
     np.testing.assert_array_equal(got, want)
@@ -54,10 +62,12 @@ def test_row_band_bit_exact(oracle, case):
 @pytest.mark.parametrize("y_signed,zp_y,qmin,qmax", [(True, 0, -128, 127), (False, 10, 10, 200),
                                                       (True, -5, -100, 90)])
 def test_row_band_output_modes(oracle, y_signed, zp_y, qmin, qmax):
+    from computeengine_b200 import _lib as L
     case = CASES[0]
     # a fine output scale so that both clamps are reached
-    x, wq, bias, mult, got, plan = _run(case, 5, s_y_scale=0.06, y_signed=y_signed, zp_y=zp_y,
-                                        qmin=qmin, qmax=qmax)
+    with tile_policy(L.IE_TILE_DEFAULT):
+        x, wq, bias, mult, got, plan = _run(case, 5, s_y_scale=0.06, y_signed=y_signed,
+                                            zp_y=zp_y, qmin=qmin, qmax=qmax)
     assert plan.row_band == 1
     want = oracle.conv2d_q8(x, wq, bias, mult, 128, zp_y, qmin, qmax, y_signed=y_signed,
                             pads=case[8])
