@@ -230,29 +230,30 @@ namespace ie_cuda {
 //   is outside [0, w/2)), i in [0, h/2), j in [0, w/2); channels 16c..63 are 0
 // For a fixed (ch, dy) the eight bytes 2b+dx = 0..7 are the input columns
 // 2j-4 .. 2j+3 of one row, in order, so every output word is one
-// funnel-shifted word of that row.  One block per (image, output row i):
-// input rows 2i and 2i+1 of every channel are staged in shared memory between
-// 16-byte zero margins (so columns outside the image read as 0), each thread
-// builds one output pixel's 64 bytes from one funnel-shifted word pair per
-// (ch, dy), and the row (w/2 pixels x 64 bytes) is staged with a 16-byte-chunk
-// swizzle (conflict-free 128-bit shared stores and loads) and written with
-// coalesced 16-byte stores.  The channel order is this layout's own; the
-// weights are packed to match (stem_pack_weights_q8).
+// funnel-shifted word of that row, and 16-byte chunk ch of a pixel is
+// channel ch's two rows.  One block per (image, output row i): input rows 2i
+// and 2i+1 of every channel are staged in shared memory between 16-byte zero
+// margins (so columns outside the image read as 0), then each thread builds
+// one 16-byte chunk of one output pixel from two funnel-shifted word pairs
+// and stores it directly (consecutive threads, consecutive chunks: coalesced
+// 16-byte stores).  The channel order is this layout's own; the weights are
+// packed to match (stem_pack_weights_q8).
 constexpr int kStemMargin = 16;
 
+// Staged row stride: margins, the row, rounded to 16 bytes, plus 16 bytes so
+// that the 2C staged rows start in different shared-memory banks.
 __host__ __device__ constexpr int stem_row_stride(int w) {
-  return ((w + 2 * kStemMargin + 15) / 16) * 16;
+  return ((w + 2 * kStemMargin + 15) / 16) * 16 + 16;
 }
 
 template <int C>
-__global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restrict__ x,
+__global__ void __launch_bounds__(128) stem_pack_s2d_u8(const uint8_t* __restrict__ x,
                                                         uint8_t* __restrict__ y, int32_t h,
                                                         int32_t w, uint8_t xor_mask) {
   extern __shared__ __align__(16) uint8_t stem_smem[];
   const int32_t ho = h / 2, wo = w / 2;
   const int32_t rs = stem_row_stride(w);
-  uint8_t* rows = stem_smem;               // [C][2][rs]: margin | w columns | margin
-  uint8_t* tile = stem_smem + C * 2 * rs;  // [wo][64], 16-byte chunks swizzled
+  uint8_t* rows = stem_smem;  // [C][2][rs]: margin | w columns | margin
   const int32_t i = blockIdx.x % ho;
   const int64_t img = blockIdx.x / ho;
   const uint8_t* xi = x + img * C * h * static_cast<int64_t>(w);
@@ -265,21 +266,24 @@ __global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restric
     rows[r * rs + (k < kStemMargin ? k : kStemMargin + w + k - kStemMargin)] = 0;
   }
   // rows 2i, 2i+1 of every channel (contiguous 2w bytes per channel in NCHW)
+  if ((w & 15) == 0 && ((reinterpret_cast<uintptr_t>(xi) + 2 * i * static_cast<int64_t>(w)) & 15) == 0) {
+    // all channels' 16-byte pieces in one pass
+    const int32_t per = (2 * w) >> 4;
+    for (int t = threadIdx.x; t < C * per; t += blockDim.x) {
+      const int32_t cc = t / per, q = t - cc * per;
+      uint4 v = __ldg(reinterpret_cast<const uint4*>(xi + (static_cast<int64_t>(cc) * h + 2 * i) * w) + q);
+      v.x ^= mask4;
+      v.y ^= mask4;
+      v.z ^= mask4;
+      v.w ^= mask4;
+      const int32_t off = q << 4, dy = off >= w;
+      *reinterpret_cast<uint4*>(rows + cc * 2 * rs + kStemMargin + dy * rs + off - dy * w) = v;
+    }
+  } else {
 #pragma unroll
-  for (int cc = 0; cc < C; ++cc) {
-    const uint8_t* src = xi + (static_cast<int64_t>(cc) * h + 2 * i) * w;
-    uint8_t* dst = rows + cc * 2 * rs + kStemMargin;
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (w & 15) == 0) {
-      for (int t = threadIdx.x; t < (2 * w) >> 4; t += blockDim.x) {
-        uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + t);
-        v.x ^= mask4;
-        v.y ^= mask4;
-        v.z ^= mask4;
-        v.w ^= mask4;
-        const int32_t off = t << 4, dy = off >= w;
-        *reinterpret_cast<uint4*>(dst + dy * rs + off - dy * w) = v;
-      }
-    } else {
+    for (int cc = 0; cc < C; ++cc) {
+      const uint8_t* src = xi + (static_cast<int64_t>(cc) * h + 2 * i) * w;
+      uint8_t* dst = rows + cc * 2 * rs + kStemMargin;
       for (int t = threadIdx.x; t < 2 * w; t += blockDim.x) {
         const int32_t dy = t >= w;
         dst[dy * rs + t - dy * w] = src[t] ^ xor_mask;
@@ -288,42 +292,25 @@ __global__ void __launch_bounds__(256) stem_pack_s2d_u8(const uint8_t* __restric
   }
   __syncthreads();
 
-  for (int j = threadIdx.x; j < wo; j += blockDim.x) {
-    // columns 2j-4 .. 2j+3 start at byte kStemMargin - 4 + 2j (even)
-    const int32_t base = kStemMargin - 4 + 2 * j;
-    const uint32_t sh = (base & 3) * 8;
-    uint32_t lo[C][2], hi[C][2];
-#pragma unroll
-    for (int cc = 0; cc < C; ++cc) {
-#pragma unroll
-      for (int dy = 0; dy < 2; ++dy) {
-        const uint32_t* r = reinterpret_cast<const uint32_t*>(rows + (cc * 2 + dy) * rs + (base & ~3));
-        const uint32_t w0 = r[0], w1 = r[1], w2 = r[2];
-        lo[cc][dy] = __funnelshift_r(w0, w1, sh);
-        hi[cc][dy] = __funnelshift_r(w1, w2, sh);
-      }
-    }
-    // word (ch * 2 + dy) * 2 + half = input columns 2j-4+4*half .. +3 of
-    // row 2i+dy of channel ch; words 4C..15 are zero
-    uint32_t o[16];
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const int cc = q >> 2, dy = (q >> 1) & 1;
-      o[q] = q < 4 * C ? ((q & 1) ? hi[cc < C ? cc : 0][dy] : lo[cc < C ? cc : 0][dy]) : 0u;
-    }
-    const int32_t swz = (j >> 1) & 3;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      *reinterpret_cast<uint4*>(tile + j * 64 + 16 * (k ^ swz)) =
-          make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-    }
-  }
-  __syncthreads();
-
+  // 16-byte chunk k of pixel j = words 4k .. 4k+3 = channel k: input
+  // columns 2j-4 .. 2j+3 of rows 2i and 2i+1 (zero for k >= C).  Consecutive
+  // threads write consecutive chunks: coalesced 16-byte stores.
   uint4* out = reinterpret_cast<uint4*>(y + ((img * ho + i) * static_cast<int64_t>(wo)) * 64);
-  for (int q = threadIdx.x; q < wo * 4; q += blockDim.x) {
-    const int32_t p = q >> 2, k = q & 3;
-    out[q] = *reinterpret_cast<const uint4*>(tile + p * 64 + 16 * (k ^ ((p >> 1) & 3)));
+  for (int t = threadIdx.x; t < wo * 4; t += blockDim.x) {
+    const int32_t j = t >> 2, k = t & 3;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (k < C) {
+      // columns 2j-4 .. 2j+3 start at byte kStemMargin - 4 + 2j (even)
+      const int32_t base = kStemMargin - 4 + 2 * j;
+      const uint32_t sh = (base & 3) * 8;
+      const uint32_t* r0 = reinterpret_cast<const uint32_t*>(rows + (k * 2) * rs + (base & ~3));
+      const uint32_t* r1 = reinterpret_cast<const uint32_t*>(rows + (k * 2 + 1) * rs + (base & ~3));
+      v.x = __funnelshift_r(r0[0], r0[1], sh);
+      v.y = __funnelshift_r(r0[1], r0[2], sh);
+      v.z = __funnelshift_r(r1[0], r1[1], sh);
+      v.w = __funnelshift_r(r1[1], r1[2], sh);
+    }
+    out[t] = v;
   }
 }
 
