@@ -1072,9 +1072,80 @@ ie::Status CudaPool2DOp::forward_q8(const ie::Tensor& x, std::vector<ie::Tensor*
   return deliver(*yc, logical, x.dtype, context, outputs, st);
 }
 
+ie::Status CudaGlobalAvgPoolOp::configure(const ie::Attrs& attrs) {
+  has_scale_ = false;
+  x_scale_ = 0.0;
+  x_zero_point_ = 0;
+  if (auto st = read_double(attrs, "x_scale", &has_scale_, &x_scale_); !st.has_value()) return st;
+  if (has_scale_ && !(x_scale_ > 0.0 && std::isfinite(x_scale_))) {
+    return ie::Error::invalid_argument("GlobalAvgPool x_scale must be positive and finite");
+  }
+  bool found = false;
+  if (auto st = read_int(attrs, "x_zero_point", &found, &x_zero_point_); !st.has_value()) return st;
+  if (found && (x_zero_point_ < -128 || x_zero_point_ > 255)) {
+    return ie::Error::invalid_argument("GlobalAvgPool x_zero_point out of the 8-bit range");
+  }
+  return {};
+}
+
+ie::Status CudaGlobalAvgPoolOp::forward_q8(const ie::Tensor& x, std::vector<ie::Tensor*>& outputs,
+                                          ie::ExecutionContext& context) {
+  if (outputs.size() != 1 || outputs[0] == nullptr) {
+    return ie::Error::invalid_argument("GlobalAvgPool expects one input and one output");
+  }
+  if (context.allocator == nullptr) return ie::Error::invalid_argument("GlobalAvgPool requires an allocator");
+  if (x.buffer == nullptr) return ie::Error::invalid_argument("null tensor or buffer");
+  if (!has_scale_) {
+    return ie::Error::invalid_argument("GlobalAvgPool of an int8 activation needs \"x_scale\"");
+  }
+  const bool is_signed = x.dtype == ie::DType::I8;
+  if ((is_signed && x_zero_point_ > 127) || (!is_signed && x_zero_point_ < 0)) {
+    return ie::Error::invalid_argument("GlobalAvgPool x_zero_point outside the input's storage type");
+  }
+  const auto& dm = x.shape.dims;
+  if (dm.size() != 4) return ie::Error::invalid_argument("GlobalAvgPool expects 4D NCHW tensors");
+  for (int64_t v : dm) {
+    if (v <= 0) return ie::Error::invalid_argument("GlobalAvgPool expects positive dimensions");
+  }
+  const bool x_nhwc = x.layout == ie::Layout::NHWC;
+  if (x_nhwc && x.device != ie::Device::CUDA) {
+    return ie::Error::invalid_argument("an NHWC int8 activation must be a device tensor");
+  }
+  if (auto st = require_device(); !st.has_value()) return st;
+  cudaStream_t st = static_cast<cudaStream_t>(context.stream);
+  const int64_t n = dm[0], c = dm[1], h = dm[2], w = dm[3];
+  const int64_t c_store = (c + 15) / 16 * 16;
+  auto xd = to_device(dev_, kSlotX, x, st);
+  if (!xd.has_value()) return xd.error();
+  const void* xn = *xd;
+  if (!x_nhwc) {
+    auto packed = dev_.scratch(kSlotXPacked, static_cast<size_t>(n * h * w * c_store));
+    if (!packed.has_value()) return packed.error();
+    if (auto e = to_status(ie_cuda_q8_pack_input(*xd, *packed, n, c, h, w, c_store, 0, st));
+        !e.has_value()) {
+      return e;
+    }
+    xn = *packed;
+  }
+  auto ydev = dev_.scratch(kSlotY, static_cast<size_t>(n * c) * sizeof(float));
+  if (!ydev.has_value()) return ydev.error();
+  if (auto e = to_status(ie_cuda_q8_global_avg_pool_nhwc(xn, static_cast<float*>(*ydev), n, c, h, w,
+                                                         is_signed ? 1 : 0,
+                                                         static_cast<int32_t>(x_zero_point_),
+                                                         x_scale_, st));
+      !e.has_value()) {
+    return e;
+  }
+  return download_f32(*ydev, ie::Shape{{n, c, 1, 1}}, context, outputs, st);
+}
+
 ie::Status CudaGlobalAvgPoolOp::forward(const std::vector<ie::Tensor*>& inputs,
                                         std::vector<ie::Tensor*>& outputs,
                                         ie::ExecutionContext& context) {
+  if (inputs.size() == 1 && inputs[0] != nullptr &&
+      (inputs[0]->dtype == ie::DType::U8 || inputs[0]->dtype == ie::DType::I8)) {
+    return forward_q8(*inputs[0], outputs, context);
+  }
   if (auto st = validate_unary(inputs, outputs, context, "GlobalAvgPool"); !st.has_value()) return st;
   if (auto st = require_device(); !st.has_value()) return st;
   const ie::Tensor& x = *inputs[0];

@@ -233,12 +233,24 @@ class CudaPool2DOp final : public ie::Op {
 };
 
 // Replaces GlobalAvgPoolOp (pool_ops.h:71-79): [N, C, H, W] -> [N, C, 1, 1].
+// An int8 input (U8 / I8: NCHW, or the int8 activation layout in device mode)
+// is the head of a quantized graph: the node carries "x_scale" and
+// "x_zero_point" (0 when absent) and the output is the fp32 mean of the
+// dequantized values, fp32((sum q - zp * h * w) * x_scale / (h * w))
+// (ie_cuda_q8_global_avg_pool_nhwc), ready for the fp32 Gemm after it.
 class CudaGlobalAvgPoolOp final : public ie::Op {
  public:
+  ie::Status configure(const ie::Attrs& attrs) override;
   ie::Status forward(const std::vector<ie::Tensor*>& inputs, std::vector<ie::Tensor*>& outputs,
                      ie::ExecutionContext& context) override;
 
  private:
+  ie::Status forward_q8(const ie::Tensor& x, std::vector<ie::Tensor*>& outputs,
+                        ie::ExecutionContext& context);
+
+  bool has_scale_ = false;
+  double x_scale_ = 0.0;
+  int64_t x_zero_point_ = 0;
   DeviceBuffers dev_;
 };
 

@@ -310,6 +310,89 @@ std::unique_ptr<QGraph> make_q8_block_graph(int64_t c = 32, int64_t mid = 16) {
   return qg;
 }
 
+// A whole quantized network, stem to logits: int8 stem Conv2D 7x7 / 2 (input
+// zero point 128) -> MaxPool 3x3 / 2 -> bottleneck (1x1 -> 3x3 -> 1x1, the
+// last with zero point 128 and no ReLU) + int8 shortcut Add with ReLU ->
+// GlobalAvgPool of the int8 activation into fp32 -> Flatten -> fp32 Gemm.
+std::unique_ptr<QGraph> make_q8_net_graph() {
+  auto qg = std::make_unique<QGraph>();
+  ie::Graph& g = qg->g;
+  Lcg rng(53);
+  ie::ValueId next = 0;
+  auto value = [&](const std::string& name, bool in = false, bool out = false) {
+    ie::Value v;
+    v.id = next++;
+    v.name = name;
+    v.is_input = in;
+    v.is_output = out;
+    g.values.push_back(v);
+    return v.id;
+  };
+  auto tensor = [&](const std::string& name, std::vector<int64_t> dims, ie::DType dt) {
+    qg->keep.push_back(std::make_unique<HostTensor>(dims, dt));
+    HostTensor& t = *qg->keep.back();
+    for (int64_t i = 0; i < t.t.numel(); ++i) {
+      if (dt == ie::DType::I8) {
+        t.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+      } else {
+        t.data<float>()[i] = rng.uniform(-0.5f, 0.5f);
+      }
+    }
+    g.weights.emplace(name, t.t);
+    return value(name);
+  };
+  auto qattrs = [&](int64_t m, double mlo, double mhi, int64_t zp_x, int64_t zp_y, int64_t qmin,
+                    int64_t pad, int64_t stride) {
+    std::vector<double> mult(static_cast<size_t>(m));
+    std::vector<int64_t> bias(static_cast<size_t>(m));
+    for (int64_t i = 0; i < m; ++i) {
+      mult[static_cast<size_t>(i)] = static_cast<double>(static_cast<float>(mlo + (mhi - mlo) * rng.uniform(0.f, 1.f)));
+      bias[static_cast<size_t>(i)] = static_cast<int64_t>(rng.next() % 2001) - 1000;
+    }
+    qg->mult.push_back(mult);
+    qg->bias.push_back(bias);
+    return ie::Attrs{{"multiplier", mult}, {"bias", bias}, {"x_zero_point", zp_x},
+                     {"y_zero_point", zp_y}, {"qmin", qmin}, {"qmax", int64_t{255}},
+                     {"pads", std::vector<int64_t>{pad, pad, pad, pad}},
+                     {"strides", std::vector<int64_t>{stride, stride}}};
+  };
+  auto node = [&](ie::OpType op, std::vector<ie::ValueId> in, ie::ValueId out, ie::Attrs attrs = {}) {
+    ie::Node n;
+    n.id = static_cast<ie::NodeId>(g.nodes.size());
+    n.op = op;
+    n.inputs = std::move(in);
+    n.outputs = {out};
+    n.attrs = std::move(attrs);
+    g.nodes.push_back(n);
+  };
+  const ie::ValueId x = value("x", true);
+  const ie::ValueId w0 = tensor("nw0", {16, 3, 7, 7}, ie::DType::I8);
+  const ie::ValueId w1 = tensor("nw1", {8, 16, 1, 1}, ie::DType::I8);
+  const ie::ValueId w2 = tensor("nw2", {8, 8, 3, 3}, ie::DType::I8);
+  const ie::ValueId w3 = tensor("nw3", {16, 8, 1, 1}, ie::DType::I8);
+  const ie::ValueId wfc = tensor("nfcw", {10, 16}, ie::DType::F32);
+  const ie::ValueId bfc = tensor("nfcb", {10}, ie::DType::F32);
+  const ie::ValueId s0 = value("ns0"), pl = value("npool"), c1 = value("nc1"), c2 = value("nc2"),
+                    c3 = value("nc3"), sum = value("nsum"), gp = value("ngap"), fl = value("nflat");
+  const ie::ValueId y = value("ny", false, true);
+  node(ie::OpType::Conv2D, {x, w0}, s0, qattrs(16, 0.002, 0.004, 128, 0, 0, 3, 2));
+  node(ie::OpType::MaxPool2D, {s0}, pl,
+       {{"kernel_shape", std::vector<int64_t>{3, 3}}, {"strides", std::vector<int64_t>{2, 2}},
+        {"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+  node(ie::OpType::Conv2D, {pl, w1}, c1, qattrs(8, 0.004, 0.008, 0, 0, 0, 0, 1));
+  node(ie::OpType::Conv2D, {c1, w2}, c2, qattrs(8, 0.002, 0.004, 0, 0, 0, 1, 1));
+  node(ie::OpType::Conv2D, {c2, w3}, c3, qattrs(16, 0.004, 0.008, 0, 128, 0, 0, 1));
+  node(ie::OpType::Add, {c3, pl}, sum,
+       {{"a_multiplier", std::vector<double>{0.5}}, {"b_multiplier", std::vector<double>{0.75}},
+        {"a_zero_point", int64_t{128}}, {"b_zero_point", int64_t{0}},
+        {"y_zero_point", int64_t{0}}, {"qmin", int64_t{0}}});
+  node(ie::OpType::GlobalAvgPool, {sum}, gp, {{"x_scale", 0.05}, {"x_zero_point", int64_t{0}}});
+  node(ie::OpType::Flatten, {gp}, fl);
+  node(ie::OpType::Gemm, {fl, wfc, bfc}, y, {{"transB", int64_t{1}}});
+  return qg;
+}
+
+
 // ------------------------------------------------------------ cpu checks
 
 int run_cpu() {
@@ -809,6 +892,39 @@ int run_gpu(const std::string& dir) {
       dump(dir, manifest, ("q8g_bias" + std::to_string(l + 1)).c_str(), bt.t);
     }
     dump(dir, manifest, "q8g_y", (*r1)[0]);
+  }
+  // a whole quantized network through CudaExecutor: int8 from the stem to the
+  // GlobalAvgPool, fp32 logits from the Gemm
+  {
+    auto qn = make_q8_net_graph();
+    HostTensor x({2, 3, 32, 32}, ie::DType::U8);
+    Lcg rng(59);
+    for (int64_t i = 0; i < x.t.numel(); ++i) x.data<uint8_t>()[i] = static_cast<uint8_t>(rng.next() % 256);
+    ie_b200::CudaExecutor exec(reg);
+    std::unordered_map<std::string, ie::Tensor> in{{"x", x.t}};
+    auto r = exec.run(qn->g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r.has_value() && r->size() == 1, "Q8NET: run");
+    if (!r.has_value()) {
+      std::printf("  %s\n", r.error().message.c_str());
+      return 4;
+    }
+    expect((*r)[0].shape.dims == std::vector<int64_t>{2, 10} && (*r)[0].dtype == ie::DType::F32,
+           "Q8NET: fp32 logits [2, 10]");
+    dump(dir, manifest, "q8n_x", x.t);
+    for (const char* k : {"nw0", "nw1", "nw2", "nw3", "nfcw", "nfcb"}) {
+      dump(dir, manifest, (std::string("q8n_") + k).c_str(), qn->g.weights.at(k));
+    }
+    for (size_t l = 0; l < 4; ++l) {
+      const int64_t m = static_cast<int64_t>(qn->mult[l].size());
+      HostTensor mt({m}, ie::DType::F32), bt({m}, ie::DType::F32);
+      for (int64_t i = 0; i < m; ++i) {
+        mt.data<float>()[i] = static_cast<float>(qn->mult[l][static_cast<size_t>(i)]);
+        bt.data<float>()[i] = static_cast<float>(qn->bias[l][static_cast<size_t>(i)]);
+      }
+      dump(dir, manifest, ("q8n_mult" + std::to_string(l)).c_str(), mt.t);
+      dump(dir, manifest, ("q8n_bias" + std::to_string(l)).c_str(), bt.t);
+    }
+    dump(dir, manifest, "q8n_y", (*r)[0]);
   }
   // conv + BN + shortcut add + Relu fused, run with a residual input
   {

@@ -1441,6 +1441,33 @@ int ie_cuda_global_avg_pool_f32(const float* x, float* y, int64_t n, int64_t c, 
   return check_launch("global_avg_pool_f32");
 }
 
+int ie_cuda_q8_global_avg_pool_nhwc(const void* x, float* y, int64_t n, int64_t c, int64_t h,
+                                    int64_t w, int32_t is_signed, int32_t zp, double scale,
+                                    void* stream) {
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) {
+    return fail(IE_INVALID_ARGUMENT, "GlobalAvgPool expects positive dimensions");
+  }
+  int rc;
+  if ((rc = check_ptr(x, "x", 16)) != IE_OK) return rc;
+  if (y == nullptr) return fail(IE_INVALID_ARGUMENT, "null tensor");
+  const int64_t c_store = round_up(c, 16);
+  if (h * w > INT32_MAX / 255 || n > INT32_MAX || c_store > INT32_MAX) {
+    return fail(IE_UNSUPPORTED, "GlobalAvgPool plane too large for the int32 sums");
+  }
+  const int64_t warps = n * (c_store / 16);
+  const auto xp = static_cast<const uint8_t*>(x);
+  if (is_signed) {
+    q8_global_avg_pool_nhwc<true><<<grid_1d(warps * 32, 256), 256, 0, as_stream(stream)>>>(
+        xp, y, static_cast<int32_t>(n), static_cast<int32_t>(c), static_cast<int32_t>(c_store),
+        h * w, zp, scale);
+  } else {
+    q8_global_avg_pool_nhwc<false><<<grid_1d(warps * 32, 256), 256, 0, as_stream(stream)>>>(
+        xp, y, static_cast<int32_t>(n), static_cast<int32_t>(c), static_cast<int32_t>(c_store),
+        h * w, zp, scale);
+  }
+  return check_launch("q8_global_avg_pool_nhwc");
+}
+
 namespace {
 
 // 1x1 convolution view of a Gemm: M "pixels" of K channels against N filters.

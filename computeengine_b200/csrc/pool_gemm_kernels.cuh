@@ -76,6 +76,51 @@ __global__ void global_avg_pool_f32(const float* __restrict__ x, float* __restri
   }
 }
 
+// Global average pooling of 8-bit NHWC activations (c_store channels per
+// pixel) into dequantized fp32: y[img, ch] = fp32((sum_p q - zp * hw) * scale
+// / hw), the sum exact in int32 and the rest in double, rounded once.  One
+// warp per (image, 16-channel group): lanes stride over the pixels with
+// 16-byte loads, then the 16 per-channel sums are reduced across the warp.
+// hw * 255 must fit int32 (the host checks).
+template <bool kSigned>
+__global__ void q8_global_avg_pool_nhwc(const uint8_t* __restrict__ x, float* __restrict__ y,
+                                        int32_t n, int32_t c, int32_t c_store, int64_t hw,
+                                        int32_t zp, double scale) {
+  const int32_t groups = c_store >> 4;
+  const int64_t warp_id = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= static_cast<int64_t>(n) * groups) return;
+  const int32_t img = static_cast<int32_t>(warp_id / groups);
+  const int32_t g = static_cast<int32_t>(warp_id - static_cast<int64_t>(img) * groups);
+  const uint8_t* base = x + static_cast<int64_t>(img) * hw * c_store + g * 16;
+  int32_t s[16] = {};
+  for (int64_t p = lane; p < hw; p += 32) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + p * c_store));
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t byte = (w4[i] >> (8 * b)) & 0xFFu;
+        s[4 * i + b] += kSigned ? static_cast<int32_t>(static_cast<int8_t>(byte))
+                                : static_cast<int32_t>(byte);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) s[k] = __reduce_add_sync(0xFFFFFFFFu, s[k]);
+  if (lane < 16) {
+    const int32_t ch = g * 16 + lane;
+    int32_t mine = s[0];
+#pragma unroll
+    for (int k = 1; k < 16; ++k) mine = lane == k ? s[k] : mine;
+    if (ch < c) {
+      const double centered = static_cast<double>(mine) - static_cast<double>(zp) * static_cast<double>(hw);
+      y[static_cast<int64_t>(img) * c + ch] = __double2float_rn(centered * scale / static_cast<double>(hw));
+    }
+  }
+}
+
 // C broadcast modes of the Gemm bias (gemm_op.cpp:103-139).
 enum : int32_t { kGemmCNone = 0, kGemmCScalar = 1, kGemmCRow = 2, kGemmCColumn = 3, kGemmCFull = 4 };
 

@@ -389,6 +389,18 @@ int ie_cuda_q8_maxpool2d_nhwc(const ie_pool2d_desc* desc, int32_t is_signed, con
 int ie_cuda_global_avg_pool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h,
                                 int64_t w, void* stream);
 
+/* Global average pooling of an 8-bit activation into dequantized fp32: the
+ * GlobalAvgPool node at the head of a quantized graph, ahead of the fp32 Gemm
+ * (the reference GlobalAvgPoolOp is fp32-only; this rule is the backend's
+ * own).  x [n, h, w, c_store] (c_store = round_up(c, 16), the int8 activation
+ * layout), y [n, c] fp32:
+ *   y = fp32((sum over the plane of q - zp * h * w) * scale / (h * w))
+ * with the sum exact in integers and the rest in double, rounded once.
+ * h * w * 255 must fit int32 (IE_UNSUPPORTED otherwise). */
+int ie_cuda_q8_global_avg_pool_nhwc(const void* x, float* y, int64_t n, int64_t c, int64_t h,
+                                    int64_t w, int32_t is_signed, int32_t zp, double scale,
+                                    void* stream);
+
 /* C broadcast of Gemm (gemm_op.cpp:103-139). */
 enum {
   IE_GEMM_C_NONE = 0,   /* no C */

@@ -80,6 +80,38 @@ def test_cpp_q8_block_graph_device_resident(oracle, refconv, tmp_path):
     np.testing.assert_array_equal(t["q8g_y"], want.astype(np.uint8))
 
 
+def test_cpp_q8_network_to_logits(oracle, refconv, tmp_path):
+    """A whole quantized network through CudaExecutor: int8 stem Conv2D 7x7 /
+    2 (input zero point 128) -> int8 MaxPool -> bottleneck + int8 shortcut Add
+    -> GlobalAvgPool of the int8 activation into fp32 -> Flatten -> Gemm.  The
+    int8 part is recomputed with the oracle and the reference pool, the
+    GlobalAvgPool by its rule (exact integer sum, double arithmetic, one fp32
+    rounding), the Gemm by the reference GemmOp; logits within 1e-3 * max |ref|
+    (the Gemm runs as bf16x3)."""
+    r = subprocess.run([str(driver()), "gpu", str(tmp_path)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    t = read_dump(tmp_path)
+    x = t["q8n_x"]
+    p = [(t[f"q8n_nw{i}"], t[f"q8n_bias{i}"].astype(np.int32), t[f"q8n_mult{i}"]) for i in range(4)]
+    s0 = oracle.conv2d_q8(x, *p[0], 128, 0, 0, 255, strides=(2, 2), pads=(3, 3, 3, 3))
+    rc, pool = refconv.pool2d(s0.astype(np.float32), (3, 3), (2, 2), (1, 1, 1, 1), kind="max")
+    assert rc == 0
+    pool = pool.astype(np.uint8)
+    c1 = oracle.conv2d_q8(pool, *p[1], 0, 0, 0, 255)
+    c2 = oracle.conv2d_q8(c1, *p[2], 0, 0, 0, 255, pads=(1, 1, 1, 1))
+    c3 = oracle.conv2d_q8(c2, *p[3], 0, 128, 0, 255)
+    sm = oracle.qadd(c3, 128, np.float32(0.5), pool, 0, np.float32(0.75), 0, 0, 255)
+    assert len(np.unique(sm)) > 16
+    hw = sm.shape[2] * sm.shape[3]
+    gap = (sm.astype(np.int64).sum(axis=(2, 3)).astype(np.float64) * np.float64(0.05)
+           / np.float64(hw)).astype(np.float32)
+    rc, want = refconv.gemm(gap, t["q8n_nfcw"], t["q8n_nfcb"], trans_b=1)
+    assert rc == 0
+    err = float(np.abs(t["q8n_y"] - want).max())
+    assert err <= REL_TOL * float(np.abs(want).max()), err
+
+
 def test_cpp_head_ops_match_reference(refconv, tmp_path):
     """MaxPool2D, AvgPool2D (ceil_mode, count_include_pad), GlobalAvgPool and
     Gemm (transB, bias) through the registry against the reference's own ops:

@@ -125,6 +125,35 @@ def test_global_avg_pool_bit_exact(refconv, shape):
     np.testing.assert_array_equal(y.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("shape,signed,zp,scale", [
+    ((4, 2048, 7, 7), False, 0, 0.05),   # the ResNet-50 head
+    ((2, 40, 7, 7), True, -3, 0.031),    # int8, channels not a multiple of 16
+    ((1, 16, 56, 56), False, 131, 0.2),  # a large plane: lanes stride over 3136 pixels
+])
+def test_q8_global_avg_pool_rule(shape, signed, zp, scale):
+    """int8 GlobalAvgPool into fp32: fp32((sum q - zp * hw) * scale / hw), the
+    sum exact, the rest in double rounded once -- equal bit for bit."""
+    import torch
+    from computeengine_b200 import _lib as L
+    n, c, h, w = shape
+    rng = np.random.default_rng(c + h)
+    dt = np.int8 if signed else np.uint8
+    lo, hi = (-128, 128) if signed else (0, 256)
+    x = rng.integers(lo, hi, shape).astype(dt)
+    cs = (c + 15) // 16 * 16
+    xn = np.full((n, h, w, cs), 0x7F, np.uint8)
+    xn[..., :c] = x.view(np.uint8).transpose(0, 2, 3, 1)
+    xd = torch.from_numpy(xn).cuda()
+    y = torch.full((n, c), float("nan"), device="cuda")
+    L.check(L.lib.ie_cuda_q8_global_avg_pool_nhwc(xd.data_ptr(), y.data_ptr(), n, c, h, w,
+                                                   int(signed), zp, scale, None))
+    torch.cuda.synchronize()
+    hw = h * w
+    want = ((x.astype(np.int64).sum(axis=(2, 3)).astype(np.float64) - np.float64(zp) * hw)
+            * np.float64(scale) / np.float64(hw)).astype(np.float32)
+    np.testing.assert_array_equal(y.cpu().numpy(), want)
+
+
 C_MODE = {"none": 0, "scalar": 1, "row": 2, "column": 3, "full": 4}
 
 GEMMS = [
