@@ -1,6 +1,6 @@
 // Inline-PTX building blocks for the sm_100a kernels: mbarriers with bounded
-// waits, TMA tensor loads (tiled and im2col, never with cluster multicast),
-// and the tcgen05 tensor-core / tensor-memory instructions.
+// waits, TMA tensor loads (tiled and im2col; each CTA loads only into its own
+// shared memory), and the tcgen05 tensor-core / tensor-memory instructions.
 #pragma once
 
 #include <cuda.h>
