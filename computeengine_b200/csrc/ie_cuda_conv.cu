@@ -271,17 +271,20 @@ struct TilePlan {
   int grid = 0;
   double est = 0.0;
   double mma_cycles = 0.0;  // estimated MMA time of one tile
+  int64_t ck = 0;           // channels per tap in the packed weights
 };
 
 // Builds the plan for tiles of bn output channels x 128 * m_sub positions.
 // Returns false when no pipeline of that shape fits in shared memory.
 //
 // The estimate: the CTAs of a persistent grid each run ceil(tiles / CTAs)
-// tiles; a tile costs its 32-byte K steps times the measured cycles of one
-// 128-row MMA step at that width (the shared-memory operand rate bounds N=64
-// and N=128, the tensor pipe N=256: ~68, ~91 and ~137 cycles), its outputs at
-// the epilogue's ~11.7 per cycle per SM, and ~1000 cycles of hand-offs; a
-// CTA with resident weights first loads its bn x K slice at ~64 B/cycle.
+// tiles; a tile costs its 32-byte K steps times the cycles of one 128-row MMA
+// step at that width -- int8: the shared-memory operand rate bounds N=64 and
+// N=128, the tensor pipe N=256 (~68, ~91 and ~137 cycles, measured); bf16x3
+// (three products per step): the tensor pipe N=128 and N=256 (~203, ~406),
+// the operand rate N=64 (~133) -- its outputs at the epilogue's ~11.7 per
+// cycle per SM, and ~1000 cycles of hand-offs; a CTA with resident weights
+// first loads its bn x K slice at ~64 B/cycle.
 bool plan_tiles(const ie_conv2d_desc* d, const ie_conv2d_shape& s, bool i8, int elem_bytes,
                 int64_t x_c_store, bool allow_halo, int bn, int m_sub, int sms, TilePlan* p) {
   *p = TilePlan{};
@@ -376,7 +379,9 @@ bool plan_tiles(const ie_conv2d_desc* d, const ie_conv2d_shape& s, bool i8, int 
     waves = ceil_div(p->m_tiles * p->n_tiles, static_cast<int64_t>(p->grid));
   }
   const double k_steps = static_cast<double>(num_k) * (v.bkb / 32.0);
-  const double mma = v.bn <= 64 ? 68.0 : (v.bn <= 128 ? 91.0 : 137.0);
+  const double mma = i8 ? (v.bn <= 64 ? 68.0 : (v.bn <= 128 ? 91.0 : 137.0))
+                       : (v.bn <= 64 ? 133.0 : (v.bn <= 128 ? 203.0 : 406.0));
+  p->ck = cblocks * bk_elems;
   const double rows = 128.0 * v.m_sub;
   p->mma_cycles = k_steps * mma * v.m_sub;
   const double t_tile = p->mma_cycles + rows * v.bn / 11.7 + 1000.0;
@@ -390,15 +395,17 @@ bool plan_tiles(const ie_conv2d_desc* d, const ie_conv2d_shape& s, bool i8, int 
 //   allow_halo: the caller's output goes through the staged TMA store (int8
 //   requantized), so the row-band mode may be used
 //
-// The int8 path considers narrower or shorter tiles beside the default (the
-// widest channel tile that wastes least, 256 positions below 256 channels):
+// Narrower or shorter tiles are considered beside the default (the widest
+// channel tile that wastes least; int8: 256 positions below 256 channels):
 // a launch whose default tiles cannot fill the GPU and carry at least ~2000
 // cycles of MMA work each takes the plan with the smallest estimate when that
 // is at least 10% below the default's.  Shallower launches keep the default:
 // they are bound by launch and pipeline latency, and a narrow grid leaves
 // SMs to the next launch's prologue (measured: MobileNetV2's K = 160-192 1x1
 // layers at batch 64 ran 13-16% slower on twice the CTAs).  The packed int8
-// weights do not depend on the tile shape.
+// weights do not depend on the tile shape; the packed bf16x3 weights do only
+// through the channel-block rounding, so an fp32 candidate must keep the
+// default's channels per tap.
 int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_bytes,
                 int64_t x_c_store, const void* x, const void* packed, IgemmSetup* out,
                 bool allow_halo = false) {
@@ -421,16 +428,17 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
   if (!plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, bn0, ms0, sms, &plan)) {
     return fail(IE_UNSUPPORTED, "no pipeline fits in shared memory");
   }
-  if (i8 && plan.grid < sms && plan.mma_cycles >= 2000.0 &&
+  if (plan.grid < sms && plan.mma_cycles >= 2000.0 &&
       g_tile_policy.load(std::memory_order_relaxed) == IE_TILE_FILL) {
     const double limit = 0.9 * plan.est;
     const int cand[][2] = {{bn0, 1}, {128, 1}, {64, 2}, {64, 1}};
     TilePlan best = plan;
     for (const auto& c : cand) {
       if (c[0] > bn0 || (c[0] == bn0 && c[1] == ms0)) continue;
+      if (!i8 && c[1] != 1) continue;  // the bf16x3 kernel runs 128-position tiles
       TilePlan t;
       if (plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, c[0], c[1], sms, &t) &&
-          t.est < limit && t.est < best.est) {
+          (i8 || t.ck == plan.ck) && t.est < limit && t.est < best.est) {
         best = t;
       }
     }

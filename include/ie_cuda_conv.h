@@ -441,15 +441,17 @@ typedef struct {
 } ie_conv_plan;
 int ie_cuda_last_plan(ie_conv_plan* out);
 
-/* Tile choice of the int8 implicit GEMM, process-wide (performance control;
- * no counterpart in the reference).  Every plan gives the same bytes.
+/* Tile choice of the implicit GEMM (int8 and bf16x3), process-wide
+ * (performance control; no counterpart in the reference).  Every plan gives
+ * the same results: the int8 bytes, and for fp32 the same products summed in
+ * the same K order.
  *   IE_TILE_FILL     (default) a launch whose default tiles cannot fill the
  *                    GPU and carry enough MMA work each (deep K) takes
  *                    narrower (64 / 128 channel) or shorter (128 position)
  *                    tiles when a cycle estimate says they finish at least
  *                    10% sooner
  *   IE_TILE_DEFAULT  always the default tiles: the widest channel tile that
- *                    wastes least, 256 positions below 256 channels
+ *                    wastes least (int8: 256 positions below 256 channels)
  * *previous (may be NULL) receives the policy that was in force. */
 enum { IE_TILE_FILL = 0, IE_TILE_DEFAULT = 1 };
 int ie_cuda_set_tile_policy(int32_t policy, int32_t* previous);

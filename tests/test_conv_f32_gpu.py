@@ -86,3 +86,28 @@ def test_config1_against_reference_conv(refconv):
     got = run_f32(x, wt, b, pads=(1, 1, 1, 1))
     err = np.abs(got - want).max()
     assert err <= REL_TOL * np.abs(want).max(), err
+
+
+def test_f32_tile_policy_same_results(oracle):
+    """An fp32 layer whose default tiles leave most SMs idle (deep K, small
+    batch) takes narrower 128-position tiles under the fill policy; the
+    products and their K order are the same, so both policies give the same
+    floats, within tolerance of the oracle."""
+    from computeengine_b200 import _lib as L
+    from tests.qconv import tile_policy
+    rng = np.random.default_rng(5)
+    n, c, h, w, m = 2, 256, 14, 14, 256
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * 9)), (m, c, 3, 3)).astype(np.float32)
+    b = rng.normal(0, 0.01, m).astype(np.float32)
+    with tile_policy(L.IE_TILE_DEFAULT):
+        ref = run_f32(x, wt, b, act=1, pads=(1, 1, 1, 1))
+        plan_d = L.last_plan()
+    with tile_policy(L.IE_TILE_FILL):
+        got = run_f32(x, wt, b, act=1, pads=(1, 1, 1, 1))
+        plan_f = L.last_plan()
+    assert plan_d.bn == 256 and plan_d.grid < 148
+    assert plan_f.bn < plan_d.bn and plan_f.grid > plan_d.grid
+    np.testing.assert_array_equal(got, ref)
+    want = oracle.conv2d_f32(x, wt, b, act=1, pads=(1, 1, 1, 1), nthreads=8)
+    assert np.abs(got - want).max() <= REL_TOL * np.abs(want).max()
