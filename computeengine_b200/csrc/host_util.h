@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -17,6 +18,20 @@ namespace ie_cuda {
 
 inline thread_local std::string g_last_error;
 inline thread_local uint64_t g_launches = 0;
+
+// Stream (+1; 0 = none) whose last launch by this library packed weights.
+// The implicit-GEMM kernel reads resident weights before it waits on the
+// kernel launched before it (programmatic dependent launch), which is sound
+// only when that kernel did not write them; a convolution launched right
+// after a weight-packing launch on the same stream therefore goes without
+// the overlap.  Every other launch clears the mark (check_launch).
+inline std::atomic<uintptr_t> g_packed_weights_stream{0};
+
+inline uintptr_t stream_key(cudaStream_t s) { return reinterpret_cast<uintptr_t>(s) + 1; }
+
+inline void mark_weights_packed(cudaStream_t s) {
+  g_packed_weights_stream.store(stream_key(s), std::memory_order_relaxed);
+}
 
 inline int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -30,6 +45,7 @@ inline int fail(int code, const char* fmt, ...) {
 
 inline int check_launch(const char* what) {
   ++g_launches;
+  g_packed_weights_stream.store(0, std::memory_order_relaxed);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     return fail(IE_RUNTIME, "%s: %s", what, cudaGetErrorString(e));

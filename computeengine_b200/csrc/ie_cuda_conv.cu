@@ -179,7 +179,9 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // right after this stream's weights were packed: plain stream order, so the
+  // resident-weight loads issued before griddepcontrol.wait see them
+  cfg.numAttrs = g_packed_weights_stream.load(std::memory_order_relaxed) == stream_key(st) ? 0 : 1;
   const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, ta, tb, ty, args);
   if (le != cudaSuccess) {
     ++g_launches;
@@ -783,7 +785,9 @@ int ie_cuda_q8_pack_weights(const ie_conv2d_desc* desc, const int8_t* w, void* p
       w, static_cast<int8_t*>(packed), static_cast<int32_t>(desc->m),
       static_cast<int32_t>(desc->c), static_cast<int32_t>(taps), static_cast<int32_t>(ck));
   if ((rc = check_launch("pack_weights_q8")) != IE_OK) return rc;
-  return q8_write_weight_sums(desc, packed, as_stream(stream));
+  if ((rc = q8_write_weight_sums(desc, packed, as_stream(stream))) != IE_OK) return rc;
+  mark_weights_packed(as_stream(stream));
+  return IE_OK;
 }
 
 int ie_cuda_q8_pack_input(const void* x_nchw, void* x_nhwc, int64_t n, int64_t c, int64_t h,
@@ -1070,7 +1074,9 @@ int ie_cuda_q8_stem_pack_weights(const int8_t* w, void* packed, int64_t m, int64
   if (rc != IE_OK) return rc;
   ie_conv2d_desc d;
   if ((rc = ie_cuda_q8_stem_desc(1, c, 2, 2, m, &d)) != IE_OK) return rc;
-  return q8_write_weight_sums(&d, packed, as_stream(stream));
+  if ((rc = q8_write_weight_sums(&d, packed, as_stream(stream))) != IE_OK) return rc;
+  mark_weights_packed(as_stream(stream));
+  return IE_OK;
 }
 
 namespace {
