@@ -86,6 +86,7 @@ def test_depthwise_signed_output_general_zero_point(oracle):
     ((0.25, 0.9), 0, 0, 255, False),       # shifts <= 32: exact per-column requantize
     ((0.001, 0.01), 0, -128, 127, True),    # zp_y > qmin: sign-corrected rounding
     ((0.001, 0.01), 3, 3, 100, False),      # folded addend with a narrower clamp
+    ((0.001, 0.01), 0, 0, 255, False),      # folded addend, the saturating pack alone clamps
 ])
 def test_depthwise_requantize_modes(oracle, mult_range, zp_y, qmin, qmax, y_signed):
     rng = np.random.default_rng(17)
