@@ -646,6 +646,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
         cpu_reference_stack(1, 1)  # untimed: page-in, thread start-up
+        t1, _, _, _ = cpu_reference_stack(1, 1)  # one image on one thread
         dt, passes = 0.0, 0
         while dt < 10.0 and passes < 30:  # about 10 s of host work
             t, kind, cores, rk = cpu_reference_stack(threads, threads)
@@ -655,7 +656,10 @@ def run_ours(args, world, rank, local):
                "kind": kind,
                "sample": f"{passes} passes of {threads} images through the 53-conv stack, "
                          f"one image per thread ({rk} row kernel, {cpu_model()})",
-               "images_per_s": threads * passes / dt}
+               "images_per_s": threads * passes / dt,
+               "single_thread": {"value": ops_img / t1 / 1e12, "unit": "TOPS",
+                                 "images_per_s": 1.0 / t1},
+               "host_threads": os.cpu_count(), "cpu_model": cpu_model()}
 
     if rank != 0:
         return
