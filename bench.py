@@ -25,6 +25,7 @@ K steps take about REFERENCE_ARM_BUDGET_S of host time.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -663,6 +664,11 @@ def run_ours(args, world, rank, local):
 
     if rank != 0:
         return
+    # this GPU's own int8 tensor-core rate (back-to-back tcgen05.mma kind::i8,
+    # M=128 N=256 K=32, every SM), after every timed region
+    i8_peak = ctypes.c_double()
+    L.check(L.lib.ie_cuda_mma_i8_peak(40000, ctypes.byref(i8_peak),
+                                      torch.cuda.current_stream(dev).cuda_stream))
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     workloads = None
@@ -719,6 +725,11 @@ def run_ours(args, world, rank, local):
                                "launches of itself (events on the replay stream); achieved = "
                                "ops of the 53 convs / the sum of their launch times",
                      "frac_of_nominal_int8_4500": achieved / 4500.0,
+                     "measured_int8_peak": i8_peak.value,
+                     "frac_of_measured_int8_peak": achieved / i8_peak.value,
+                     "measured_int8_peak_source": "ie_cuda_mma_i8_peak: 40000 back-to-back "
+                                                  "tcgen05.mma kind::i8 M=128 N=256 K=32 per "
+                                                  "SM, this GPU, this run",
                      "layer_us": {k: round(v * 1e3, 2) for k, v in net.layer_ms.items()}},
         "clocks": clocks.summary(),
     }

@@ -118,6 +118,7 @@ def _load() -> C.CDLL:
         "ie_cuda_pool2d_f32": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
         "ie_cuda_q8_maxpool2d_nhwc": (C.c_int, [P(PoolDesc), _i32, _p, _p, _p]),
         "ie_cuda_set_tile_policy": (C.c_int, [_i32, P(_i32)]),
+        "ie_cuda_mma_i8_peak": (C.c_int, [_i32, P(C.c_double), _p]),
         "ie_cuda_q8_global_avg_pool_nhwc": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _i32, _i32,
                                                       C.c_double, _p]),
         "ie_cuda_global_avg_pool_f32": (C.c_int, [_p, _p, _i64, _i64, _i64, _i64, _p]),

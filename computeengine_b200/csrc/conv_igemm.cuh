@@ -48,6 +48,7 @@ enum : unsigned int {
   kErrWaitWeights = 0x105,
   kErrWaitOutFull = 0x106,
   kErrWaitOutFree = 0x107,
+  kErrWaitPeak = 0x108,   // mma_i8_peak's final wait
   kErrWaitProbe = 0x1FF,  // the bounded-wait self-test (bounded_wait_probe)
 };
 
@@ -1029,6 +1030,53 @@ __global__ void __launch_bounds__(64, 1) bounded_wait_probe(uint64_t limit_ns, u
     tc_fence_after();
     __syncwarp();
     tmem_dealloc(tmem_slot, 32);
+  }
+}
+
+// Rate of the int8 tensor cores on this GPU: every CTA (one per SM) issues
+// `iters` back-to-back tcgen05.mma kind::i8 of M=128, N=256, K=32 from one
+// thread into one tensor-memory accumulator, its operands a zeroed 128 x 32 B
+// A and 256 x 32 B B tile in shared memory (32-byte rows, 32-byte swizzle: the
+// operand form the implicit GEMM uses for 32-byte channel blocks).  One
+// commit, a bounded wait for it, then the accumulator is freed.  The host
+// times the launch: 2 * 128 * 256 * 32 * iters ops per CTA.
+__global__ void __launch_bounds__(128, 1) mma_i8_peak(uint32_t iters, uint64_t wait_limit_ns) {
+  __shared__ __align__(1024) uint8_t ops[128 * 32 + 256 * 32];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < static_cast<int>(sizeof(ops) / 16); i += blockDim.x) {
+    reinterpret_cast<uint4*>(ops)[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  fence_proxy_async_smem();  // the zeroed operands -> visible to the tensor core
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) {
+    const uint64_t a = make_smem_desc(smem_u32(ops), 16, 8 * 32, swizzle_layout_code(32));
+    const uint64_t b = make_smem_desc(smem_u32(ops + 128 * 32), 16, 8 * 32, swizzle_layout_code(32));
+    constexpr uint32_t kIdesc = make_idesc_i8(128, 256, false, true);
+    for (uint32_t i = 0; i < iters; ++i) mma_i8(tmem, a, b, kIdesc, i != 0 ? 1u : 0u);
+    tc_commit(&bar);
+    mbar_wait(&bar, 0, &abort_flag, kErrWaitPeak, wait_limit_ns);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    __syncwarp();
+    tmem_dealloc(tmem, 256);
   }
 }
 

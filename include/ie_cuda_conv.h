@@ -341,6 +341,14 @@ int ie_cuda_bounded_wait_probe(uint64_t wait_limit_ns, uint64_t* waited_ns, void
  * since the last reset (for the benchmark's launch count). */
 uint64_t ie_cuda_launch_count(int reset);
 
+/* Measured int8 tensor-core rate of the current GPU (no counterpart in the
+ * reference; the denominator for int8 roofline fractions): one CTA per SM
+ * issues `iters` back-to-back tcgen05.mma kind::i8, M=128 N=256 K=32, from
+ * shared memory into tensor memory; *tops = 2 * 128 * 256 * 32 * iters * SMs
+ * / the launch's event time, in TOPS.  Synchronizes the stream.  iters in
+ * [1000, 1e7] (40000 takes a few ms). */
+int ie_cuda_mma_i8_peak(int32_t iters, double* tops, void* stream);
+
 /* ---------------------------------------------------------------- head ops
  * The rest of a ResNet graph's head on the GPU, so no node falls back to the
  * host: 2D pooling, global average pooling and Gemm over fp32 tensors. */

@@ -113,3 +113,12 @@ def test_tile_policy_values():
         assert L.set_tile_policy(L.IE_TILE_FILL) == L.IE_TILE_DEFAULT
     finally:
         L.set_tile_policy(prev)
+
+
+def test_mma_peak_rejects_bad_arguments():
+    """ie_cuda_mma_i8_peak checks its arguments before any CUDA call."""
+    import ctypes
+    from computeengine_b200 import _lib as L
+    out = ctypes.c_double()
+    assert L.lib.ie_cuda_mma_i8_peak(5, ctypes.byref(out), None) == L.IE_INVALID_ARGUMENT
+    assert L.lib.ie_cuda_mma_i8_peak(40000, None, None) == L.IE_INVALID_ARGUMENT
