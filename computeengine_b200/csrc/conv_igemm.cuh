@@ -219,11 +219,14 @@ struct EpiQ8 {
 template <int kMode, bool kS8, bool kClamp, int kCols, int kRows, int kPanelW>
 __device__ __forceinline__ void epi_q8_tile(uint32_t t_q, uint8_t* s_tile, int row0, int col0,
                                             const EpiQ8& e, uint64_t* acce) {
-  static_assert(kPanelW == 128 || kPanelW == 64, "staging panel width");
+  static_assert(kPanelW == 128 || kPanelW == 64 || kPanelW == 32, "staging panel width");
   const int q4 = e.lane & 3, r8 = e.lane >> 2;
-  // TMA's 128 B (64 B) swizzle XORs the 16-byte chunk index with row % 8
-  // ((row / 2) % 4); the rows row0 + 8i + r8 this thread writes all share it.
-  const uint32_t xr = kPanelW == 128 ? (r8 << 4) : (((r8 >> 1) & 3) << 4);
+  // TMA's 128 B (64 B, 32 B) swizzle XORs the 16-byte chunk index with
+  // row % 8 ((row / 2) % 4, (row / 4) % 2); the rows row0 + 8i + r8 this
+  // thread writes all share it.
+  const uint32_t xr = kPanelW == 128  ? (r8 << 4)
+                      : kPanelW == 64 ? (((r8 >> 1) & 3) << 4)
+                                      : (((r8 >> 2) & 1) << 4);
   uint32_t lo_part[4];  // column-within-32 part of the swizzled offset
 #pragma unroll
   for (int j = 0; j < 4; ++j) lo_part[j] = (8 * j + 2 * q4) ^ (xr & 0x10u);

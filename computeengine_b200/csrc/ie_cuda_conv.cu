@@ -203,20 +203,25 @@ LaunchFn pick_bn_bk(int m_sub, bool b_res) {
     // layer than twice the warps.
     if constexpr (BN <= 128) {
       // 256 positions per tile by default; 128 where the default tiles cannot
-      // fill the GPU
+      // fill the GPU (not for 32 channels: 8 epilogue warps need 32 columns
+      // each, so that tile always has two sub-tiles)
       if (m_sub == 2) {
         return b_res ? launch_variant<BN, BKB, 8, 2, true, I8, AS>
                      : launch_variant<BN, BKB, 8, 2, false, I8, AS>;
       }
-      return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
-                   : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
+      if constexpr (BN >= 64) {
+        return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
+                     : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
+      } else {
+        return nullptr;
+      }
     } else {
       return b_res ? launch_variant<BN, BKB, 8, 1, true, I8, AS>
                    : launch_variant<BN, BKB, 8, 1, false, I8, AS>;
     }
   } else {
     if (m_sub != 1 || b_res) return nullptr;
-    if constexpr (BN >= 256 && BKB > 64) {
+    if constexpr (BN < 64 || (BN >= 256 && BKB > 64)) {
       return nullptr;
     } else {
       return launch_variant<BN, BKB, (BN >= 256 ? 8 : 4), 1, false, I8, AS>;
@@ -228,6 +233,7 @@ template <bool I8, bool AS>
 LaunchFn pick_launch(const Variant& v) {
 #define IE_CASE(BN_, BK_) \
   if (v.bn == BN_ && v.bkb == BK_) return pick_bn_bk<BN_, BK_, I8, AS>(v.m_sub, v.b_res);
+  IE_CASE(32, 32) IE_CASE(32, 64) IE_CASE(32, 128)
   IE_CASE(64, 32) IE_CASE(64, 64) IE_CASE(64, 128)
   IE_CASE(128, 32) IE_CASE(128, 64) IE_CASE(128, 128)
   IE_CASE(256, 32) IE_CASE(256, 64) IE_CASE(256, 128)
@@ -381,7 +387,7 @@ bool plan_tiles(const ie_conv2d_desc* d, const ie_conv2d_shape& s, bool i8, int 
     waves = ceil_div(p->m_tiles * p->n_tiles, static_cast<int64_t>(p->grid));
   }
   const double k_steps = static_cast<double>(num_k) * (v.bkb / 32.0);
-  const double mma = i8 ? (v.bn <= 64 ? 68.0 : (v.bn <= 128 ? 91.0 : 137.0))
+  const double mma = i8 ? (v.bn <= 32 ? 52.0 : v.bn <= 64 ? 68.0 : (v.bn <= 128 ? 91.0 : 137.0))
                        : (v.bn <= 64 ? 133.0 : (v.bn <= 128 ? 203.0 : 406.0));
   p->ck = cblocks * bk_elems;
   const double rows = 128.0 * v.m_sub;
@@ -424,7 +430,9 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
     }
   }
   const int sms = num_sms();
-  const int bn0 = choose_bn(d->m);
+  // int8 layers of at most 32 channels (MobileNet's narrow projections) run
+  // 32-channel tiles instead of 64-channel ones that are half padding
+  const int bn0 = (i8 && d->m <= 32) ? 32 : choose_bn(d->m);
   const int ms0 = (i8 && bn0 <= 128) ? 2 : 1;
   TilePlan plan;
   if (!plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, bn0, ms0, sms, &plan)) {
@@ -438,6 +446,7 @@ int setup_igemm(const ie_conv2d_desc* d, const ie_conv2d_shape& s, int elem_byte
     for (const auto& c : cand) {
       if (c[0] > bn0 || (c[0] == bn0 && c[1] == ms0)) continue;
       if (!i8 && c[1] != 1) continue;  // the bf16x3 kernel runs 128-position tiles
+      if (c[0] == 32 && c[1] == 1) continue;  // 32-channel tiles need two sub-tiles
       TilePlan t;
       if (plan_tiles(d, s, i8, elem_bytes, x_c_store, allow_halo, c[0], c[1], sms, &t) &&
           (i8 || t.ck == plan.ck) && t.est < limit && t.est < best.est) {

@@ -73,3 +73,19 @@ def test_full_launch_keeps_default_tiles(oracle):
     plan = _run(oracle, case, L.IE_TILE_FILL)
     assert (plan.bn, plan.m_sub) == (64, 2) and plan.grid == 148
 
+
+
+@pytest.mark.parametrize("case", [
+    (4, 32, 56, 56, 16, 1, 1, (1, 1), (0, 0, 0, 0), 128, False),  # MobileNetV2 b00 projection shape
+    (2, 64, 30, 30, 24, 3, 3, (1, 1), (1, 1, 1, 1), 128, False),  # row band, 24 channels
+    (3, 96, 15, 13, 32, 3, 3, (2, 2), (1, 1, 1, 1), 37, True),    # stride 2, haloed input, int8 output
+], ids=_ids)
+def test_narrow_layers_run_32_channel_tiles(oracle, case):
+    """int8 layers of at most 32 output channels run 32-channel tiles (two
+    128-position sub-tiles, 32-byte staging panels with the 32-byte TMA
+    swizzle) instead of 64-channel tiles that are half padding; bit-exact."""
+    from computeengine_b200 import _lib as L
+    plan = _run(oracle, case, L.IE_TILE_DEFAULT)
+    assert (plan.bn, plan.m_sub) == (32, 2)
+    fill = _run(oracle, case, L.IE_TILE_FILL)
+    assert fill.bn == 32
