@@ -469,6 +469,26 @@ def cpu_workloads(threads: int, stack_tops: float = None) -> dict:
     return out
 
 
+def engine_resnet50_q8(batch: int = 256, iters: int = 20, warmup: int = 3) -> dict:
+    """The int8 ResNet-50 as one engine graph (the 53 convolutions, the max
+    pool, the 16 int8 shortcut Adds, the int8 GAP, the FC) run through the C++
+    CudaExecutor -- the reference Executor's interface -- with host tensors in
+    and out: per run the pinned upload of the uint8 batch, every node launched
+    from its op's forward(), the logits downloaded, one synchronize.  Timed by
+    the host clock around the synchronous calls in the backend's test driver
+    (a separate process on the same GPU); its check that one image alone gives
+    the batch's first row of logits is part of the line."""
+    from computeengine_b200.build import BACKEND_TEST
+    out = subprocess.run([str(BACKEND_TEST), "engine-bench", str(batch), str(iters), str(warmup)],
+                         capture_output=True, text=True, timeout=600)
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    r = json.loads(lines[-1]) if lines else {"error": (out.stderr or out.stdout)[-300:]}
+    r["returncode"] = out.returncode
+    r["workload"] = ("int8 ResNet-50 graph (53 convs, max pool, 16 int8 Adds, GAP, FC) through "
+                     "CudaExecutor::run, host tensors in and out")
+    return r
+
+
 def gpu_workloads(peaks: dict) -> dict:
     """Configs 1-4 on this GPU (CUDA events on the launching stream, after
     warm-up), each with its roofline fraction and the denominator it uses."""
@@ -480,7 +500,9 @@ def gpu_workloads(peaks: dict) -> dict:
     r1, r2 = c12[1], c12[2]
     f3 = resnet.bench_f32(32, iters=20)
     m4 = mobilenet.benchmark(64, 50)
+    engine = engine_resnet50_q8()
     return {
+        "engine": engine,
         "1": {"workload": r1["workload"], "value": r1["gflops"] / 1e3, "unit": "TFLOP/s",
               "us_per_call": r1["us"], "dtype": "f32 (bf16x3)",
               "e2e": {"value": 2 * 64 * 64 * 9 * 56 * 56 / r1["e2e_us"] / 1e6, "unit": "TFLOP/s",

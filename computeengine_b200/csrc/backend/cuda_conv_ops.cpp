@@ -627,6 +627,17 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     return ie::Error::unsupported("grouped int8 convolution (1 < group < C)");
   }
   if (auto st = require_device(); !st.has_value()) return st;
+  // A ResNet stem (7x7 / 2, pad 3, at most 4 channels, even extent) over an
+  // NCHW input with zero point 0 after the re-basing above runs as its
+  // space-to-depth equivalent: a 4x1 stride-1 layer over 64 stored channels
+  // (ie_cuda_q8_stem_*), bit-identical to the direct 7x7 / 2 convolution.
+  ie_conv2d_desc stem_d;
+  const bool stem = !depthwise && !x_nhwc && !halo && q.zp_x == 0 && d.kh == 7 && d.kw == 7 &&
+                    d.stride_h == 2 && d.stride_w == 2 && d.dil_h == 1 && d.dil_w == 1 &&
+                    s.pad_top == 3 && s.pad_left == 3 && s.pad_bottom == 3 && s.pad_right == 3 &&
+                    d.c <= 4 && d.h % 2 == 0 && d.w % 2 == 0 &&
+                    ie_cuda_q8_stem_desc(d.n, d.c, d.h, d.w, d.m, &stem_d) == IE_OK;
+  const ie_conv2d_desc& kd = stem ? stem_d : d;  // the layer the kernel runs
 
   cudaStream_t st = static_cast<cudaStream_t>(context.stream);
   const int64_t c_store = (d.c + 15) / 16 * 16, m_store = (d.m + 15) / 16 * 16;
@@ -645,18 +656,21 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   } else {
     auto xd = to_device(dev_, kSlotX, x, st);
     if (!xd.has_value()) return xd.error();
-    auto xn = dev_.scratch(kSlotXPacked, halo ? ie_cuda_q8_halo_input_bytes(&d)
-                                               : static_cast<size_t>(d.n * d.h * d.w * c_store));
+    const size_t xn_bytes = halo ? ie_cuda_q8_halo_input_bytes(&d)
+                            : stem ? static_cast<size_t>(kd.n * kd.h * kd.w * kd.c)
+                                   : static_cast<size_t>(d.n * d.h * d.w * c_store);
+    auto xn = dev_.scratch(kSlotXPacked, xn_bytes);
     if (!xn.has_value()) return xn.error();
-    const int prc = halo ? ie_cuda_q8_pack_input_halo(&d, *xd, *xn, q.zp_x, st)
-                         : ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st);
+    const int prc = halo   ? ie_cuda_q8_pack_input_halo(&d, *xd, *xn, q.zp_x, st)
+                    : stem ? ie_cuda_q8_stem_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, xor_mask, st)
+                           : ie_cuda_q8_pack_input(*xd, *xn, d.n, d.c, d.h, d.w, c_store, xor_mask, st);
     if (auto e = to_status(prc); !e.has_value()) return e;
     xin = *xn;
   }
   // packed weights, bias and multipliers: uploaded once per host buffer
   bool fresh = false;
   const size_t wbytes = depthwise ? ie_cuda_dw_q8_packed_weight_bytes(&d)
-                                  : ie_cuda_q8_packed_weight_bytes(&d);
+                                  : ie_cuda_q8_packed_weight_bytes(&kd);
   auto wp = dev_.cached(w.buffer, wbytes, kCacheWPacked, &fresh);
   if (!wp.has_value()) return wp.error();
   if (fresh) {
@@ -671,8 +685,10 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
       }
       wsrc = *tmp;
     }
-    const int rc = depthwise ? ie_cuda_dw_q8_pack_weights(&d, static_cast<const int8_t*>(wsrc), *wp, st)
-                             : ie_cuda_q8_pack_weights(&d, static_cast<const int8_t*>(wsrc), *wp, st);
+    const int8_t* w8 = static_cast<const int8_t*>(wsrc);
+    const int rc = depthwise ? ie_cuda_dw_q8_pack_weights(&d, w8, *wp, st)
+                   : stem    ? ie_cuda_q8_stem_pack_weights(w8, *wp, d.m, d.c, st)
+                             : ie_cuda_q8_pack_weights(&d, w8, *wp, st);
     if (auto e = to_status(rc); !e.has_value()) return e;
   }
   auto md = dev_.cached(mult_.data(), mult_.size() * sizeof(float), kCacheMult, &fresh);
@@ -719,7 +735,7 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   }
   const int rc = depthwise
                      ? ie_cuda_dwconv2d_q8(&d, &q, xin, *wp, bd, static_cast<const float*>(*md), yn, st)
-                     : ie_cuda_conv2d_q8(&d, &q, xin, *wp, bd, static_cast<const float*>(*md), yn, st);
+                     : ie_cuda_conv2d_q8(&kd, &q, xin, *wp, bd, static_cast<const float*>(*md), yn, st);
   if (auto e = to_status(rc); !e.has_value()) return e;
   if (dev_out) {
     *outputs[0] = std::move(*dev_out);

@@ -43,9 +43,44 @@ ie::Result<ie::Tensor> flatten(const ie::Tensor& x, const ie::Attrs& attrs) {
 
 }  // namespace
 
+CudaDeviceAllocator::~CudaDeviceAllocator() {
+  if (pool_ != nullptr) cudaMemPoolDestroy(static_cast<cudaMemPool_t>(pool_));
+}
+
 ie::Result<ie::BufferHandle> CudaDeviceAllocator::alloc(std::size_t bytes, ie::MemoryKind) {
+  if (pool_ == nullptr) {
+    int dev = 0;
+    if (auto st = cuda_check(cudaGetDevice(&dev), "cudaGetDevice"); !st.has_value()) {
+      cudaGetLastError();
+      return st.error();
+    }
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (auto st = cuda_check(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate"); !st.has_value()) {
+      cudaGetLastError();
+      return st.error();
+    }
+    // keep freed memory in the pool across synchronizations
+    uint64_t keep = ~uint64_t{0};
+    if (auto st = cuda_check(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
+                             "cudaMemPoolSetAttribute");
+        !st.has_value()) {
+      cudaGetLastError();
+      cudaMemPoolDestroy(pool);
+      return st.error();
+    }
+    pool_ = pool;
+  }
   void* p = nullptr;
-  if (auto st = cuda_check(cudaMalloc(&p, bytes == 0 ? 256 : bytes), "cudaMalloc"); !st.has_value()) {
+  if (auto st = cuda_check(cudaMallocFromPoolAsync(&p, bytes == 0 ? 256 : bytes,
+                                                   static_cast<cudaMemPool_t>(pool_),
+                                                   static_cast<cudaStream_t>(stream_)),
+                           "cudaMallocFromPoolAsync");
+      !st.has_value()) {
     cudaGetLastError();
     return st.error();
   }
@@ -53,7 +88,18 @@ ie::Result<ie::BufferHandle> CudaDeviceAllocator::alloc(std::size_t bytes, ie::M
 }
 
 void CudaDeviceAllocator::free(ie::BufferHandle handle) {
-  if (handle != nullptr) cudaFree(handle);
+  if (handle != nullptr) cudaFreeAsync(handle, static_cast<cudaStream_t>(stream_));
+}
+
+std::size_t CudaDeviceAllocator::reserved_bytes() const {
+  if (pool_ == nullptr) return 0;
+  uint64_t v = 0;
+  if (cudaMemPoolGetAttribute(static_cast<cudaMemPool_t>(pool_), cudaMemPoolAttrReservedMemCurrent, &v) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return static_cast<std::size_t>(v);
 }
 
 std::size_t CudaDeviceAllocator::available(ie::MemoryKind) const {
@@ -75,6 +121,7 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
     return ie::Error::runtime("no CUDA device: the CUDA executor has no CPU fallback");
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  device_alloc_->set_stream(stream);
   if (graph_ != &graph || ops_.size() != graph.nodes.size()) {
     ops_.clear();
     for (const ie::Node& node : graph.nodes) {
@@ -121,6 +168,18 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
     }
     values.emplace(v.id, std::move(*d));
   }
+  // the last node that reads each value; graph outputs are kept to the end
+  std::unordered_map<ie::ValueId, size_t> last_use;
+  for (size_t i = 0; i < graph.nodes.size(); ++i) {
+    for (ie::ValueId id : graph.nodes[i].inputs) last_use[id] = i;
+  }
+  for (const ie::Value& v : graph.values) {
+    if (v.is_output) last_use[v.id] = graph.nodes.size();
+  }
+  auto release_after = [&](size_t i, ie::ValueId id) {
+    auto it = last_use.find(id);
+    if (it == last_use.end() || it->second == i) values.erase(id);
+  };
   ie::ExecutionContext ctx;
   ctx.device = ie::Device::CUDA;
   ctx.allocator = device_alloc_;
@@ -140,6 +199,8 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
       auto y = flatten(*in_ptrs[0], node.attrs);
       if (!y.has_value()) return y.error();
       values.emplace(node.outputs[0], std::move(*y));
+      for (ie::ValueId id : node.inputs) release_after(i, id);
+      release_after(i, node.outputs[0]);
       continue;
     }
     std::vector<ie::Tensor> out_storage(node.outputs.size());
@@ -149,6 +210,9 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
     for (size_t k = 0; k < node.outputs.size(); ++k) {
       values.emplace(node.outputs[k], std::move(out_storage[k]));
     }
+    // stream-ordered frees: the memory is reused only by work queued later
+    for (ie::ValueId id : node.inputs) release_after(i, id);
+    for (ie::ValueId id : node.outputs) release_after(i, id);
   }
   std::vector<ie::Tensor> outputs;
   for (const ie::Value& v : graph.values) {
@@ -177,12 +241,6 @@ ie::Result<std::vector<ie::Tensor>> CudaExecutor::run(
     if (auto s = cuda_check(cudaMemcpyAsync(h->buffer, t->buffer, t->bytes(), kind, st), "cudaMemcpyAsync D2H");
         !s.has_value()) {
       return s.error();
-    }
-    if (nchw) {
-      // the temporary must outlive the copy
-      if (auto s = cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize"); !s.has_value()) {
-        return s.error();
-      }
     }
     outputs.push_back(std::move(*h));
   }

@@ -7,8 +7,11 @@
 // device mode (ExecutionContext::device = CUDA: inputs and outputs stay in
 // device memory, no per-node copy or synchronize), and copies the graph
 // outputs back into host tensors from `host_allocator`.  Flatten is a
-// zero-copy reshape.  One op instance per node is kept across runs of the
-// same graph object, so device copies of the weights are uploaded once.
+// zero-copy reshape.  Each intermediate value is released right after the
+// last node that reads it (stream-ordered, so the next node's output may
+// reuse its memory), so a run holds the live set of the graph, not the sum
+// of its values.  One op instance per node is kept across runs of the same
+// graph object, so device copies of the weights are uploaded once.
 // Nodes without a CUDA op (BatchNorm, a Relu / Add that was not fused, ...)
 // return Unsupported: run ConvBnReluFusionPass on the graph first.  A device
 // error (a bounded wait that timed out) returns Runtime.
@@ -26,13 +29,30 @@
 
 namespace ie_b200 {
 
-// cudaMalloc / cudaFree behind the engine's Allocator interface
-// (src/core/memory/allocator.h:10-22), for device-resident tensors.
+// Device-resident tensors behind the engine's Allocator interface
+// (src/core/memory/allocator.h:10-22): stream-ordered allocations
+// (cudaMallocFromPoolAsync / cudaFreeAsync on the executor's stream) from a
+// memory pool of its own that keeps freed memory reserved, so after the first
+// run of a graph its activations cost no driver allocation at all.  The pool
+// is created on the current device at the first allocation and destroyed with
+// the allocator (memory still in use is released when its last tensor is).
 class CudaDeviceAllocator final : public ie::Allocator {
  public:
+  CudaDeviceAllocator() = default;
+  CudaDeviceAllocator(const CudaDeviceAllocator&) = delete;
+  CudaDeviceAllocator& operator=(const CudaDeviceAllocator&) = delete;
+  ~CudaDeviceAllocator() override;
   ie::Result<ie::BufferHandle> alloc(std::size_t bytes, ie::MemoryKind kind) override;
   void free(ie::BufferHandle handle) override;
   std::size_t available(ie::MemoryKind kind) const override;
+  // the stream that orders allocations and frees (a cudaStream_t)
+  void set_stream(void* stream) { stream_ = stream; }
+  // bytes the pool holds from the device (in use + kept for reuse)
+  std::size_t reserved_bytes() const;
+
+ private:
+  void* pool_ = nullptr;    // cudaMemPool_t
+  void* stream_ = nullptr;  // cudaStream_t
 };
 
 class CudaExecutor {
@@ -48,6 +68,8 @@ class CudaExecutor {
                                           const std::unordered_map<std::string, ie::Tensor>& inputs,
                                           std::shared_ptr<ie::Allocator> host_allocator,
                                           void* stream = nullptr);
+  // device memory the executor's pool holds (the peak live set of the runs)
+  std::size_t reserved_device_bytes() const { return device_alloc_->reserved_bytes(); }
 
  private:
   OpFactory create_;

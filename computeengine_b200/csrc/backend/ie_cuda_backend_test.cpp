@@ -10,6 +10,10 @@
 //   ie_cuda_backend_test quant <dir> runs the int8 quantizer on seeded host
 //                                    tensors (no GPU) and writes its outputs
 //                                    for the Python side to check
+//   ie_cuda_backend_test engine-bench <batch> <iters> <warmup>
+//                                    times the int8 ResNet-50 graph through
+//                                    CudaExecutor with host tensors (one JSON
+//                                    line)
 //
 // The cases follow the reference's Conv2DOp tests
 // (tests/unit/traditional_ops_test.cpp:82-340): attribute errors are
@@ -17,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -391,6 +396,133 @@ std::unique_ptr<QGraph> make_q8_net_graph() {
   node(ie::OpType::Gemm, {fl, wfc, bfc}, y, {{"transB", int64_t{1}}});
   return qg;
 }
+
+
+// The whole int8 ResNet-50 v1.5 as one engine graph: the 7x7 / 2 stem (uint8
+// input, zero point 128), MaxPool 3x3 / 2, 16 bottlenecks (1x1 -> 3x3 -> 1x1,
+// stride on the 3x3, 1x1 projection on each stage's first block) with the
+// int8 shortcut Add + ReLU, the int8 GlobalAvgPool into fp32, Flatten and the
+// fp32 FC 2048 -> 1000.  The int8 scheme of the benchmark's convolution
+// stack: per-channel weights U{-127..127} with scales U(0.001, 0.01), int32
+// bias U{-1000..1000}, activation scale 0.05 (input 0.02), multiplier
+// fp32(s_x * s_w / s_y); ReLU outputs have zero point 0, the block's last
+// 1x1 and the projection (no ReLU before the Add) zero point 128.
+std::unique_ptr<QGraph> make_resnet50_q8_graph() {
+  auto qg = std::make_unique<QGraph>();
+  ie::Graph& g = qg->g;
+  Lcg rng(50);
+  ie::ValueId next = 0;
+  auto value = [&](const std::string& name, bool in = false, bool out = false) {
+    ie::Value v;
+    v.id = next++;
+    v.name = name;
+    v.is_input = in;
+    v.is_output = out;
+    g.values.push_back(v);
+    return v.id;
+  };
+  auto node = [&](ie::OpType op, std::vector<ie::ValueId> in, ie::ValueId out, ie::Attrs attrs = {}) {
+    ie::Node n;
+    n.id = static_cast<ie::NodeId>(g.nodes.size());
+    n.op = op;
+    n.inputs = std::move(in);
+    n.outputs = {out};
+    n.attrs = std::move(attrs);
+    g.nodes.push_back(n);
+  };
+  constexpr double kAct = 0.05, kIn = 0.02;
+  int conv_id = 0;
+  // a quantized Conv2D node; returns its output value
+  auto conv = [&](ie::ValueId x, int64_t cin, int64_t cout, int64_t k, int64_t stride, double s_x,
+                  int64_t zp_x, bool relu) {
+    const std::string name = "c" + std::to_string(conv_id++);
+    qg->keep.push_back(std::make_unique<HostTensor>(std::vector<int64_t>{cout, cin, k, k}, ie::DType::I8));
+    HostTensor& w = *qg->keep.back();
+    for (int64_t i = 0; i < w.t.numel(); ++i) {
+      w.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+    }
+    g.weights.emplace(name + "_w", w.t);
+    const ie::ValueId wv = value(name + "_w");
+    std::vector<double> mult(static_cast<size_t>(cout));
+    std::vector<int64_t> bias(static_cast<size_t>(cout));
+    for (int64_t i = 0; i < cout; ++i) {
+      const double s_w = 0.001 + 0.009 * rng.uniform(0.f, 1.f);
+      mult[static_cast<size_t>(i)] = static_cast<double>(static_cast<float>(s_x * s_w / kAct));
+      bias[static_cast<size_t>(i)] = static_cast<int64_t>(rng.next() % 2001) - 1000;
+    }
+    const int64_t pad = k / 2;
+    const ie::ValueId y = value(name);
+    node(ie::OpType::Conv2D, {x, wv}, y,
+         ie::Attrs{{"multiplier", mult}, {"bias", bias}, {"x_zero_point", zp_x},
+                   {"y_zero_point", int64_t{relu ? 0 : 128}}, {"qmin", int64_t{0}},
+                   {"qmax", int64_t{255}}, {"pads", std::vector<int64_t>{pad, pad, pad, pad}},
+                   {"strides", std::vector<int64_t>{stride, stride}}});
+    return y;
+  };
+  const ie::ValueId x = value("x", true);
+  ie::ValueId h = conv(x, 3, 64, 7, 2, kIn, 128, true);
+  const ie::ValueId pooled = value("pool");
+  node(ie::OpType::MaxPool2D, {h}, pooled,
+       {{"kernel_shape", std::vector<int64_t>{3, 3}}, {"strides", std::vector<int64_t>{2, 2}},
+        {"pads", std::vector<int64_t>{1, 1, 1, 1}}});
+  h = pooled;
+  int64_t cin = 64;
+  const int64_t widths[4] = {64, 128, 256, 512}, blocks[4] = {3, 4, 6, 3};
+  int add_id = 0;
+  for (int st = 0; st < 4; ++st) {
+    for (int64_t b = 0; b < blocks[st]; ++b) {
+      const int64_t wd = widths[st], stride = (st > 0 && b == 0) ? 2 : 1;
+      const ie::ValueId c1 = conv(h, cin, wd, 1, 1, kAct, 0, true);
+      const ie::ValueId c2 = conv(c1, wd, wd, 3, stride, kAct, 0, true);
+      const ie::ValueId c3 = conv(c2, wd, 4 * wd, 1, 1, kAct, 0, false);
+      ie::ValueId sc = h;
+      int64_t zp_sc = 0;
+      if (b == 0) {
+        sc = conv(h, cin, 4 * wd, 1, stride, kAct, 0, false);
+        zp_sc = 128;
+      }
+      const ie::ValueId sum = value("add" + std::to_string(add_id++));
+      node(ie::OpType::Add, {c3, sc}, sum,
+           {{"a_multiplier", std::vector<double>{1.0}}, {"b_multiplier", std::vector<double>{1.0}},
+            {"a_zero_point", int64_t{128}}, {"b_zero_point", zp_sc},
+            {"y_zero_point", int64_t{0}}, {"qmin", int64_t{0}}});
+      h = sum;
+      cin = 4 * wd;
+    }
+  }
+  const ie::ValueId gp = value("gap"), fl = value("flat"), y = value("logits", false, true);
+  node(ie::OpType::GlobalAvgPool, {h}, gp, {{"x_scale", kAct}, {"x_zero_point", int64_t{0}}});
+  node(ie::OpType::Flatten, {gp}, fl);
+  qg->keep.push_back(std::make_unique<HostTensor>(std::vector<int64_t>{1000, 2048}, ie::DType::F32));
+  HostTensor& fw = *qg->keep.back();
+  for (int64_t i = 0; i < fw.t.numel(); ++i) fw.data<float>()[i] = rng.uniform(-0.05f, 0.05f);
+  qg->keep.push_back(std::make_unique<HostTensor>(std::vector<int64_t>{1000}, ie::DType::F32));
+  HostTensor& fb = *qg->keep.back();
+  for (int64_t i = 0; i < fb.t.numel(); ++i) fb.data<float>()[i] = rng.uniform(-0.1f, 0.1f);
+  g.weights.emplace("fc_w", fw.t);
+  g.weights.emplace("fc_b", fb.t);
+  const ie::ValueId fwv = value("fc_w"), fbv = value("fc_b");
+  node(ie::OpType::Gemm, {fl, fwv, fbv}, y, {{"transB", int64_t{1}}});
+  return qg;
+}
+
+// Page-locked host memory behind the engine's Allocator interface, so the
+// executor's input upload and logits download run at full link speed.
+class PinnedAllocator final : public ie::Allocator {
+ public:
+  ie::Result<ie::BufferHandle> alloc(std::size_t bytes, ie::MemoryKind) override {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, bytes == 0 ? 1 : bytes, cudaHostAllocDefault) != cudaSuccess) {
+      cudaGetLastError();
+      return ie::Error::out_of_memory("cudaHostAlloc");
+    }
+    return p;
+  }
+  void free(ie::BufferHandle handle) override {
+    if (handle != nullptr) cudaFreeHost(handle);
+  }
+  std::size_t available(ie::MemoryKind) const override { return 0; }
+};
 
 
 // ------------------------------------------------------------ cpu checks
@@ -1199,12 +1331,88 @@ int run_quant(const std::string& dir) {
   return 0;
 }
 
+// The int8 ResNet-50 graph through CudaExecutor::run with host tensors in and
+// out (the call an engine makes per batch): per run the upload of the uint8
+// NCHW batch, 53 convolutions, the max pool, 16 int8 Adds, the int8 GAP, the
+// FC and the download of the logits, then one synchronize.  Times `iters`
+// runs after `warmup` with the host clock around the synchronous calls and
+// prints one JSON line.  Check: image 0 alone through the same executor gives
+// the batch's first row of logits (the int8 stages do not depend on the batch;
+// the FC may split K by batch size, so within 1e-5 of max|y|).
+int run_engine_bench(int64_t batch, int iters, int warmup) {
+  if (batch < 1 || iters < 1 || warmup < 0) return 2;
+  cudaStream_t stream;
+  if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return 3;
+  ie::OpRegistry reg;
+  if (!ie_b200::register_cuda_ops(reg).has_value()) return 2;
+  auto qg = make_resnet50_q8_graph();
+  auto pinned = std::make_shared<PinnedAllocator>();
+  auto x = ie::Tensor::allocate(ie::Shape{{batch, 3, 224, 224}}, ie::DType::U8, pinned);
+  auto x1 = ie::Tensor::allocate(ie::Shape{{1, 3, 224, 224}}, ie::DType::U8, pinned);
+  if (!x.has_value() || !x1.has_value()) return 3;
+  Lcg rng(224);
+  for (int64_t i = 0; i < x->numel(); ++i) x->data<uint8_t>()[i] = static_cast<uint8_t>(rng.next() >> 8);
+  std::memcpy(x1->buffer, x->buffer, x1->bytes());
+  ie_b200::CudaExecutor exec(reg);
+  auto run = [&](const ie::Tensor& in) {
+    std::unordered_map<std::string, ie::Tensor> inputs{{"x", in}};
+    return exec.run(qg->g, inputs, pinned, stream);
+  };
+  auto fail = [](const ie::Error& e) {
+    std::printf("{\"error\": \"%s\"}\n", e.message.c_str());
+    return 4;
+  };
+  for (int i = 0; i < warmup; ++i) {
+    auto r = run(*x);
+    if (!r.has_value()) return fail(r.error());
+  }
+  ie_cuda_launch_count(1);
+  const auto t0 = std::chrono::steady_clock::now();
+  std::vector<ie::Tensor> last;
+  for (int i = 0; i < iters; ++i) {
+    auto r = run(*x);
+    if (!r.has_value()) return fail(r.error());
+    last = std::move(*r);
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  const uint64_t launches = ie_cuda_launch_count(0);
+  const std::size_t reserved = exec.reserved_device_bytes();
+  auto one = run(*x1);
+  if (!one.has_value()) return fail(one.error());
+  const float* yb = static_cast<const float*>(last[0].buffer);
+  const float* y1 = static_cast<const float*>((*one)[0].buffer);
+  double ymax = 0.0, dmax = 0.0;
+  for (int64_t j = 0; j < 1000; ++j) {
+    ymax = std::max(ymax, std::fabs(static_cast<double>(yb[j])));
+    dmax = std::max(dmax, std::fabs(static_cast<double>(yb[j]) - y1[j]));
+  }
+  const bool ok = dmax <= 1e-5 * ymax;
+  const double ms = std::chrono::duration<double, std::milli>(t1 - t0).count() / iters;
+  const double conv_ops_img = 8.174e9;  // 2 x MACs of the 53 convolutions per image
+  std::printf("{\"batch\": %lld, \"iters\": %d, \"warmup\": %d, \"ms_per_run\": %.4f, "
+              "\"images_per_s\": %.1f, \"conv_tops\": %.2f, \"nodes\": %zu, "
+              "\"launches_per_run\": %.1f, \"h2d_bytes_per_run\": %zu, \"d2h_bytes_per_run\": %zu, "
+              "\"device_pool_reserved_bytes\": %zu, \"max_abs_logit\": %.6g, "
+              "\"batch1_max_abs_diff\": %.6g, \"batch1_ok\": %s}\n",
+              static_cast<long long>(batch), iters, warmup, ms, batch / (ms / 1e3),
+              conv_ops_img * batch / (ms / 1e3) / 1e12, qg->g.nodes.size(),
+              static_cast<double>(launches) / iters, x->bytes(), last[0].bytes(), reserved, ymax, dmax,
+              ok ? "true" : "false");
+  std::fflush(stdout);
+  cudaStreamDestroy(stream);
+  return ok ? 0 : 1;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
+  if (argc >= 5 && std::strcmp(argv[1], "engine-bench") == 0) {
+    return run_engine_bench(std::atoll(argv[2]), std::atoi(argv[3]), std::atoi(argv[4]));
+  }
   if (argc >= 2 && std::strcmp(argv[1], "cpu") == 0) return run_cpu();
   if (argc >= 3 && std::strcmp(argv[1], "gpu") == 0) return run_gpu(argv[2]);
   if (argc >= 3 && std::strcmp(argv[1], "quant") == 0) return run_quant(argv[2]);
-  std::fprintf(stderr, "usage: %s cpu | gpu <outdir> | quant <outdir>\n", argv[0]);
+  std::fprintf(stderr, "usage: %s cpu | gpu <outdir> | quant <outdir> | engine-bench <batch> <iters> <warmup>\n",
+               argv[0]);
   return 2;
 }

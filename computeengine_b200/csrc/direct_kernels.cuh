@@ -381,12 +381,31 @@ struct QAddArgs {
   int32_t a_signed, b_signed, y_signed;
 };
 
+// One term of the narrow (64-bit) form, and its rounding half away from zero,
+// zero point and clamp.
+__device__ __forceinline__ long long qadd_term64(int32_t x, int32_t zp, long long m, int32_t d) {
+  return (static_cast<long long>(x - zp) * m) << d;
+}
+__device__ __forceinline__ uint32_t qadd_round64(long long v, const QAddArgs& k) {
+  const long long r = (v + (1ll << (k.s - 1)) - (v < 0 ? 1 : 0)) >> k.s;
+  long long q = r + k.zp_y;
+  q = q < k.qmin ? k.qmin : (q > k.qmax ? k.qmax : q);
+  return static_cast<uint32_t>(q) & 0xFFu;
+}
+
+// kWide = false when both terms and their sum fit in 64 bits and the shift is
+// in [1, 62] (|x - zp| <= 255 < 2^8, significand < 2^31, da, db <= 22: each
+// term < 2^61); the host checks that before choosing it.
+template <bool kWide>
 __device__ __forceinline__ uint32_t qadd_one(uint32_t av, uint32_t bv, const QAddArgs& k) {
   const int32_t a = k.a_signed ? static_cast<int32_t>(static_cast<int8_t>(av)) : static_cast<int32_t>(av);
   const int32_t b = k.b_signed ? static_cast<int32_t>(static_cast<int8_t>(bv)) : static_cast<int32_t>(bv);
+  long long r;
+  if constexpr (!kWide) {
+    return qadd_round64(qadd_term64(a, k.zp_a, k.ma, k.da) + qadd_term64(b, k.zp_b, k.mb, k.db), k);
+  }
   const __int128 v = (static_cast<__int128>(static_cast<long long>(a - k.zp_a) * k.ma) << k.da) +
                      (static_cast<__int128>(static_cast<long long>(b - k.zp_b) * k.mb) << k.db);
-  long long r;
   if (k.s >= 127) {
     r = 0;
   } else if (k.s <= 0) {
@@ -402,6 +421,7 @@ __device__ __forceinline__ uint32_t qadd_one(uint32_t av, uint32_t bv, const QAd
 
 // 16 elements per thread when vec16 (pointers 16-byte aligned, count a
 // multiple of 16), else one.
+template <bool kWide>
 __global__ void __launch_bounds__(256) qadd_u8(const uint8_t* __restrict__ a,
                                                const uint8_t* __restrict__ b,
                                                uint8_t* __restrict__ y, QAddArgs k, int vec16) {
@@ -418,7 +438,7 @@ __global__ void __launch_bounds__(256) qadd_u8(const uint8_t* __restrict__ a,
         uint32_t o = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          o |= qadd_one((wa[q] >> (8 * i)) & 0xFFu, (wb[q] >> (8 * i)) & 0xFFu, k) << (8 * i);
+          o |= qadd_one<kWide>((wa[q] >> (8 * i)) & 0xFFu, (wb[q] >> (8 * i)) & 0xFFu, k) << (8 * i);
         }
         wy[q] = o;
       }
@@ -426,9 +446,78 @@ __global__ void __launch_bounds__(256) qadd_u8(const uint8_t* __restrict__ a,
     }
   } else {
     for (int64_t t = t0; t < k.count; t += stride) {
-      y[t] = static_cast<uint8_t>(qadd_one(__ldg(a + t), __ldg(b + t), k));
+      y[t] = static_cast<uint8_t>(qadd_one<kWide>(__ldg(a + t), __ldg(b + t), k));
     }
   }
+}
+
+// The same Add over large tensors through a table: the result depends only on
+// the two input bytes, so each block first fills a 64 KB shared-memory table
+// with the exact rule above (from the two 256-entry term tables in the 64-bit
+// form) and then maps 16 byte pairs per 16-byte load through it, two loads per
+// thread in flight.  One 1024-thread block per SM; the table costs a few
+// microseconds per launch.  The pair (a, b) sits at a * 256 + (b ^ ((a & 31)
+// << 2)): with the plain a * 256 + b every row starts in bank 0, so lanes that
+// share b (a ReLU output full of zeros) but differ in a would all hit one
+// bank; the XOR spreads them over the 32 banks.  Requires 16-byte aligned
+// pointers.
+__device__ __forceinline__ uint32_t qadd_lut_slot(uint32_t i) {
+  return i ^ ((i >> 6) & 0x007C007Cu);  // both 16-bit halves: b ^= (a & 31) << 2
+}
+
+__device__ __forceinline__ uint32_t qadd_lut4(uint32_t wa, uint32_t wb, const uint8_t* lut) {
+  // [b0 a0 b1 a1]: a0 * 256 + b0 | a1 * 256 + b1, then the bank swizzle
+  const uint32_t i01 = qadd_lut_slot(__byte_perm(wb, wa, 0x5140));
+  const uint32_t i23 = qadd_lut_slot(__byte_perm(wb, wa, 0x7362));
+  return static_cast<uint32_t>(lut[i01 & 0xFFFFu]) | (static_cast<uint32_t>(lut[i01 >> 16]) << 8) |
+         (static_cast<uint32_t>(lut[i23 & 0xFFFFu]) << 16) | (static_cast<uint32_t>(lut[i23 >> 16]) << 24);
+}
+
+__device__ __forceinline__ uint4 qadd_lut16(const uint4 va, const uint4 vb, const uint8_t* lut) {
+  return make_uint4(qadd_lut4(va.x, vb.x, lut), qadd_lut4(va.y, vb.y, lut), qadd_lut4(va.z, vb.z, lut),
+                    qadd_lut4(va.w, vb.w, lut));
+}
+
+constexpr int kQAddLutThreads = 1024;
+constexpr int kQAddLutBytes = 65536;
+
+template <bool kWide>
+__global__ void __launch_bounds__(kQAddLutThreads) qadd_lut_u8(const uint4* __restrict__ a,
+                                                               const uint4* __restrict__ b,
+                                                               uint4* __restrict__ y, QAddArgs k,
+                                                               int64_t chunks) {
+  extern __shared__ __align__(16) uint8_t lut[];
+  __shared__ long long ta[256], tb[256];
+  const int tid = threadIdx.x;
+  if constexpr (!kWide) {
+    if (tid < 256) {
+      const int32_t x = k.a_signed ? static_cast<int32_t>(static_cast<int8_t>(tid)) : tid;
+      ta[tid] = qadd_term64(x, k.zp_a, k.ma, k.da);
+    } else if (tid < 512) {
+      const int32_t x = k.b_signed ? static_cast<int32_t>(static_cast<int8_t>(tid - 256)) : tid - 256;
+      tb[tid - 256] = qadd_term64(x, k.zp_b, k.mb, k.db);
+    }
+    __syncthreads();
+    for (int i = tid; i < kQAddLutBytes; i += kQAddLutThreads) {
+      const int av = i >> 8, bv = (i & 255) ^ ((av & 31) << 2);  // the pair stored at slot i
+      lut[i] = static_cast<uint8_t>(qadd_round64(ta[av] + tb[bv], k));
+    }
+  } else {
+    for (int i = tid; i < kQAddLutBytes; i += kQAddLutThreads) {
+      const uint32_t av = static_cast<uint32_t>(i) >> 8, bv = (static_cast<uint32_t>(i) & 255u) ^ ((av & 31u) << 2);
+      lut[i] = static_cast<uint8_t>(qadd_one<true>(av, bv, k));
+    }
+  }
+  __syncthreads();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kQAddLutThreads;
+  int64_t t = static_cast<int64_t>(blockIdx.x) * kQAddLutThreads + tid;
+  for (; t + stride < chunks; t += 2 * stride) {
+    const uint4 a0 = __ldg(a + t), b0 = __ldg(b + t);
+    const uint4 a1 = __ldg(a + t + stride), b1 = __ldg(b + t + stride);
+    y[t] = qadd_lut16(a0, b0, lut);
+    y[t + stride] = qadd_lut16(a1, b1, lut);
+  }
+  if (t < chunks) y[t] = qadd_lut16(__ldg(a + t), __ldg(b + t), lut);
 }
 
 // depthwise int8 weights [c, 1, kh, kw] -> [kh*kw][c_store], zero filled.

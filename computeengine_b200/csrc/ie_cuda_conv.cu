@@ -1659,9 +1659,23 @@ int ie_cuda_qadd(const ie_qadd_params* p, const void* a, const void* b, void* y,
                    reinterpret_cast<uintptr_t>(b) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
   const int64_t work = vec ? count / 16 : count;
   const int blocks = static_cast<int>(std::min<int64_t>(ceil_div(work, 256), int64_t{num_sms()} * 16));
-  qadd_u8<<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const uint8_t*>(a),
-                                                 static_cast<const uint8_t*>(b),
-                                                 static_cast<uint8_t*>(y), k, vec ? 1 : 0);
+  // 64-bit arithmetic is exact when each term stays below 2^61 and the
+  // rounding shift is in [1, 62]
+  const bool narrow = k.da <= 22 && k.db <= 22 && k.s >= 1 && k.s <= 62;
+  if (vec && count >= (int64_t{1} << 22)) {
+    // large tensors: the 64 KB table per block pays for itself
+    auto lut_kern = narrow ? qadd_lut_u8<false> : qadd_lut_u8<true>;
+    cudaFuncSetAttribute(lut_kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kQAddLutBytes);
+    const int64_t chunks = count / 16;
+    const int lut_blocks = static_cast<int>(std::min<int64_t>(ceil_div(chunks, kQAddLutThreads), num_sms()));
+    lut_kern<<<lut_blocks, kQAddLutThreads, kQAddLutBytes, as_stream(stream)>>>(
+        static_cast<const uint4*>(a), static_cast<const uint4*>(b), static_cast<uint4*>(y), k, chunks);
+    return check_launch("qadd_lut_u8");
+  }
+  auto kern = narrow ? qadd_u8<false> : qadd_u8<true>;
+  kern<<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const uint8_t*>(a),
+                                             static_cast<const uint8_t*>(b),
+                                             static_cast<uint8_t*>(y), k, vec ? 1 : 0);
   return check_launch("qadd_u8");
 }
 
