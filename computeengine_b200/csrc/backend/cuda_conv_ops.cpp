@@ -276,7 +276,7 @@ ie::Status deliver(const void* ydev, ie::Shape shape, ie::DType dtype,
   return {};
 }
 
-enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork, kSlotResidual };
+enum Slot { kSlotX = 0, kSlotXPacked, kSlotY, kSlotYPacked, kSlotWork, kSlotResidual, kSlotWPacked };
 enum CacheKind { kCacheW = 0, kCacheWPacked, kCacheBias, kCacheMult, kCacheBiasI32 };
 
 }  // namespace
@@ -444,12 +444,22 @@ ie::Status CudaConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
   cudaStream_t st = static_cast<cudaStream_t>(context.stream);
   auto xd = to_device(dev_, kSlotX, x, st);
   if (!xd.has_value()) return xd.error();
-  // weights (and bias) stay on the device for the op's lifetime, keyed by the
-  // host buffer; the dense path also keeps them in packed bf16 hi/lo form
+  // host weights (and bias) stay on the device for the op's lifetime, keyed
+  // by the host buffer; the dense path also keeps them in packed bf16 hi/lo
+  // form.  Device-resident weights may be runtime values at an address that
+  // is reused with new contents, so they are read (and packed) every call.
   const bool dense = d.group == 1;
   const void* wdev = nullptr;
   if (w.device == ie::Device::CUDA && !dense) {
     wdev = w.buffer;
+  } else if (w.device == ie::Device::CUDA) {
+    auto slot = dev_.scratch(kSlotWPacked, ie_cuda_f32_packed_weight_bytes(&d));
+    if (!slot.has_value()) return slot.error();
+    if (auto e = to_status(ie_cuda_f32_pack_weights(&d, static_cast<const float*>(w.buffer), *slot, st));
+        !e.has_value()) {
+      return e;
+    }
+    wdev = *slot;
   } else {
     bool fresh = false;
     const size_t bytes = dense ? ie_cuda_f32_packed_weight_bytes(&d) : w.bytes();
@@ -667,11 +677,13 @@ ie::Status CudaQLinearConv2DOp::forward(const std::vector<ie::Tensor*>& inputs,
     if (auto e = to_status(prc); !e.has_value()) return e;
     xin = *xn;
   }
-  // packed weights, bias and multipliers: uploaded once per host buffer
-  bool fresh = false;
+  // packed weights, bias and multipliers: uploaded once per host buffer;
+  // device-resident weights (possibly runtime values) are packed every call
+  bool fresh = true;
   const size_t wbytes = depthwise ? ie_cuda_dw_q8_packed_weight_bytes(&d)
                                   : ie_cuda_q8_packed_weight_bytes(&kd);
-  auto wp = dev_.cached(w.buffer, wbytes, kCacheWPacked, &fresh);
+  auto wp = w.device == ie::Device::CUDA ? dev_.scratch(kSlotWPacked, wbytes)
+                                         : dev_.cached(w.buffer, wbytes, kCacheWPacked, &fresh);
   if (!wp.has_value()) return wp.error();
   if (fresh) {
     const void* wsrc = w.buffer;

@@ -66,10 +66,11 @@ using DeviceAllocFn = int (*)(void** ptr, size_t bytes);
 void set_device_alloc(DeviceAllocFn fn);
 
 // Device memory owned by one op: weights uploaded (and packed) once per host
-// buffer, scratch buffers that only grow.  Weight inputs are keyed by their
-// host buffer and size: they must be constants that outlive the op and keep
-// their contents (graph weights are; a runtime value reusing one address with
-// new contents would be served the old packed copy).
+// buffer, scratch buffers that only grow.  Host weight inputs are keyed by
+// their buffer and size: they must be constants that outlive the op and keep
+// their contents (graph weights are).  The convolutions read device-resident
+// weights afresh on every call (packing them into scratch), since a device
+// value's address is reused with new contents by the executor's pool.
 class DeviceBuffers {
  public:
   DeviceBuffers() = default;

@@ -816,6 +816,64 @@ int run_gpu(const std::string& dir) {
   ie::OpRegistry reg;
   if (!ie_b200::register_cuda_ops(reg).has_value()) return 2;
 
+  // Device-resident weights are read on every call: the same device buffer
+  // rewritten with new weights gives the result of the new weights (int8 and
+  // fp32 convolutions), never a packed copy of the old ones.
+  {
+    Lcg rng(71);
+    HostTensor xq({2, 16, 9, 9}, ie::DType::U8), xf({2, 16, 9, 9}, ie::DType::F32);
+    HostTensor wq1({8, 16, 3, 3}, ie::DType::I8), wq2({8, 16, 3, 3}, ie::DType::I8);
+    HostTensor wf1({8, 16, 3, 3}, ie::DType::F32), wf2({8, 16, 3, 3}, ie::DType::F32);
+    for (int64_t i = 0; i < xq.t.numel(); ++i) {
+      xq.data<uint8_t>()[i] = static_cast<uint8_t>(rng.next() % 256);
+      xf.data<float>()[i] = rng.uniform(-1.f, 1.f);
+    }
+    for (int64_t i = 0; i < wq1.t.numel(); ++i) {
+      wq1.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+      wq2.data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+      wf1.data<float>()[i] = rng.uniform(-0.2f, 0.2f);
+      wf2.data<float>()[i] = rng.uniform(-0.2f, 0.2f);
+    }
+    const ie::Attrs qattrs{{"multiplier", std::vector<double>(8, 0.004)},
+                           {"bias", std::vector<int64_t>(8, 100)},
+                           {"x_zero_point", int64_t{128}},
+                           {"y_zero_point", int64_t{0}},
+                           {"pads", std::vector<int64_t>{1, 1, 1, 1}}};
+    const ie::Attrs fattrs{{"pads", std::vector<int64_t>{1, 1, 1, 1}}};
+    struct Case {
+      const char* name;
+      HostTensor* x;
+      HostTensor* w1;
+      HostTensor* w2;
+      const ie::Attrs* attrs;
+    } cases[] = {{"DEVW int8", &xq, &wq1, &wq2, &qattrs}, {"DEVW fp32", &xf, &wf1, &wf2, &fattrs}};
+    for (const Case& c : cases) {
+      void* wd = nullptr;
+      if (cudaMalloc(&wd, c.w1->t.bytes()) != cudaSuccess) return 3;
+      ie::Tensor wdev = c.w1->t;
+      wdev.buffer = wd;
+      wdev.device = ie::Device::CUDA;
+      auto op = reg.create(ie::OpType::Conv2D);
+      auto fresh_op = reg.create(ie::OpType::Conv2D);
+      if (!op.has_value() || !fresh_op.has_value()) return 3;
+      expect((*op)->configure(*c.attrs).has_value() && (*fresh_op)->configure(*c.attrs).has_value(),
+             c.name);
+      ie::Tensor y1, y2, y2_ref;
+      std::vector<ie::Tensor*> o1{&y1}, o2{&y2}, o3{&y2_ref};
+      cudaMemcpy(wd, c.w1->t.buffer, c.w1->t.bytes(), cudaMemcpyHostToDevice);
+      const bool ok1 = (*op)->forward({&c.x->t, &wdev}, o1, ctx).has_value();
+      cudaMemcpy(wd, c.w2->t.buffer, c.w2->t.bytes(), cudaMemcpyHostToDevice);
+      const bool ok2 = (*op)->forward({&c.x->t, &wdev}, o2, ctx).has_value();
+      const bool ok3 = (*fresh_op)->forward({&c.x->t, &c.w2->t}, o3, ctx).has_value();
+      expect(ok1 && ok2 && ok3, c.name);
+      if (ok1 && ok2 && ok3) {
+        expect(y2.bytes() == y2_ref.bytes() && std::memcmp(y2.buffer, y2_ref.buffer, y2.bytes()) == 0,
+               c.name);
+        expect(std::memcmp(y1.buffer, y2.buffer, y1.bytes()) != 0, c.name);
+      }
+      cudaFree(wd);
+    }
+  }
   // fp32 Conv2D, the 3x3 / 64-channel single-image case, bias, pads 1
   {
     Lcg rng(1);
