@@ -874,6 +874,79 @@ int run_gpu(const std::string& dir) {
       cudaFree(wd);
     }
   }
+  // Executor liveness: a value that is a graph output and also read by a
+  // later node stays alive to the end of the run (int8 x -> conv1 -> c1
+  // (output) -> conv2 -> y (output)); c1 equals conv1 run on its own, and a
+  // second run of the same executor gives the same bytes.
+  {
+    Lcg rng(83);
+    ie::Graph g;
+    std::vector<std::unique_ptr<HostTensor>> keep;
+    ie::ValueId next = 0;
+    auto value = [&](const std::string& name, bool in = false, bool out = false) {
+      ie::Value v;
+      v.id = next++;
+      v.name = name;
+      v.is_input = in;
+      v.is_output = out;
+      g.values.push_back(v);
+      return v.id;
+    };
+    auto weight = [&](const std::string& name, std::vector<int64_t> dims) {
+      keep.push_back(std::make_unique<HostTensor>(dims, ie::DType::I8));
+      for (int64_t i = 0; i < keep.back()->t.numel(); ++i) {
+        keep.back()->data<int8_t>()[i] = static_cast<int8_t>(static_cast<int32_t>(rng.next() % 255) - 127);
+      }
+      g.weights.emplace(name, keep.back()->t);
+      return value(name);
+    };
+    const ie::Attrs qa{{"multiplier", std::vector<double>(16, 0.003)},
+                       {"bias", std::vector<int64_t>(16, -50)},
+                       {"x_zero_point", int64_t{0}},
+                       {"y_zero_point", int64_t{0}},
+                       {"pads", std::vector<int64_t>{1, 1, 1, 1}}};
+    const ie::ValueId x = value("x", true);
+    const ie::ValueId w1 = weight("lw1", {16, 16, 3, 3}), w2 = weight("lw2", {16, 16, 3, 3});
+    const ie::ValueId c1 = value("c1", false, true), y = value("y", false, true);
+    auto add_node = [&](ie::ValueId in, ie::ValueId w, ie::ValueId out) {
+      ie::Node n;
+      n.id = static_cast<ie::NodeId>(g.nodes.size());
+      n.op = ie::OpType::Conv2D;
+      n.inputs = {in, w};
+      n.outputs = {out};
+      n.attrs = qa;
+      g.nodes.push_back(n);
+    };
+    add_node(x, w1, c1);
+    add_node(c1, w2, y);
+    HostTensor xin({2, 16, 12, 10}, ie::DType::U8);
+    for (int64_t i = 0; i < xin.t.numel(); ++i) xin.data<uint8_t>()[i] = static_cast<uint8_t>(rng.next() % 256);
+    ie_b200::CudaExecutor exec(reg);
+    std::unordered_map<std::string, ie::Tensor> in{{"x", xin.t}};
+    auto r1 = exec.run(g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    auto r2 = exec.run(g, in, std::make_shared<ie::MallocAllocator>(), stream);
+    expect(r1.has_value() && r2.has_value() && r1->size() == 2 && r2->size() == 2, "LIVE: runs");
+    auto op = reg.create(ie::OpType::Conv2D);
+    if (!op.has_value()) return 3;
+    expect((*op)->configure(qa).has_value(), "LIVE: configure");
+    ie::Tensor c1_ref;
+    std::vector<ie::Tensor*> o{&c1_ref};
+    const bool ok = (*op)->forward({&xin.t, &keep[0]->t}, o, ctx).has_value();
+    if (r1.has_value() && r2.has_value() && r1->size() == 2 && r2->size() == 2 && ok) {
+      const ie::Tensor& c1_out = (*r1)[0];
+      expect(c1_out.shape.dims == c1_ref.shape.dims && c1_out.bytes() == c1_ref.bytes() &&
+                 std::memcmp(c1_out.buffer, c1_ref.buffer, c1_ref.bytes()) == 0,
+             "LIVE: output read by a later node equals conv1 alone");
+      bool same = true;
+      for (size_t k = 0; k < 2; ++k) {
+        same = same && (*r1)[k].bytes() == (*r2)[k].bytes() &&
+               std::memcmp((*r1)[k].buffer, (*r2)[k].buffer, (*r1)[k].bytes()) == 0;
+      }
+      expect(same, "LIVE: second run identical");
+    } else {
+      expect(false, "LIVE: results");
+    }
+  }
   // fp32 Conv2D, the 3x3 / 64-channel single-image case, bias, pads 1
   {
     Lcg rng(1);
