@@ -478,9 +478,14 @@ def engine_resnet50_q8(batch: int = 256, iters: int = 20, warmup: int = 3) -> di
     the host clock around the synchronous calls in the backend's test driver
     (a separate process on the same GPU); its check that one image alone gives
     the batch's first row of logits is part of the line."""
-    from computeengine_b200.build import BACKEND_TEST
-    out = subprocess.run([str(BACKEND_TEST), "engine-bench", str(batch), str(iters), str(warmup)],
-                         capture_output=True, text=True, timeout=600)
+    from computeengine_b200.build import BACKEND_TEST, build
+    try:
+        if not BACKEND_TEST.exists():
+            build()
+        out = subprocess.run([str(BACKEND_TEST), "engine-bench", str(batch), str(iters), str(warmup)],
+                             capture_output=True, text=True, timeout=600)
+    except (OSError, RuntimeError, subprocess.SubprocessError) as e:
+        return {"error": f"engine-bench did not run: {e}"}
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     r = json.loads(lines[-1]) if lines else {"error": (out.stderr or out.stdout)[-300:]}
     r["returncode"] = out.returncode
